@@ -1,0 +1,467 @@
+#!/usr/bin/env python3
+"""Forward tokens/s of the B200 transformer path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C2] [--impl b200|reference]
+
+A step is one forward of the whole stack (L blocks + final LayerNorm + masking)
+over one batch of the chosen BASELINE.json configuration (default C2 =
+L4 D512 H8 F2048, batch 8 x seq 1024, causal, fp16).  With N > 1 the
+script runs under torchrun, one process per GPU; every rank processes its own
+batch of the configuration (weak scaling, no collective on the data path) and the
+reported time is the max over ranks.
+
+--impl b200 (default): the CUDA path through make_optimized_transformer.
+  value      tokens/s, inputs resident in HBM, L2 flushed between steps
+  e2e        the same through the public module call with pinned host buffers:
+             H2D of x and the mask + forward + D2H of the output every step
+  roofline   the dominant kernel class, timed with CUDA events inside real forwards
+  cpu_baseline  the fp32 oracle (op-for-op restatement of the reference module's
+             PyTorch eager forward) on the host cores, bounded sample (rank 0, N=1)
+--impl reference: the reference's CPU path (the fp32 oracle port, all host threads)
+  on a bounded sample of the same workload; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+if str(REPO) not in sys.path:
+    sys.path.insert(0, str(REPO))
+
+# (B, S, D, H, F, L, causal, dtype name, prefix-length range or None)
+CONFIGS = {
+    "C1": (2, 128, 256, 4, 1024, 2, False, "float32", (64, 128)),
+    "C2": (8, 1024, 512, 8, 2048, 4, True, "float16", None),
+    "C3": (32, 512, 256, 8, 1024, 6, False, "float16", (32, 512)),
+    "C4": (4, 8192, 768, 12, 3072, 12, True, "float16", (4096, 8192)),
+    "C5": (256, 256, 1024, 16, 4096, 24, True, "float16", (128, 256)),
+}
+# Bounded CPU sample per config: (sequences, layers) of the workload per step.
+CPU_SAMPLE = {"C1": (2, 2), "C2": (1, 4), "C3": (4, 6), "C4": (1, 1), "C5": (1, 24)}
+METRIC = "forward tokens/sec"
+UNIT = "tokens/s"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description="B200 transformer forward benchmark")
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
+    return ap.parse_args(argv)
+
+
+def workload_desc(name: str) -> str:
+    B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    mask = "mask=None" if lens is None else f"prefix mask len~U[{lens[0]},{lens[1]}]"
+    return (f"{name}: L{L} D{D} H{H} hd{D // H} F{F} B{B} S{S} "
+            f"{'causal' if causal else 'non-causal'}, {mask}, {dt}")
+
+
+def make_case(name: str, seed: int, rank: int, device):
+    import torch
+
+    import optimized_transformer  # noqa: F401
+    import tttj_2026_b200 as tb
+
+    B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    dtype = getattr(torch, dt)
+    cfg = tb.TransformerConfig(B, S, D, H, F, L, causal)
+    model = tb.make_parameter_model(cfg, seed, dtype, device)
+    # Each rank gets its own batch (different input seed), same weights.
+    x, mask = tb.generate_inputs(cfg, seed + 1 + 1000 * rank, dtype, lens, device)
+    return cfg, model, x, mask
+
+
+def useful_work(cfg, mask, out_bytes: int = 2):
+    """Valid tokens, attention pairs and per-class FLOPs / bytes of one forward."""
+    import torch
+
+    B, S = cfg.batch_size, cfg.seq_len
+    if mask is None:
+        lengths = [S] * B
+    else:
+        lengths = mask.sum(1).tolist()
+    Tv = sum(lengths)
+    if cfg.causal:
+        pairs = sum(l * (l + 1) // 2 for l in lengths)
+    else:
+        pairs = sum(l * l for l in lengths)
+    D, F, H = cfg.d_model, cfg.ffn_dim, cfg.num_heads
+    hd = D // H
+    per_launch = {
+        "gemm_qkv": ("tensor", 2.0 * Tv * 3 * D * D),
+        "gemm_out_proj": ("tensor", 2.0 * Tv * D * D),
+        "gemm_ffn_in_gelu": ("tensor", 2.0 * Tv * F * D),
+        "gemm_ffn_out": ("tensor", 2.0 * Tv * D * F),
+        "attention": ("tensor", 4.0 * hd * H * pairs),
+        # bytes: fp16 row read + fp16 row write
+        "layernorm": ("hbm", 4.0 * Tv * D),
+        "final_layernorm_scatter": ("hbm", 2.0 * Tv * D + B * S * D * out_bytes),
+        "plan_tokens": ("hbm", float(B * S)),
+    }
+    flops = (2.0 * Tv * (4 * D * D + 2 * D * F) + 4.0 * hd * H * pairs) * cfg.num_layers
+    return Tv, pairs, per_launch, flops
+
+
+def load_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while GPU work runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        import torch
+
+        self.proc = None
+        self.path = None
+        try:
+            props = torch.cuda.get_device_properties(device_index)
+            self.bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        except Exception:
+            self.bus = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
+            if self.bus:
+                cmd += ["-i", self.bus]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        busy = [sm for sm, _, _ in rows]
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(m for _, m, _ in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def cpu_oracle_rate(name: str, seed: int, seconds: float, threads: int):
+    """Time the fp32 oracle (the reference module's math in PyTorch eager fp32) on
+    the host cores over a bounded sample of the workload.  Returns tokens/s scaled
+    to the full stack, plus a description."""
+    import torch
+
+    import optimized_transformer  # noqa: F401
+    import tttj_2026_b200 as tb
+    from oracle import forward_fp32, state_dict_fp32
+
+    torch.set_num_threads(threads)
+    B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    n_seq, n_layers = CPU_SAMPLE[name]
+    full = tb.TransformerConfig(B, S, D, H, F, L, causal)
+    torch.manual_seed(seed)
+    params = tb.TransformerParameters(full).to(getattr(torch, dt))
+    p = state_dict_fp32(params, "cpu")
+    cfg = tb.TransformerConfig(n_seq, S, D, H, F, n_layers, causal)
+    x, mask = tb.generate_inputs(full, seed + 1, getattr(torch, dt), lens, "cpu")
+    x = x[:n_seq].float()
+    mask = None if mask is None else mask[:n_seq]
+    with torch.inference_mode():
+        forward_fp32(p, cfg, x, mask)  # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            forward_fp32(p, cfg, x, mask)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= seconds or reps >= 1000:
+                break
+    per_step_full = el / reps * (L / n_layers)  # seconds for n_seq sequences, all layers
+    value = n_seq * S / per_step_full
+    sample = (f"{n_seq} of {B} sequences x {n_layers} of {L} layers per rep, {reps} reps in {el:.1f} s; "
+              f"time scaled x{L / n_layers:g} to the full stack")
+    return value, sample, el / reps
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return 0
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    name = args.config
+    B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    n_seq, n_layers = CPU_SAMPLE[name]
+
+    import optimized_transformer  # noqa: F401
+    import tttj_2026_b200 as tb
+    from oracle import forward_fp32, state_dict_fp32
+
+    full = tb.TransformerConfig(B, S, D, H, F, L, causal)
+    torch.manual_seed(args.seed)
+    params = tb.TransformerParameters(full).to(getattr(torch, dt))
+    p = state_dict_fp32(params, "cpu")
+    cfg = tb.TransformerConfig(n_seq, S, D, H, F, n_layers, causal)
+    x, mask = tb.generate_inputs(full, args.seed + 1, getattr(torch, dt), lens, "cpu")
+    x = x[:n_seq].float()
+    mask = None if mask is None else mask[:n_seq]
+    times = []
+    with torch.inference_mode():
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            forward_fp32(p, cfg, x, mask)
+            if i >= args.warmup:
+                times.append(time.perf_counter() - t0)
+    scale = L / n_layers
+    step_s = statistics.fmean(times) * scale
+    value = n_seq * S / step_s
+    sample = f"{n_seq} of {B} sequences x {n_layers} of {L} layers per step, time scaled x{scale:g}"
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": workload_desc(name), "global_batch": B, "seq_len": S,
+                   "parallelism": "cpu"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_b200(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    import optimized_transformer  # noqa: F401
+    import tttj_2026_b200 as tb
+
+    name = args.config
+    B, S = CONFIGS[name][0], CONFIGS[name][1]
+    cfg, model, x, mask = make_case(name, args.seed, rank, dev)
+    opt = tb.make_optimized_transformer(model)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local_rank).start()
+    with torch.inference_mode():
+        # ---- device-resident timed loop ----
+        for _ in range(args.warmup):
+            opt(x, mask)
+            flush.zero_()
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            opt(x, mask)
+            ends[i].record(stream)
+            flush.zero_()  # L2 flush between timed steps (outside the events)
+        torch.cuda.synchronize(dev)
+        barrier()
+        step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+        total_ms = max_over_ranks(sum(step_ms))
+
+        # ---- end to end through the public call with host buffers ----
+        x_host = x.cpu().pin_memory()
+        m_host = None if mask is None else mask.cpu().pin_memory()
+        out_host = torch.empty(x.shape, dtype=x.dtype).pin_memory()
+        h2d = x_host.numel() * x_host.element_size() + (0 if m_host is None else m_host.numel())
+        d2h = out_host.numel() * out_host.element_size()
+        x_dev = torch.empty_like(x)
+        m_dev = None if mask is None else torch.empty_like(mask)
+
+        def e2e_step():
+            x_dev.copy_(x_host, non_blocking=True)
+            if m_dev is not None:
+                m_dev.copy_(m_host, non_blocking=True)
+            out = opt(x_dev, m_dev)
+            out_host.copy_(out, non_blocking=True)
+
+        for _ in range(args.warmup):
+            e2e_step()
+        e_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        e_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize(dev)
+        for i in range(args.steps):
+            e_starts[i].record(stream)
+            e2e_step()
+            e_ends[i].record(stream)
+            flush.zero_()
+        torch.cuda.synchronize(dev)
+        barrier()
+        e2e_total_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(e_starts, e_ends)))
+        ok_e2e = torch.equal(out_host, opt(x, mask).cpu())
+
+        # ---- per-kernel-class timing inside real forwards ----
+        opt.set_kernel_timing(B, S, True)
+        for _ in range(args.steps):
+            opt(x, mask)
+            flush.zero_()
+        ktimes = opt.kernel_times(B, S)
+        opt.set_kernel_timing(B, S, False)
+        launches = opt.launches_per_forward(B, S)
+        opt.device_status()
+    clk = clocks.stop()
+
+    if rank != 0:
+        return 0
+
+    tokens = B * S
+    value = world * tokens * args.steps / (total_ms / 1e3)
+    e2e_value = world * tokens * args.steps / (e2e_total_ms / 1e3)
+    Tv, pairs, per_launch, flops = useful_work(cfg, mask, x.element_size())
+    peaks = load_peaks()
+    kernels = {}
+    for cls, (ms, n) in ktimes.items():
+        if n == 0:
+            continue
+        bound, work = per_launch[cls]
+        avg_ms = ms / n
+        if bound == "tensor":
+            achieved = work / (avg_ms * 1e-3) / 1e12
+            peak, unit = peaks["tflops"], "TFLOP/s"
+        else:
+            achieved = work / (avg_ms * 1e-3) / 1e9
+            peak, unit = peaks["hbm_gbs"], "GB/s"
+        kernels[cls] = {"launches": n, "total_ms": round(ms, 4), "avg_us": round(avg_ms * 1e3, 2),
+                        "share": None, "bound": "hbm" if bound == "hbm" else "tensor",
+                        "achieved": round(achieved, 2), "unit": unit, "frac": round(achieved / peak, 4)}
+    ksum = sum(v["total_ms"] for v in kernels.values())
+    for v in kernels.values():
+        v["share"] = round(v["total_ms"] / ksum, 4) if ksum else None
+    dom = max(kernels, key=lambda k: kernels[k]["total_ms"])
+    dk = kernels[dom]
+    traffic = _profile_traffic(dom, name)
+    roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"],
+                "peak": peaks["tflops"] if dk["bound"] == "tensor" else peaks["hbm_gbs"],
+                "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic,
+                "peak_source": f"{peaks['source']} ({'bf16_tflops burst' if dk['bound'] == 'tensor' else 'hbm_gbs'})"}
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cval, sample, _ = cpu_oracle_rate(name, args.seed, args.cpu_seconds, threads)
+        cpu = {"value": cval, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+
+    ms_per_step = total_ms / args.steps
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": workload_desc(name), "global_batch": world * B, "seq_len": S,
+                   "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
+                   "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",
+                   "inputs": f"x~N(0,1), input seed {args.seed + 1} (+1000*rank)"},
+        "p50_ms": statistics.median(step_ms),
+        "valid_tokens_per_s": world * Tv * args.steps / (total_ms / 1e3),
+        "useful_tflops": flops / (ms_per_step * 1e-3) / 1e12,
+        "useful_frac_of_peak": flops / (ms_per_step * 1e-3) / 1e12 / peaks["tflops"],
+        "roofline": roofline,
+        "kernels": kernels,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_total_ms / args.steps, "output_matches_device_path": ok_e2e},
+        "clocks": clk,
+        "gpu_launches": launches * args.steps,
+        "launches_per_step": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _profile_traffic(kernel_class: str, config: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (a line `traffic_bytes_per_launch <class> <config> <bytes>`), else None."""
+    for f in sorted((REPO / "profiles").glob("*.md")):
+        for line in f.read_text().splitlines():
+            parts = line.strip().strip("`").split()
+            if len(parts) == 4 and parts[0] == "traffic_bytes_per_launch" and parts[1] == kernel_class \
+                    and parts[2] == config:
+                try:
+                    return float(parts[3])
+                except ValueError:
+                    return None
+    return None
+
+
+def main(argv=None) -> int:
+    args = parse_args(argv)
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        return run_b200(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

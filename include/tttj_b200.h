@@ -1,0 +1,194 @@
+/*
+ * tttj_b200.h -- C ABI of the B200 (sm_100a) forward path for the pre-LayerNorm
+ * transformer stack of Scallion3008/tttj-2026:
+ *
+ *     for each block: x = x + out_proj(attn(LN1 x)); x = x + ffn_out(gelu(ffn_in(LN2 x)));
+ *                     x = x.masked_fill(~valid_token_mask, 0)
+ *     out = LN_final(x).masked_fill(~valid_token_mask, 0)
+ *
+ * (benchmarks/torch_transformer_benchmark.py:59-172 in the reference).
+ *
+ * The reference exposes this path to Python through a pybind11 module whose entry
+ * point is forward(input, valid_mask, packed_weights, capture_debug)
+ * (kernels/csrc/sequence_resident.cpp:23-32, host side
+ * kernels/csrc/sequence_resident.cu:468-533), JIT-built and loaded by
+ * kernels/sequence_resident.py:51-65.  This header is the C replacement for that
+ * binding: plain pointers, sizes and a CUDA stream handle, no torch types.  All
+ * device pointers are CUDA device addresses on the plan's device; `stream` is a
+ * cudaStream_t (NULL = legacy default stream).
+ *
+ * Every function returns TTTJ_OK (0) or an error code; tttj_last_error() returns a
+ * message for the calling thread's last failure.  Shape errors are reported the way
+ * the reference's TORCH_CHECKs report them (kernels/csrc/sequence_resident.cu:473-496):
+ * nothing is launched.
+ */
+#ifndef TTTJ_B200_H
+#define TTTJ_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TTTJ_OK 0
+#define TTTJ_ERR_INVALID 1        /* unsupported shape / bad argument (Python: ValueError) */
+#define TTTJ_ERR_CUDA 2           /* CUDA runtime or driver error (Python: RuntimeError) */
+#define TTTJ_ERR_DEVICE_TIMEOUT 3 /* a device-side wait hit its limit (Python: RuntimeError) */
+
+#define TTTJ_DTYPE_F16 0
+#define TTTJ_DTYPE_F32 1
+
+/* Mirrors TransformerConfig (benchmarks/torch_transformer_benchmark.py:29-56). */
+typedef struct tttj_config {
+  int32_t batch_size;
+  int32_t seq_len;
+  int32_t d_model;
+  int32_t num_heads;
+  int32_t ffn_dim;
+  int32_t num_layers;
+  int32_t causal;
+} tttj_config;
+
+/* Fields of the packed weight buffer.  Matrices are fp16 in nn.Linear's [out, in]
+ * layout; vectors are fp32.  Replaces pack_model_weights
+ * (kernels/sequence_resident.py:74-109), which packs the same parameters into one
+ * flat fp16 buffer in the order LN1, q, k, v, out, LN2, ffn_in, ffn_out, final LN. */
+#define TTTJ_W_QKV 0     /* fp16 [3D, D]: rows q_proj | k_proj | v_proj */
+#define TTTJ_W_OUT 1     /* fp16 [D, D]  out_proj.weight */
+#define TTTJ_W_FFN_IN 2  /* fp16 [F, D]  ffn_in.weight */
+#define TTTJ_W_FFN_OUT 3 /* fp16 [D, F]  ffn_out.weight */
+#define TTTJ_B_QKV 4     /* fp32 [3D]    q|k|v biases */
+#define TTTJ_B_OUT 5     /* fp32 [D] */
+#define TTTJ_B_FFN_IN 6  /* fp32 [F] */
+#define TTTJ_B_FFN_OUT 7 /* fp32 [D] */
+#define TTTJ_LN1_W 8     /* fp32 [D]  norm1.weight */
+#define TTTJ_LN1_B 9     /* fp32 [D]  norm1.bias */
+#define TTTJ_LN2_W 10    /* fp32 [D]  norm2.weight */
+#define TTTJ_LN2_B 11    /* fp32 [D]  norm2.bias */
+#define TTTJ_LNF_W 12    /* fp32 [D]  final_norm.weight (layer index = num_layers) */
+#define TTTJ_LNF_B 13    /* fp32 [D]  final_norm.bias   (layer index = num_layers) */
+
+/* Last error message of the calling thread ("" if none). */
+const char* tttj_last_error(void);
+
+/* Library version string. */
+const char* tttj_version(void);
+
+/* Check a configuration against what the kernels support (head_dim 32 or 64,
+ * d_model and ffn_dim multiples of 64, ...).  Mirrors case_number_for_model's
+ * ValueError contract (optimized_transformer.py:45-66): TTTJ_ERR_INVALID + message. */
+int tttj_validate_config(const tttj_config* cfg);
+
+/* Size of the packed weight buffer, and the byte offset/size of one field.
+ * layer in [0, num_layers) for per-block fields, layer == num_layers for LNF. */
+size_t tttj_weights_bytes(const tttj_config* cfg);
+int tttj_weight_offset(const tttj_config* cfg, int layer, int field, size_t* offset,
+                       size_t* bytes);
+
+/* Device workspace the forward needs (activations of the packed valid tokens,
+ * token plan, device status word).  It must be zero-filled once before the first
+ * forward (the plan never reads a byte the same call did not write, except rows of
+ * earlier calls, which stay finite). */
+size_t tttj_workspace_bytes(const tttj_config* cfg);
+
+/* A plan binds a configuration to one device, one packed weight buffer and one
+ * workspace (all owned by the caller), and pre-builds every TMA descriptor.
+ * Replaces SequenceResidentTransformer.prepare (kernels/sequence_resident.py:143-150). */
+typedef struct tttj_plan tttj_plan;
+int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
+                     size_t workspace_bytes, tttj_plan** out_plan);
+int tttj_plan_destroy(tttj_plan* plan);
+
+/* One forward pass, enqueued on `stream` (no host synchronisation).
+ *   x          [B, S, D] in x_dtype (TTTJ_DTYPE_F16 or TTTJ_DTYPE_F32)
+ *   valid_mask [B, S] bytes (0 = padded token), or NULL = every token valid
+ *   out        [B, S, D] in x_dtype; padded rows are written as exact zeros.
+ * Replaces the pybind forward(input, valid_mask, packed_weights, capture_debug)
+ * (kernels/csrc/sequence_resident.cpp:23-32) and the Python forward
+ * SequenceResidentTransformer.forward (kernels/sequence_resident.py:227-233). */
+int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
+                 void* out, void* stream);
+
+/* Synchronise the plan's device and read (then clear) the device status word that
+ * bounded device waits write on timeout.  *device_status = 0 when healthy. */
+int tttj_plan_status(tttj_plan* plan, int* device_status);
+
+/* ---- instrumentation ---- */
+
+/* Number of kernel launches one tttj_forward of this plan enqueues. */
+int tttj_plan_launch_count(tttj_plan* plan);
+
+/* Kernel classes of the forward, for per-class timing. */
+#define TTTJ_KCLASS_PLAN 0
+#define TTTJ_KCLASS_LAYERNORM 1
+#define TTTJ_KCLASS_GEMM_QKV 2
+#define TTTJ_KCLASS_ATTENTION 3
+#define TTTJ_KCLASS_GEMM_OUT 4
+#define TTTJ_KCLASS_GEMM_FFN_IN 5
+#define TTTJ_KCLASS_GEMM_FFN_OUT 6
+#define TTTJ_KCLASS_FINAL_LN 7
+#define TTTJ_KCLASS_COUNT 8
+
+/* With timing enabled, every later tttj_forward records a CUDA event pair around
+ * each launch on the forward's stream; tttj_plan_kernel_times returns, per class,
+ * the summed device milliseconds and launch count since timing was enabled (it
+ * waits for the last timed forward).  Enabling resets the totals.  Replaces the
+ * reference's per-step timing scripts (benchmarks/benchmark_step_6.py:40-54). */
+int tttj_plan_enable_timing(tttj_plan* plan, int enable);
+int tttj_plan_kernel_times(tttj_plan* plan, double* total_ms /* [TTTJ_KCLASS_COUNT] */,
+                           long* launches /* [TTTJ_KCLASS_COUNT] */);
+const char* tttj_kernel_class_name(int cls);
+
+/* ---- per-kernel entry points (same kernels the forward launches) ---- */
+
+/* Linear layer with fused epilogue: out = epi(a @ w^T + bias).
+ * Replaces F.linear / nn.Linear on the hot path (torch_transformer_benchmark.py:93-95,
+ * 118, 141) and the reference's Triton epilogue kernels linear_gelu /
+ * linear_residual_layer_norm (kernels/case13_linear.py:262-376).
+ *   a [rows, k] fp16 (row stride lda), w [n, k] fp16 (row stride ldw), bias [n] fp32,
+ *   out [rows, n] fp16 (ldo); residual [rows, n] fp16 (ldr) for TTTJ_EPI_BIAS_RESIDUAL
+ *   (out may equal residual).  rows_dev (nullable) holds a device row count <= rows.
+ *   n % 32 == 0, k % 64 == 0, strides multiples of 8 elements. */
+#define TTTJ_EPI_BIAS 0
+#define TTTJ_EPI_BIAS_GELU 1
+#define TTTJ_EPI_BIAS_RESIDUAL 2
+int tttj_linear(const void* a, int lda, const void* w, int ldw, const float* bias, void* out,
+                int ldo, const void* residual, int ldr, int rows, const int* rows_dev, int n, int k,
+                int epilogue, int* status_dev, void* stream);
+
+/* nn.LayerNorm over rows of an fp16 [rows, d] matrix (d % 8 == 0, d <= 2048),
+ * fp32 statistics, biased variance.  Replaces standalone_layer_norm /
+ * residual_layer_norm (kernels/case13_fusions.py:137-215, kernels/case8_fusions.py:223). */
+int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamma,
+                   const float* beta, float eps, void* stream);
+
+/* Fused multi-head attention over the packed valid-token layout.
+ *   qkv  [Tv, 3*d_model] fp16: valid tokens of sequence 0, then 1, ... in token
+ *        order; columns q | k | v with head h at h*head_dim.
+ *   ctx  [Tv, d_model] fp16 output (rows of valid tokens only).
+ *   valid_mask [batch, seq_len] bytes or NULL (all valid) -- defines the packing.
+ * Replaces packed_causal_attention / two_pass_causal_attention
+ * (kernels/case8_attention.py:168, kernels/case14_attention.py:181) and the
+ * score/softmax/PV sequence of BaselineSelfAttention.forward
+ * (torch_transformer_benchmark.py:97-117).  `workspace` (device, at least
+ * tttj_attention_workspace_bytes) holds the token plan and work list. */
+size_t tttj_attention_workspace_bytes(int batch, int seq_len, int num_heads);
+int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch, int seq_len,
+                   int d_model, int num_heads, int causal, void* workspace,
+                   size_t workspace_bytes, void* stream);
+
+/* Failure-detection self test: launches a kernel whose bounded wait on an mbarrier
+ * that is never signalled gives up after limit_ns and writes 0x1ff into *status_dev.
+ * No counterpart in the reference (its device waits are unbounded). */
+int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream);
+
+/* Number of SMs of `device` (grid sizing of the persistent kernels). */
+int tttj_device_sm_count(int device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TTTJ_B200_H */

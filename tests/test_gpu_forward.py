@@ -1,0 +1,109 @@
+"""GPU: the whole forward through make_optimized_transformer -> tttj_forward, against
+the golden reference outputs and the fp32 oracle at the BASELINE.json configs."""
+import pytest
+import torch
+
+import tttj_2026_b200 as tb
+from helpers import CONFIGS, gate, golden_index, load_golden
+from oracle import forward_fp32, forward_fp32_per_sequence, state_dict_fp32
+from test_oracle_golden import _model as golden_model
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _no_tf32():
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    yield
+    torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+@pytest.mark.parametrize("name", sorted(golden_index()))
+def test_golden_cases_fp32_model(name):
+    """fp32 parameter model (weights cast to fp16 inside), fp32 input and output."""
+    entry = golden_index()[name]
+    cfg, model = golden_model(entry)
+    x, mask, ref_out = load_golden(name)
+    opt = tb.make_optimized_transformer(model.to(DEV))
+    with torch.inference_mode():
+        out = opt(x.to(DEV), None if mask is None else mask.to(DEV))
+    torch.cuda.synchronize()
+    assert out.dtype == torch.float32 and out.shape == x.shape
+    r = gate(ref_out, out, mask)
+    assert r.passed, r
+
+
+def _case(name, seed=0):
+    B, S, D, H, F, L, causal, dtype, lengths = CONFIGS[name]
+    cfg = tb.TransformerConfig(B, S, D, H, F, L, causal)
+    model = tb.make_parameter_model(cfg, seed, dtype, DEV)
+    x, mask = tb.generate_inputs(cfg, seed + 1, dtype, lengths, DEV)
+    return cfg, model, x, mask
+
+
+@pytest.mark.parametrize("name", ["C1", "C2", "C3", "C5"])
+def test_baseline_config_vs_oracle(name):
+    cfg, model, x, mask = _case(name)
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        out = opt(x, mask)
+        ref = forward_fp32(state_dict_fp32(model, DEV), cfg, x.float(), mask)
+    torch.cuda.synchronize()
+    assert out.dtype == x.dtype
+    r = gate(ref, out, mask)
+    print(name, r)
+    assert r.passed, r
+
+
+def test_c4_long_sequence_vs_oracle():
+    cfg, model, x, mask = _case("C4")
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        out = opt(x, mask)
+        ref = forward_fp32_per_sequence(state_dict_fp32(model, DEV), cfg, x.float(), mask)
+    torch.cuda.synchronize()
+    r = gate(ref, out, mask)
+    print("C4", r)
+    assert r.passed, r
+
+
+def test_repeat_is_bit_identical_and_mask_none_equals_all_valid():
+    cfg, model, x, _ = _case("C2")
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        a = opt(x, None)
+        b = opt(x, None)
+        c = opt(x, torch.ones(x.shape[:2], dtype=torch.bool, device=DEV))
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert torch.equal(a, c)
+
+
+def test_sequences_are_independent():
+    """Changing one sequence's tokens leaves every other sequence's output unchanged
+    (padding and packing never leak across sequences)."""
+    cfg, model, x, mask = _case("C3")
+    opt = tb.make_optimized_transformer(model)
+    x2 = x.clone()
+    x2[5] = torch.randn_like(x2[5].float()).half() * 10
+    with torch.inference_mode():
+        a = opt(x, mask)
+        b = opt(x2, mask)
+    torch.cuda.synchronize()
+    keep = torch.ones(cfg.batch_size, dtype=torch.bool)
+    keep[5] = False
+    assert torch.equal(a[keep.to(DEV)], b[keep.to(DEV)])
+    assert not torch.equal(a[5], b[5])
+
+
+def test_other_batch_shapes_and_no_device_error():
+    cfg, model, x, mask = _case("C3")
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        full = opt(x, mask)
+        part = opt(x[3:9].contiguous(), mask[3:9].contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(full[3:9], part)
+    assert opt.device_status() == 0

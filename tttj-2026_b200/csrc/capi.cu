@@ -1,0 +1,635 @@
+// C ABI of the forward path (include/tttj_b200.h): configuration checks, packed
+// weight and workspace layouts, TMA descriptor construction, the plan object and the
+// per-layer launch sequence.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/tttj_b200.h"
+#include "launch.h"
+
+using namespace tttj;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(TTTJ_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+#define TTTJ_CUDA(call)                                   \
+  do {                                                    \
+    cudaError_t e_ = (call);                              \
+    if (e_ != cudaSuccess) return cuda_fail(e_, #call);   \
+  } while (0)
+
+constexpr size_t kAlign = 256;
+inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+constexpr float kLnEps = 1e-5f;  // nn.LayerNorm default (torch_transformer_benchmark.py:128)
+constexpr unsigned long long kWaitLimitNs = TTTJ_WAIT_LIMIT_NS;
+
+// ---------------------------------------------------------------- weights layout
+size_t field_bytes(const tttj_config& c, int field) {
+  const size_t D = c.d_model, F = c.ffn_dim;
+  switch (field) {
+    case TTTJ_W_QKV: return 3 * D * D * 2;
+    case TTTJ_W_OUT: return D * D * 2;
+    case TTTJ_W_FFN_IN: return F * D * 2;
+    case TTTJ_W_FFN_OUT: return D * F * 2;
+    case TTTJ_B_QKV: return 3 * D * 4;
+    case TTTJ_B_OUT: return D * 4;
+    case TTTJ_B_FFN_IN: return F * 4;
+    case TTTJ_B_FFN_OUT: return D * 4;
+    case TTTJ_LN1_W: case TTTJ_LN1_B: case TTTJ_LN2_W: case TTTJ_LN2_B:
+    case TTTJ_LNF_W: case TTTJ_LNF_B: return D * 4;
+    default: return 0;
+  }
+}
+
+size_t layer_stride(const tttj_config& c) {
+  size_t s = 0;
+  for (int f = TTTJ_W_QKV; f <= TTTJ_LN2_B; ++f) s += align_up(field_bytes(c, f));
+  return s;
+}
+
+bool weight_offset(const tttj_config& c, int layer, int field, size_t* off, size_t* bytes) {
+  if (layer < 0 || layer > c.num_layers) return false;
+  if (layer == c.num_layers) {
+    if (field != TTTJ_LNF_W && field != TTTJ_LNF_B) return false;
+    *off = (size_t)c.num_layers * layer_stride(c) +
+           (field == TTTJ_LNF_B ? align_up(field_bytes(c, TTTJ_LNF_W)) : 0);
+    *bytes = field_bytes(c, field);
+    return true;
+  }
+  if (field < TTTJ_W_QKV || field > TTTJ_LN2_B) return false;
+  size_t o = (size_t)layer * layer_stride(c);
+  for (int f = TTTJ_W_QKV; f < field; ++f) o += align_up(field_bytes(c, f));
+  *off = o;
+  *bytes = field_bytes(c, field);
+  return true;
+}
+
+// ---------------------------------------------------------------- workspace layout
+struct WsLayout {
+  size_t seq_len, seq_off, packed_src, dst_map, items, item_count, status;
+  size_t resid, h, qkv, ctx, hid;
+  size_t total;
+};
+
+size_t attn_items_max(size_t B, size_t S, size_t H) {
+  return B * H * ((S + ATT_BM - 1) / ATT_BM);
+}
+
+// Token-plan part of the workspace (shared by the forward and tttj_attention).
+size_t plan_layout(size_t B, size_t S, size_t H, WsLayout* w) {
+  const size_t T = B * S;
+  size_t o = 0;
+  w->seq_len = o; o += align_up(B * 4);
+  w->seq_off = o; o += align_up((B + 1) * 4);
+  w->packed_src = o; o += align_up(T * 4);
+  w->dst_map = o; o += align_up(T * 4);
+  w->items = o; o += align_up(attn_items_max(B, S, H) * 8);
+  w->item_count = o; o += align_up(4);
+  w->status = o; o += align_up(4);
+  return o;
+}
+
+WsLayout ws_layout(const tttj_config& c) {
+  WsLayout w{};
+  const size_t T = (size_t)c.batch_size * c.seq_len, D = c.d_model, F = c.ffn_dim;
+  size_t o = plan_layout(c.batch_size, c.seq_len, c.num_heads, &w);
+  w.resid = o; o += align_up(T * D * 2);
+  w.h = o; o += align_up(T * D * 2);
+  w.qkv = o; o += align_up(T * 3 * D * 2);
+  w.ctx = o; o += align_up(T * D * 2);
+  w.hid = o; o += align_up(T * F * 2);
+  w.total = o;
+  return w;
+}
+
+TokenPlan token_plan_at(uint8_t* base, const WsLayout& w) {
+  TokenPlan tp;
+  tp.seq_len = reinterpret_cast<int*>(base + w.seq_len);
+  tp.seq_off = reinterpret_cast<int*>(base + w.seq_off);
+  tp.packed_src = reinterpret_cast<int*>(base + w.packed_src);
+  tp.dst_map = reinterpret_cast<int*>(base + w.dst_map);
+  tp.items = reinterpret_cast<int2*>(base + w.items);
+  tp.item_count = reinterpret_cast<int*>(base + w.item_count);
+  return tp;
+}
+
+// ---------------------------------------------------------------- TMA descriptors
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D fp16 row-major matrix [rows, cols] with row stride `ld` elements, loaded in
+// boxes of 64 columns (128 B, one swizzle atom) x box_rows rows, 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+              uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+    return fail(TTTJ_ERR_INVALID, "TMA operand must be 16-byte aligned with a 16-byte row stride");
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return TTTJ_OK;
+}
+
+int sm_count(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
+  return n;
+}
+
+int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, const float* bias,
+               void* out, int ldo, const void* residual, int ldr, int rows, const int* rows_dev,
+               int n, int k, int epi, int* status, int num_sms) {
+  if (n <= 0 || k <= 0 || rows < 0) return fail(TTTJ_ERR_INVALID, "linear: bad sizes");
+  if (n % 32 != 0) return fail(TTTJ_ERR_INVALID, "linear: n=%d must be a multiple of 32", n);
+  if (k % 64 != 0) return fail(TTTJ_ERR_INVALID, "linear: k=%d must be a multiple of 64", k);
+  if (lda % 8 || ldw % 8 || ldo % 8 || (epi == EPI_BIAS_RESIDUAL && ldr % 8))
+    return fail(TTTJ_ERR_INVALID, "linear: row strides must be multiples of 8 elements");
+  if (epi < EPI_BIAS || epi > EPI_BIAS_RESIDUAL)
+    return fail(TTTJ_ERR_INVALID, "linear: unknown epilogue %d", epi);
+  if (epi == EPI_BIAS_RESIDUAL && residual == nullptr)
+    return fail(TTTJ_ERR_INVALID, "linear: residual epilogue needs a residual");
+  if ((reinterpret_cast<uintptr_t>(bias) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+      (reinterpret_cast<uintptr_t>(residual) & 15))
+    return fail(TTTJ_ERR_INVALID, "linear: bias/out/residual must be 16-byte aligned");
+  if (num_sms <= 0) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    num_sms = sm_count(dev);
+    if (num_sms <= 0) return fail(TTTJ_ERR_CUDA, "could not query the SM count");
+  }
+  std::memset(g, 0, sizeof(*g));
+  g->bn = gemm_choose_bn(rows, n, num_sms);
+  g->epi = epi;
+  int rc = make_tmap(&g->tmA, a, (uint64_t)(rows > 0 ? rows : 1), (uint64_t)k, (uint64_t)lda, GEMM_BM);
+  if (rc) return rc;
+  rc = make_tmap(&g->tmB, w, (uint64_t)n, (uint64_t)k, (uint64_t)ldw, (uint32_t)g->bn);
+  if (rc) return rc;
+  g->p.rows_dev = rows_dev;
+  g->p.rows_max = rows;
+  g->p.n = n;
+  g->p.k = k;
+  g->p.bias = bias;
+  g->p.out = static_cast<__half*>(out);
+  g->p.ldo = ldo;
+  g->p.residual = static_cast<const __half*>(residual);
+  g->p.ldr = ldr;
+  g->p.status = status;
+  g->p.wait_limit_ns = kWaitLimitNs;
+  const long tiles = (long)((rows + GEMM_BM - 1) / GEMM_BM) * ((n + g->bn - 1) / g->bn);
+  g->grid = (int)(tiles < num_sms ? tiles : num_sms);
+  return TTTJ_OK;
+}
+
+int check_config(const tttj_config* c) {
+  if (!c) return fail(TTTJ_ERR_INVALID, "null config");
+  if (c->batch_size <= 0 || c->seq_len <= 0 || c->d_model <= 0 || c->num_heads <= 0 ||
+      c->ffn_dim <= 0 || c->num_layers <= 0)
+    return fail(TTTJ_ERR_INVALID, "config fields must be positive");
+  if (c->d_model % c->num_heads != 0)
+    return fail(TTTJ_ERR_INVALID, "d_model (%d) must be divisible by num_heads (%d)", c->d_model,
+                c->num_heads);
+  const int hd = c->d_model / c->num_heads;
+  if (hd != 32 && hd != 64)
+    return fail(TTTJ_ERR_INVALID, "no B200 kernel for head_dim=%d (supported: 32, 64)", hd);
+  if (c->d_model % 64 != 0 || c->ffn_dim % 64 != 0)
+    return fail(TTTJ_ERR_INVALID, "d_model (%d) and ffn_dim (%d) must be multiples of 64",
+                c->d_model, c->ffn_dim);
+  if (c->d_model > 2048) return fail(TTTJ_ERR_INVALID, "d_model=%d exceeds 2048", c->d_model);
+  if (c->num_heads > 255) return fail(TTTJ_ERR_INVALID, "num_heads=%d exceeds 255", c->num_heads);
+  const long long T = (long long)c->batch_size * c->seq_len;
+  if (T * (long long)(c->ffn_dim > 3 * c->d_model ? c->ffn_dim : 3 * c->d_model) >= (1ll << 40) ||
+      T >= (1ll << 31) - 256)
+    return fail(TTTJ_ERR_INVALID, "batch_size*seq_len too large");
+  const long long plan_smem = 4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATT_BN - 1) / ATT_BN + 1);
+  if (plan_smem > 200 * 1024) return fail(TTTJ_ERR_INVALID, "batch_size/seq_len too large for the token plan");
+  return TTTJ_OK;
+}
+
+struct LayerGemms {
+  GemmLaunch qkv, out, ffn_in, ffn_out;
+  const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
+};
+
+}  // namespace
+
+struct tttj_plan {
+  tttj_config cfg;
+  int device;
+  int num_sms;
+  const uint8_t* weights;
+  uint8_t* ws;
+  WsLayout lay;
+  TokenPlan tp;
+  int* status;
+  __half *resid, *h, *qkv, *ctx, *hid;
+  std::vector<LayerGemms> layers;
+  const float *lnf_w, *lnf_b;
+  AttnParams attn;
+  int attn_grid;
+  // Optional per-kernel-class timing (tttj_plan_enable_timing).
+  bool timing = false;
+  std::vector<cudaEvent_t> ev_start, ev_stop;  // one pair per launch of one forward
+  std::vector<int> ev_class;
+  size_t ev_used = 0;
+  double class_ms[TTTJ_KCLASS_COUNT] = {};
+  long class_launches[TTTJ_KCLASS_COUNT] = {};
+};
+
+namespace {
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+}  // namespace
+
+int launches_per_forward(const tttj_config& c) { return 7 * c.num_layers + 2; }
+
+// Fold the events of the previous timed forward into the per-class totals.
+int collect_timing(tttj_plan* p) {
+  if (p->ev_used == 0) return TTTJ_OK;
+  TTTJ_CUDA(cudaEventSynchronize(p->ev_stop[p->ev_used - 1]));
+  for (size_t i = 0; i < p->ev_used; ++i) {
+    float ms = 0.f;
+    TTTJ_CUDA(cudaEventElapsedTime(&ms, p->ev_start[i], p->ev_stop[i]));
+    p->class_ms[p->ev_class[i]] += ms;
+    p->class_launches[p->ev_class[i]] += 1;
+  }
+  p->ev_used = 0;
+  return TTTJ_OK;
+}
+
+void destroy_events(tttj_plan* p) {
+  for (auto e : p->ev_start) cudaEventDestroy(e);
+  for (auto e : p->ev_stop) cudaEventDestroy(e);
+  p->ev_start.clear();
+  p->ev_stop.clear();
+  p->ev_class.clear();
+  p->ev_used = 0;
+}
+
+extern "C" {
+
+const char* tttj_last_error(void) { return g_last_error.c_str(); }
+
+const char* tttj_version(void) { return "tttj_b200 0.1 (sm_100a)"; }
+
+int tttj_validate_config(const tttj_config* cfg) { return check_config(cfg); }
+
+size_t tttj_weights_bytes(const tttj_config* cfg) {
+  if (check_config(cfg)) return 0;
+  size_t off, bytes;
+  weight_offset(*cfg, cfg->num_layers, TTTJ_LNF_B, &off, &bytes);
+  return align_up(off + bytes);
+}
+
+int tttj_weight_offset(const tttj_config* cfg, int layer, int field, size_t* offset,
+                       size_t* bytes) {
+  int rc = check_config(cfg);
+  if (rc) return rc;
+  if (!offset || !bytes) return fail(TTTJ_ERR_INVALID, "null output pointer");
+  if (!weight_offset(*cfg, layer, field, offset, bytes))
+    return fail(TTTJ_ERR_INVALID, "no weight field %d at layer %d", field, layer);
+  return TTTJ_OK;
+}
+
+size_t tttj_workspace_bytes(const tttj_config* cfg) {
+  if (check_config(cfg)) return 0;
+  return ws_layout(*cfg).total;
+}
+
+int tttj_device_sm_count(int device) { return sm_count(device); }
+
+int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
+                     size_t workspace_bytes, tttj_plan** out_plan) {
+  int rc = check_config(cfg);
+  if (rc) return rc;
+  if (!weights || !workspace || !out_plan) return fail(TTTJ_ERR_INVALID, "null pointer argument");
+  const WsLayout lay = ws_layout(*cfg);
+  if (workspace_bytes < lay.total)
+    return fail(TTTJ_ERR_INVALID, "workspace too small: %zu < %zu", workspace_bytes, lay.total);
+  if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(workspace)) & (kAlign - 1))
+    return fail(TTTJ_ERR_INVALID, "weights and workspace must be 256-byte aligned");
+  DeviceGuard guard(device);
+  int cc_major = 0, cc_minor = 0;
+  TTTJ_CUDA(cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, device));
+  TTTJ_CUDA(cudaDeviceGetAttribute(&cc_minor, cudaDevAttrComputeCapabilityMinor, device));
+  if (cc_major != 10 || cc_minor != 0)
+    return fail(TTTJ_ERR_INVALID, "device %d is sm_%d%d; this library is built for sm_100a only",
+                device, cc_major, cc_minor);
+
+  tttj_plan* p = new tttj_plan();
+  p->cfg = *cfg;
+  p->device = device;
+  p->num_sms = sm_count(device);
+  p->weights = static_cast<const uint8_t*>(weights);
+  p->ws = static_cast<uint8_t*>(workspace);
+  p->lay = lay;
+  p->tp = token_plan_at(p->ws, lay);
+  p->status = reinterpret_cast<int*>(p->ws + lay.status);
+  p->resid = reinterpret_cast<__half*>(p->ws + lay.resid);
+  p->h = reinterpret_cast<__half*>(p->ws + lay.h);
+  p->qkv = reinterpret_cast<__half*>(p->ws + lay.qkv);
+  p->ctx = reinterpret_cast<__half*>(p->ws + lay.ctx);
+  p->hid = reinterpret_cast<__half*>(p->ws + lay.hid);
+
+  const int B = cfg->batch_size, S = cfg->seq_len, D = cfg->d_model, F = cfg->ffn_dim;
+  const int T = B * S;
+  const int* rows_dev = p->tp.seq_off + B;  // number of valid tokens
+  auto W = [&](int layer, int field) -> const uint8_t* {
+    size_t off = 0, bytes = 0;
+    weight_offset(*cfg, layer, field, &off, &bytes);
+    return p->weights + off;
+  };
+  p->layers.resize(cfg->num_layers);
+  for (int l = 0; l < cfg->num_layers; ++l) {
+    LayerGemms& L = p->layers[l];
+    L.ln1_w = reinterpret_cast<const float*>(W(l, TTTJ_LN1_W));
+    L.ln1_b = reinterpret_cast<const float*>(W(l, TTTJ_LN1_B));
+    L.ln2_w = reinterpret_cast<const float*>(W(l, TTTJ_LN2_W));
+    L.ln2_b = reinterpret_cast<const float*>(W(l, TTTJ_LN2_B));
+    rc = build_gemm(&L.qkv, p->h, D, W(l, TTTJ_W_QKV), D,
+                    reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)), p->qkv, 3 * D, nullptr, 0, T,
+                    rows_dev, 3 * D, D, EPI_BIAS, p->status, p->num_sms);
+    if (!rc)
+      rc = build_gemm(&L.out, p->ctx, D, W(l, TTTJ_W_OUT), D,
+                      reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
+                      T, rows_dev, D, D, EPI_BIAS_RESIDUAL, p->status, p->num_sms);
+    if (!rc)
+      rc = build_gemm(&L.ffn_in, p->h, D, W(l, TTTJ_W_FFN_IN), D,
+                      reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), p->hid, F, nullptr, 0,
+                      T, rows_dev, F, D, EPI_BIAS_GELU, p->status, p->num_sms);
+    if (!rc)
+      rc = build_gemm(&L.ffn_out, p->hid, F, W(l, TTTJ_W_FFN_OUT), F,
+                      reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D, p->resid,
+                      D, T, rows_dev, D, F, EPI_BIAS_RESIDUAL, p->status, p->num_sms);
+    if (rc) {
+      delete p;
+      return rc;
+    }
+  }
+  p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
+  p->lnf_b = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_B));
+
+  const int hd = D / cfg->num_heads;
+  p->attn.qkv = p->qkv;
+  p->attn.ctx = p->ctx;
+  p->attn.seq_off = p->tp.seq_off;
+  p->attn.items = p->tp.items;
+  p->attn.item_count = p->tp.item_count;
+  p->attn.d_model = D;
+  p->attn.causal = cfg->causal ? 1 : 0;
+  p->attn.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  p->attn_grid = (int)attn_items_max(B, S, cfg->num_heads);
+  *out_plan = p;
+  return TTTJ_OK;
+}
+
+int tttj_plan_destroy(tttj_plan* plan) {
+  if (plan) {
+    DeviceGuard guard(plan->device);
+    destroy_events(plan);
+  }
+  delete plan;
+  return TTTJ_OK;
+}
+
+int tttj_plan_launch_count(tttj_plan* plan) {
+  return plan ? launches_per_forward(plan->cfg) : 0;
+}
+
+int tttj_plan_enable_timing(tttj_plan* p, int enable) {
+  if (!p) return fail(TTTJ_ERR_INVALID, "timing: null plan");
+  DeviceGuard guard(p->device);
+  if (enable && !p->timing) {
+    const int n = launches_per_forward(p->cfg);
+    p->ev_start.resize(n);
+    p->ev_stop.resize(n);
+    p->ev_class.assign(n, 0);
+    for (int i = 0; i < n; ++i) {
+      TTTJ_CUDA(cudaEventCreate(&p->ev_start[i]));
+      TTTJ_CUDA(cudaEventCreate(&p->ev_stop[i]));
+    }
+  } else if (!enable && p->timing) {
+    int rc = collect_timing(p);
+    destroy_events(p);
+    if (rc) return rc;
+  }
+  p->timing = enable != 0;
+  for (int i = 0; i < TTTJ_KCLASS_COUNT; ++i) {
+    p->class_ms[i] = 0.0;
+    p->class_launches[i] = 0;
+  }
+  return TTTJ_OK;
+}
+
+int tttj_plan_kernel_times(tttj_plan* p, double* total_ms, long* launches) {
+  if (!p || !total_ms || !launches) return fail(TTTJ_ERR_INVALID, "timing: null argument");
+  DeviceGuard guard(p->device);
+  if (p->timing) {
+    int rc = collect_timing(p);
+    if (rc) return rc;
+  }
+  for (int i = 0; i < TTTJ_KCLASS_COUNT; ++i) {
+    total_ms[i] = p->class_ms[i];
+    launches[i] = p->class_launches[i];
+  }
+  return TTTJ_OK;
+}
+
+const char* tttj_kernel_class_name(int cls) {
+  static const char* names[TTTJ_KCLASS_COUNT] = {
+      "plan_tokens", "layernorm", "gemm_qkv", "attention", "gemm_out_proj",
+      "gemm_ffn_in_gelu", "gemm_ffn_out", "final_layernorm_scatter"};
+  return (cls >= 0 && cls < TTTJ_KCLASS_COUNT) ? names[cls] : "";
+}
+
+int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask, void* out,
+                 void* stream_ptr) {
+  if (!p || !x || !out) return fail(TTTJ_ERR_INVALID, "forward: null argument");
+  if (x_dtype != TTTJ_DTYPE_F16 && x_dtype != TTTJ_DTYPE_F32)
+    return fail(TTTJ_ERR_INVALID, "forward: x must be fp16 or fp32");
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 31)
+    return fail(TTTJ_ERR_INVALID, "forward: x and out must be 32-byte aligned");
+  DeviceGuard guard(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream_ptr);
+  const tttj_config& c = p->cfg;
+  const int B = c.batch_size, S = c.seq_len, D = c.d_model, T = B * S;
+  const int hd = D / c.num_heads;
+  const int* rows_dev = p->tp.seq_off + B;
+
+  // Per-class timing: an event pair around every launch when enabled.
+  if (p->timing) {
+    int rc = collect_timing(p);
+    if (rc) return rc;
+  }
+  size_t slot = 0;
+  auto tick = [&](int cls) -> cudaError_t {
+    if (!p->timing) return cudaSuccess;
+    p->ev_class[slot] = cls;
+    return cudaEventRecord(p->ev_start[slot], s);
+  };
+  auto tock = [&]() -> cudaError_t {
+    if (!p->timing) return cudaSuccess;
+    return cudaEventRecord(p->ev_stop[slot++], s);
+  };
+#define TTTJ_TIMED(cls, call)      \
+  do {                             \
+    TTTJ_CUDA(tick(cls));          \
+    TTTJ_CUDA(call);               \
+    TTTJ_CUDA(tock());             \
+  } while (0)
+
+  TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal, p->tp, s));
+  TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
+             ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->layers[0].ln1_w,
+                              p->layers[0].ln1_b, kLnEps, p->resid, p->h, s));
+  for (int l = 0; l < c.num_layers; ++l) {
+    const LayerGemms& L = p->layers[l];
+    if (l > 0)
+      TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
+                 ln_rows_launch(p->resid, rows_dev, T, D, L.ln1_w, L.ln1_b, kLnEps, p->h, s));
+    TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
+    TTTJ_TIMED(TTTJ_KCLASS_ATTENTION, attention_launch(p->attn, hd, p->attn_grid, s));
+    TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
+    TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
+               ln_rows_launch(p->resid, rows_dev, T, D, L.ln2_w, L.ln2_b, kLnEps, p->h, s));
+    TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
+    TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));
+  }
+  TTTJ_TIMED(TTTJ_KCLASS_FINAL_LN,
+             ln_final_launch(p->resid, p->tp.dst_map, T, D, p->lnf_w, p->lnf_b, kLnEps, out,
+                             x_dtype, s));
+#undef TTTJ_TIMED
+  p->ev_used = slot;
+  return TTTJ_OK;
+}
+
+int tttj_plan_status(tttj_plan* p, int* device_status) {
+  if (!p || !device_status) return fail(TTTJ_ERR_INVALID, "status: null argument");
+  DeviceGuard guard(p->device);
+  TTTJ_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  TTTJ_CUDA(cudaMemcpy(&v, p->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v != 0) TTTJ_CUDA(cudaMemset(p->status, 0, sizeof(int)));
+  *device_status = v;
+  if (v != 0) return fail(TTTJ_ERR_DEVICE_TIMEOUT, "device wait timed out (status 0x%x)", v);
+  return TTTJ_OK;
+}
+
+int tttj_linear(const void* a, int lda, const void* w, int ldw, const float* bias, void* out,
+                int ldo, const void* residual, int ldr, int rows, const int* rows_dev, int n, int k,
+                int epilogue, int* status_dev, void* stream) {
+  if (!a || !w || !bias || !out) return fail(TTTJ_ERR_INVALID, "linear: null argument");
+  if (rows == 0) return TTTJ_OK;
+  GemmLaunch g;
+  int rc = build_gemm(&g, a, lda, w, ldw, bias, out, ldo, residual, ldr, rows, rows_dev, n, k,
+                      epilogue, status_dev, -1);
+  if (rc) return rc;
+  TTTJ_CUDA(gemm_launch(g, static_cast<cudaStream_t>(stream)));
+  return TTTJ_OK;
+}
+
+int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamma,
+                   const float* beta, float eps, void* stream) {
+  if (!in || !out || !gamma || !beta) return fail(TTTJ_ERR_INVALID, "layernorm: null argument");
+  if (d <= 0 || d % 8 || d > 2048) return fail(TTTJ_ERR_INVALID, "layernorm: d=%d unsupported", d);
+  if (rows < 0) return fail(TTTJ_ERR_INVALID, "layernorm: rows < 0");
+  if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
+       reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15)
+    return fail(TTTJ_ERR_INVALID, "layernorm: pointers must be 16-byte aligned");
+  TTTJ_CUDA(ln_rows_launch(static_cast<const __half*>(in), nullptr, rows, d, gamma, beta, eps,
+                           static_cast<__half*>(out), static_cast<cudaStream_t>(stream)));
+  return TTTJ_OK;
+}
+
+size_t tttj_attention_workspace_bytes(int batch, int seq_len, int num_heads) {
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0) return 0;
+  WsLayout w{};
+  return plan_layout(batch, seq_len, num_heads, &w);
+}
+
+int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch, int seq_len,
+                   int d_model, int num_heads, int causal, void* workspace,
+                   size_t workspace_bytes, void* stream) {
+  if (!qkv || !ctx || !workspace) return fail(TTTJ_ERR_INVALID, "attention: null argument");
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads)
+    return fail(TTTJ_ERR_INVALID, "attention: bad shape");
+  const int hd = d_model / num_heads;
+  if (hd != 32 && hd != 64)
+    return fail(TTTJ_ERR_INVALID, "attention: head_dim=%d unsupported (32, 64)", hd);
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15)
+    return fail(TTTJ_ERR_INVALID, "attention: qkv and ctx must be 16-byte aligned");
+  WsLayout w{};
+  const size_t need = plan_layout(batch, seq_len, num_heads, &w);
+  if (workspace_bytes < need)
+    return fail(TTTJ_ERR_INVALID, "attention: workspace too small: %zu < %zu", workspace_bytes, need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  TokenPlan tp = token_plan_at(base, w);
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, tp, s));
+  AttnParams ap;
+  ap.qkv = static_cast<const __half*>(qkv);
+  ap.ctx = static_cast<__half*>(ctx);
+  ap.seq_off = tp.seq_off;
+  ap.items = tp.items;
+  ap.item_count = tp.item_count;
+  ap.d_model = d_model;
+  ap.causal = causal ? 1 : 0;
+  ap.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  TTTJ_CUDA(attention_launch(ap, hd, (int)attn_items_max(batch, seq_len, num_heads), s));
+  return TTTJ_OK;
+}
+
+int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream) {
+  if (!status_dev) return fail(TTTJ_ERR_INVALID, "selftest: null status");
+  TTTJ_CUDA(selftest_wait_launch(status_dev, limit_ns, static_cast<cudaStream_t>(stream)));
+  return TTTJ_OK;
+}
+
+}  // extern "C"

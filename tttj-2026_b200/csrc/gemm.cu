@@ -1,0 +1,57 @@
+// Instantiations and launcher of the K1 tcgen05 GEMM (gemm_tc.cuh).
+#include "launch.h"
+#include "gemm_tc.cuh"
+
+namespace tttj {
+
+namespace {
+
+constexpr int STAGES_BN128 = 6;  // 6 x 32 KB ring
+constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring
+
+template <int BN, int EPI, int STAGES>
+cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
+  auto kern = gemm_tc_kernel<BN, EPI, STAGES>;
+  constexpr int smem = GemmSmem<BN, STAGES>::TOTAL;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<g.grid, GEMM_THREADS, smem, stream>>>(g.tmA, g.tmB, g.p);
+  return cudaGetLastError();
+}
+
+template <int BN, int STAGES>
+cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
+  switch (g.epi) {
+    case EPI_BIAS:
+      return launch_t<BN, EPI_BIAS, STAGES>(g, stream);
+    case EPI_BIAS_GELU:
+      return launch_t<BN, EPI_BIAS_GELU, STAGES>(g, stream);
+    case EPI_BIAS_RESIDUAL:
+      return launch_t<BN, EPI_BIAS_RESIDUAL, STAGES>(g, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace
+
+int gemm_choose_bn(int rows, int n, int num_sms) {
+  const long m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
+  auto cost = [&](int bn) {
+    const long tiles = m_tiles * ((n + bn - 1) / bn);
+    const long waves = (tiles + num_sms - 1) / num_sms;
+    // A tile's time grows with its width plus a fixed per-tile overhead (prologue,
+    // epilogue drain), modelled as 32 columns.
+    return waves * (bn + 32);
+  };
+  if (n % 256 != 0) return 128;
+  return cost(256) <= cost(128) ? 256 : 128;
+}
+
+cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream) {
+  if (g.bn == 256) return launch_bn<256, STAGES_BN256>(g, stream);
+  if (g.bn == 128) return launch_bn<128, STAGES_BN128>(g, stream);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tttj

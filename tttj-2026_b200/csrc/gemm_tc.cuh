@@ -1,0 +1,259 @@
+// K1: persistent, warp-specialised tcgen05 GEMM with fused epilogues.
+//
+//   out[m, n] = epilogue( sum_k A[m, k] * W[n, k] + bias[n] )
+//
+// A is a token-major activation [rows, K] fp16, W an nn.Linear weight [N, K] fp16
+// (both K-major).  This replaces the reference's cuBLAS `F.linear` calls and its
+// Triton linear-epilogue kernels (kernels/case13_linear.py:149-259,
+// kernels/layerwise_hybrid.py:188-192,307,324-327) for the four projections of
+// BaselineTransformerBlock (benchmarks/torch_transformer_benchmark.py:72-75,131-132).
+//
+// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
+// warp 1 owns TMEM and one thread issues tcgen05.mma (M=128, N=BN, K=16), warps 2-5
+// drain the double-buffered TMEM accumulator (tcgen05.ld 32x32b) through the
+// epilogue while the next tile's MMAs run.  One CTA per SM; tiles are walked
+// persistently, N-tile fastest, so the CTAs in flight share A row-blocks in L2.
+// The number of valid rows is read from device memory, so one launch shape serves
+// every valid-token count (no host synchronisation on the mask).
+#pragma once
+#include "common.cuh"
+#include "params.h"
+
+namespace tttj {
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
+  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int BAR_BYTES = (2 * STAGES + 4 + 1) * 8 + 16;
+  // +1024 so the tile ring can be aligned to the 1024-byte swizzle atom.
+  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+};
+
+template <int BN, int EPI, int STAGES>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const GemmParams p) {
+  using L = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sA = smem_u32(smem);
+  const uint32_t sB = sA + STAGES * L::A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  const uint32_t bar_accf = bar_empty + 8 * STAGES;
+  const uint32_t bar_acce = bar_accf + 16;
+  const uint32_t bar_drain = bar_acce + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  const int rows = p.rows_dev ? min(*p.rows_dev, p.rows_max) : p.rows_max;
+  const int m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
+  const int n_tiles = p.n / BN + ((p.n % BN) ? 1 : 0);
+  const int num_tiles = m_tiles * n_tiles;
+  const int k_iters = p.k / GEMM_BK;
+  const uint64_t limit = p.wait_limit_ns;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar_accf + 8 * b, 1);
+      mbar_init(bar_acce + 8 * b, 4 * 32);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      long issued = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile / n_tiles;
+        const int n_blk = tile - m_blk * n_tiles;
+        for (int kk = 0; kk < k_iters; ++kk) {
+          if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, limit)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bar_full + 8 * stage, L::STAGE_BYTES);
+          tma_load_2d(sA + stage * L::A_BYTES, &tmA, bar_full + 8 * stage, kk * GEMM_BK,
+                      m_blk * GEMM_BM);
+          tma_load_2d(sB + stage * L::B_BYTES, &tmB, bar_full + 8 * stage, kk * GEMM_BK,
+                      n_blk * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_PRODUCER);
+        // Let the loads already issued land before the CTA can exit.
+        for (long j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j) {
+          mbar_wait(bar_full + 8 * (int)(j % STAGES), (uint32_t)((j / STAGES) & 1), nullptr,
+                    limit);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16_f32(GEMM_BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(bar_acce + 8 * acc, acc_phase ^ 1u, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kk = 0; kk < k_iters; ++kk) {
+          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = desc_kmajor_sw128(sA + stage * L::A_BYTES);
+          const uint64_t bdesc = desc_kmajor_sw128(sB + stage * L::B_BYTES);
+#pragma unroll
+          for (int j = 0; j < GEMM_BK / 16; ++j) {
+            // Advance 16 fp16 (32 B) along K inside the 128-byte swizzle atom.
+            mma_f16_ss(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
+                       (kk | j) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          mma_commit(bar_empty + 8 * stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(bar_accf + 8 * acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_MMA);
+        if (issued_any) {
+          // Wait for the MMAs already issued before TMEM is released.
+          mma_commit(bar_drain);
+          mbar_wait(bar_drain, 0, nullptr, limit);
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 2..5 ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = quad * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_blk = tile / n_tiles;
+      const int n_blk = tile - m_blk * n_tiles;
+      if (!mbar_wait(bar_accf + 8 * acc, acc_phase, abort_flag, limit)) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);
+        break;
+      }
+      tc_fence_after();
+      const int row = m_blk * GEMM_BM + row_in_tile;
+      const bool row_ok = row < rows;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
+        tmem_wait_ld();
+        const int col0 = n_blk * BN + c * 32;
+        if (row_ok && col0 < p.n) {
+          const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+          float v[32];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+          }
+          if (EPI == EPI_BIAS_GELU) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          }
+          if (EPI == EPI_BIAS_RESIDUAL) {
+            const uint4* rs =
+                reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col0);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 rv = rs[q];
+              const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 res = unpack_half2(rr[e]);
+                v[8 * q + 2 * e + 0] += res.x;
+                v[8 * q + 2 * e + 1] += res.y;
+              }
+            }
+          }
+          uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + col0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            dst[q] = make_uint4(pack_half2(v[8 * q + 0], v[8 * q + 1]),
+                                pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                                pack_half2(v[8 * q + 4], v[8 * q + 5]),
+                                pack_half2(v[8 * q + 6], v[8 * q + 7]));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_acce + 8 * acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+}  // namespace tttj

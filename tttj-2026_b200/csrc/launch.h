@@ -1,0 +1,39 @@
+// Internal host-side launch interface shared by the .cu translation units.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "params.h"
+
+namespace tttj {
+
+struct GemmLaunch {
+  CUtensorMap tmA;
+  CUtensorMap tmB;
+  GemmParams p;
+  int bn;   // 128 or 256
+  int epi;  // GemmEpilogue
+  int grid; // persistent CTAs
+};
+
+// Column-tile width for a GEMM of `rows` x `n` on `num_sms` SMs: the one with the
+// smaller (waves x tile cost) estimate.
+int gemm_choose_bn(int rows, int n, int num_sms);
+cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
+
+cudaError_t attention_launch(const AttnParams& p, int head_dim, int grid, cudaStream_t stream);
+
+cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal,
+                               const TokenPlan& plan, cudaStream_t stream);
+cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
+                             int rows_max, int D, const float* gamma, const float* beta, float eps,
+                             __half* resid, __half* out, cudaStream_t stream);
+cudaError_t ln_rows_launch(const __half* in, const int* rows_dev, int rows_max, int D,
+                           const float* gamma, const float* beta, float eps, __half* out,
+                           cudaStream_t stream);
+cudaError_t ln_final_launch(const __half* resid, const int* dst_map, int tokens, int D,
+                            const float* gamma, const float* beta, float eps, void* out,
+                            int out_dtype, cudaStream_t stream);
+cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream);
+
+}  // namespace tttj

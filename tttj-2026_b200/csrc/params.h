@@ -1,0 +1,77 @@
+// Kernel parameter blocks and tile constants shared between the kernels and the
+// host-side launch code.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#ifndef TTTJ_WAIT_LIMIT_NS
+// A device-side wait that has not completed after this many nanoseconds is treated
+// as a hang: the waiting role records an error code and the kernel winds down.
+#define TTTJ_WAIT_LIMIT_NS 2000000000ull
+#endif
+
+// Status codes written into the caller-visible device status word.
+enum TttjDeviceStatus : int {
+  TTTJ_DEV_OK = 0,
+  TTTJ_DEV_TIMEOUT_PRODUCER = 0x101,
+  TTTJ_DEV_TIMEOUT_MMA = 0x102,
+  TTTJ_DEV_TIMEOUT_EPILOGUE = 0x103,
+  TTTJ_DEV_TIMEOUT_SELFTEST = 0x1ff,
+  TTTJ_DEV_TIMEOUT_ATTN = 0x201,
+};
+
+
+namespace tttj {
+
+enum GemmEpilogue : int {
+  EPI_BIAS = 0,           // out = fp16(acc + bias)
+  EPI_BIAS_GELU = 1,      // out = fp16(gelu_erf(acc + bias))
+  EPI_BIAS_RESIDUAL = 2,  // out = fp16(residual + acc + bias), out may alias residual
+};
+
+struct GemmParams {
+  const int* rows_dev;  // device count of valid rows (nullable: use rows_max)
+  int rows_max;         // rows allocated in A / out
+  int n;                // output columns (multiple of 32)
+  int k;                // reduction length (multiple of 64)
+  const float* bias;    // [n] fp32
+  __half* out;          // [rows, ldo]
+  int ldo;
+  const __half* residual;  // [rows, ldr] (EPI_BIAS_RESIDUAL)
+  int ldr;
+  int* status;          // device status word (nullable)
+  unsigned long long wait_limit_ns;
+};
+
+constexpr int GEMM_BM = 128;
+constexpr int GEMM_BK = 64;
+constexpr int GEMM_THREADS = 192;
+
+struct AttnParams {
+  const __half* qkv;     // [rows, 3*D]: q | k | v, head h at columns h*hd
+  __half* ctx;           // [rows, D]
+  const int* seq_off;    // [B+1] first packed row of each sequence
+  const int2* items;     // work list: {b, (q_tile << 8) | h}
+  const int* item_count; // number of valid items
+  int d_model;
+  int causal;
+  float scale_log2;      // hd^-0.5 * log2(e)
+};
+
+constexpr int ATT_BM = 128;
+constexpr int ATT_BN = 64;
+constexpr int ATT_THREADS = 256;
+
+struct TokenPlan {
+  int* seq_len;     // [B]
+  int* seq_off;     // [B+1]; seq_off[B] = number of valid tokens
+  int* packed_src;  // [B*S] packed row -> b*S + s
+  int* dst_map;     // [B*S] b*S + s -> packed row, or -1
+  int2* items;      // [B*H*ceil(S/128)] attention work list
+  int* item_count;  // [1]
+};
+
+constexpr int PLAN_THREADS = 1024;
+
+}  // namespace tttj

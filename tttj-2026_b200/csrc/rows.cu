@@ -1,0 +1,87 @@
+// Launchers of the token plan and the LayerNorm row kernels (rows.cuh).
+#include "launch.h"
+#include "rows.cuh"
+
+namespace tttj {
+
+namespace {
+constexpr int ROWS_PER_CTA = 8;  // one warp per row, 256 threads
+
+inline int ln_vpl(int D) { return (D + 255) / 256; }
+}  // namespace
+
+cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal,
+                               const TokenPlan& plan, cudaStream_t stream) {
+  const int nkeys = (S + ATT_BN - 1) / ATT_BN + 1;
+  const size_t smem = sizeof(int) * (size_t)(2 * B + 1 + nkeys + 1);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(plan_tokens_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  plan_tokens_kernel<<<1, PLAN_THREADS, smem, stream>>>(mask, B, S, H, causal, ATT_BM, ATT_BN,
+                                                        plan);
+  return cudaGetLastError();
+}
+
+#define TTTJ_VPL_DISPATCH(VPL_EXPR, CALL) \
+  switch (VPL_EXPR) {                     \
+    case 1: { constexpr int V = 1; CALL; break; } \
+    case 2: { constexpr int V = 2; CALL; break; } \
+    case 3: { constexpr int V = 3; CALL; break; } \
+    case 4: { constexpr int V = 4; CALL; break; } \
+    case 5: case 6: { constexpr int V = 6; CALL; break; } \
+    case 7: case 8: { constexpr int V = 8; CALL; break; } \
+    default: return cudaErrorInvalidValue; \
+  }
+
+cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
+                             int rows_max, int D, const float* gamma, const float* beta, float eps,
+                             __half* resid, __half* out, cudaStream_t stream) {
+  const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  if (grid == 0) return cudaSuccess;
+  if (x_dtype == 0) {
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_gather_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                                      static_cast<const __half*>(x), packed_src, rows_dev, D, gamma,
+                                      beta, eps, resid, out)));
+  } else {
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_gather_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                                      static_cast<const float*>(x), packed_src, rows_dev, D, gamma,
+                                      beta, eps, resid, out)));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t ln_rows_launch(const __half* in, const int* rows_dev, int rows_max, int D,
+                           const float* gamma, const float* beta, float eps, __half* out,
+                           cudaStream_t stream) {
+  const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  if (grid == 0) return cudaSuccess;
+  TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                                    in, rows_dev, rows_max, D, gamma, beta, eps, out)));
+  return cudaGetLastError();
+}
+
+cudaError_t ln_final_launch(const __half* resid, const int* dst_map, int tokens, int D,
+                            const float* gamma, const float* beta, float eps, void* out,
+                            int out_dtype, cudaStream_t stream) {
+  const int grid = (tokens + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  if (grid == 0) return cudaSuccess;
+  if (out_dtype == 0) {
+    TTTJ_VPL_DISPATCH(ln_vpl(D),
+                      (ln_final_scatter_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                          resid, dst_map, tokens, D, gamma, beta, eps, static_cast<__half*>(out))));
+  } else {
+    TTTJ_VPL_DISPATCH(ln_vpl(D),
+                      (ln_final_scatter_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                          resid, dst_map, tokens, D, gamma, beta, eps, static_cast<float*>(out))));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace tttj

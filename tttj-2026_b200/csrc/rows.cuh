@@ -1,0 +1,306 @@
+// K4 row kernels and the token plan.
+//
+// * plan_tokens_kernel: turns valid_token_mask [B, S] into the packed valid-token
+//   layout (per-sequence valid counts and offsets, packed row -> source token,
+//   source token -> packed row or -1) and the attention work list ordered
+//   longest-first.  Replaces the reference's host-side mask handling
+//   (kernels/sequence_resident.py:164-192, kernels/case14_hybrid.py:642-672) with a
+//   device-side pass, so a forward never synchronises with the host.
+// * layernorm rows: nn.LayerNorm(d_model) (benchmarks/torch_transformer_benchmark.py:128,
+//   130, 160): biased variance, eps 1e-5, fp32 statistics, affine.
+//   - ln_gather_kernel: reads the caller's x (fp16 or fp32) at the packed rows,
+//     writes the fp16 residual stream and LN1 of layer 0.
+//   - ln_rows_kernel: LN of the packed residual stream.
+//   - ln_final_scatter_kernel: final LayerNorm + masked_fill(~mask, 0)
+//     (torch_transformer_benchmark.py:168-171), written back to [B, S, D] in the
+//     caller's dtype.
+#pragma once
+#include "common.cuh"
+#include "params.h"
+
+namespace tttj {
+
+// Single-CTA plan.  Dynamic shared memory: (2*B + 1 + nkeys + 1) ints.
+__global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t* __restrict__ mask,
+                                                                   int B, int S, int H, int causal,
+                                                                   int q_block, int kv_block,
+                                                                   TokenPlan plan) {
+  extern __shared__ int sh[];
+  int* cnt = sh;             // [B]
+  int* off = sh + B;         // [B+1]
+  int* hist = sh + 2 * B + 1;  // [nkeys+1]
+  const int nkeys = (S + kv_block - 1) / kv_block + 1;
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int nwarps = blockDim.x >> 5;
+
+  for (int i = threadIdx.x; i <= nkeys; i += blockDim.x) hist[i] = 0;
+  for (int b = warp; b < B; b += nwarps) {
+    int c = 0;
+    if (mask == nullptr) {
+      c = S;
+    } else {
+      for (int s = lane; s < S; s += 32) c += mask[(size_t)b * S + s] != 0;
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffff, c, o);
+    }
+    if (lane == 0) cnt[b] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int b = 0; b < B; ++b) {
+      off[b] = acc;
+      acc += cnt[b];
+    }
+    off[B] = acc;
+  }
+  __syncthreads();
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    plan.seq_len[b] = cnt[b];
+    plan.seq_off[b] = off[b];
+  }
+  if (threadIdx.x == 0) plan.seq_off[B] = off[B];
+
+  // Packed row maps: a warp per sequence, ballot-scan over 32 positions at a time.
+  for (int b = warp; b < B; b += nwarps) {
+    int running = off[b];
+    for (int s0 = 0; s0 < S; s0 += 32) {
+      const int s = s0 + lane;
+      const bool in = s < S;
+      const bool v = in && (mask == nullptr || mask[(size_t)b * S + s] != 0);
+      const unsigned bal = __ballot_sync(0xffffffff, v);
+      const int rank = __popc(bal & ((1u << lane) - 1u));
+      if (in) {
+        const int tok = b * S + s;
+        if (v) {
+          plan.packed_src[running + rank] = tok;
+          plan.dst_map[tok] = running + rank;
+        } else {
+          plan.dst_map[tok] = -1;
+        }
+      }
+      running += __popc(bal);
+    }
+  }
+
+  // Attention work list, longest first: key = number of kv blocks the item streams.
+  const int qt_max = (S + q_block - 1) / q_block;
+  for (int i = threadIdx.x; i < B * qt_max; i += blockDim.x) {
+    const int b = i / qt_max;
+    const int qt = i - b * qt_max;
+    const int len = cnt[b];
+    if (qt * q_block < len) {
+      const int kv_end = causal ? min(len, (qt + 1) * q_block) : len;
+      const int key = (kv_end + kv_block - 1) / kv_block;
+      atomicAdd(&hist[key], H);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int k = nkeys; k >= 0; --k) {
+      const int c = hist[k];
+      hist[k] = acc;  // start offset of bucket k (descending keys)
+      acc += c;
+    }
+    *plan.item_count = acc;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < B * qt_max; i += blockDim.x) {
+    const int b = i / qt_max;
+    const int qt = i - b * qt_max;
+    const int len = cnt[b];
+    if (qt * q_block < len) {
+      const int kv_end = causal ? min(len, (qt + 1) * q_block) : len;
+      const int key = (kv_end + kv_block - 1) / kv_block;
+      const int pos = atomicAdd(&hist[key], H);
+      for (int h = 0; h < H; ++h) plan.items[pos + h] = make_int2(b, (qt << 8) | h);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// LayerNorm: one warp per row, each lane holds VPL 8-element vectors (D <= 256*VPL).
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load8(const T* src, float (&v)[8]);
+
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* src, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(src);
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack_half2(w[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+template <>
+__device__ __forceinline__ void load8<float>(const float* src, float (&v)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(src)[0];
+  const float4 b = reinterpret_cast<const float4*>(src)[1];
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+__device__ __forceinline__ void store8(__half* dst, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(dst) = make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]),
+                                              pack_half2(v[4], v[5]), pack_half2(v[6], v[7]));
+}
+__device__ __forceinline__ void store8(float* dst, const float (&v)[8]) {
+  reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+  reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+template <int VPL>
+__device__ __forceinline__ void ln_normalise(float (&x)[VPL][8], int D, const float* gamma,
+                                             const float* beta, float eps) {
+  const int lane = lane_id();
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    if ((lane + 32 * i) * 8 < D) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += x[i][e];
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+  const float mean = sum / (float)D;
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    if ((lane + 32 * i) * 8 < D) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float d = x[i][e] - mean;
+        sq += d * d;
+      }
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffff, sq, o);
+  const float rstd = rsqrtf(sq / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) {
+      float g[8], bb[8];
+      load8<float>(gamma + c, g);
+      load8<float>(beta + c, bb);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[i][e] = (x[i][e] - mean) * rstd * g[e] + bb[e];
+    }
+  }
+}
+
+// Layer-0 entry: gather the caller's rows into the packed fp16 residual stream and
+// write LN1 of them.
+template <int VPL, typename TIn>
+__global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ x,
+                                                        const int* __restrict__ packed_src,
+                                                        const int* __restrict__ rows_dev, int D,
+                                                        const float* gamma, const float* beta,
+                                                        float eps, __half* resid, __half* out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= *rows_dev) return;
+  const int src = packed_src[row];
+  const int lane = lane_id();
+  float v[VPL][8];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) {
+      load8<TIn>(x + (size_t)src * D + c, v[i]);
+      // The residual stream is fp16: LN1 sees the same rounded values the later
+      // residual adds do.
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = __half2float(__float2half_rn(v[i][e]));
+      store8(resid + (size_t)row * D + c, v[i]);
+    }
+  }
+  ln_normalise<VPL>(v, D, gamma, beta, eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) store8(out + (size_t)row * D + c, v[i]);
+  }
+}
+
+template <int VPL>
+__global__ void __launch_bounds__(256) ln_rows_kernel(const __half* __restrict__ in,
+                                                      const int* __restrict__ rows_dev,
+                                                      int rows_max, int D, const float* gamma,
+                                                      const float* beta, float eps,
+                                                      __half* __restrict__ out) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  const int rows = rows_dev ? min(*rows_dev, rows_max) : rows_max;
+  if (row >= rows) return;
+  const int lane = lane_id();
+  float v[VPL][8];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) load8<__half>(in + (size_t)row * D + c, v[i]);
+  }
+  ln_normalise<VPL>(v, D, gamma, beta, eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) store8(out + (size_t)row * D + c, v[i]);
+  }
+}
+
+// Final LayerNorm over every output token; padded tokens are written as exact zeros.
+template <int VPL, typename TOut>
+__global__ void __launch_bounds__(256) ln_final_scatter_kernel(const __half* __restrict__ resid,
+                                                               const int* __restrict__ dst_map,
+                                                               int tokens, int D,
+                                                               const float* gamma,
+                                                               const float* beta, float eps,
+                                                               TOut* __restrict__ out) {
+  const int tok = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (tok >= tokens) return;
+  const int lane = lane_id();
+  const int row = dst_map[tok];
+  float v[VPL][8];
+  if (row < 0) {
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      const int c = (lane + 32 * i) * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[i][e] = 0.f;
+      if (c < D) store8(out + (size_t)tok * D + c, v[i]);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) load8<__half>(resid + (size_t)row * D + c, v[i]);
+  }
+  ln_normalise<VPL>(v, D, gamma, beta, eps);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) store8(out + (size_t)tok * D + c, v[i]);
+  }
+}
+
+// Self-test of the bounded wait: waits on an mbarrier that nothing arrives on, with
+// a short limit, and reports TTTJ_DEV_TIMEOUT_SELFTEST.  Used by the failure
+// detection test; it never hangs.
+__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (!mbar_wait(smem_u32(&bar), 0, nullptr, limit_ns))
+      report_status(status, TTTJ_DEV_TIMEOUT_SELFTEST);
+  }
+}
+
+}  // namespace tttj

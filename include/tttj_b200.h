@@ -154,6 +154,7 @@ const char* tttj_kernel_class_name(int cls);
 #define TTTJ_EPI_BIAS 0
 #define TTTJ_EPI_BIAS_GELU 1
 #define TTTJ_EPI_BIAS_RESIDUAL 2
+#define TTTJ_EPI_BIAS_RESIDUAL_F32 3 /* out and residual fp32 (the forward's residual stream) */
 int tttj_linear(const void* a, int lda, const void* w, int ldw, const float* bias, void* out,
                 int ldo, const void* residual, int ldr, int rows, const int* rows_dev, int n, int k,
                 int epilogue, int* status_dev, void* stream);

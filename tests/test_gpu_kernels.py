@@ -19,7 +19,7 @@ def _close(out, ref, atol, rtol):
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 768, 256), (1000, 512, 512),
                                    (4096, 2048, 512), (2048, 1024, 4096), (77, 1536, 1024)])
-@pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual"])
+@pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual", "residual_f32"])
 def test_linear_matches_torch(M, N, K, epilogue):
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N * 3 + K)
     a = torch.randn(M, K, device=DEV, generator=g).half()
@@ -32,9 +32,16 @@ def test_linear_matches_torch(M, N, K, epilogue):
     elif epilogue == "residual":
         res = torch.randn(M, N, device=DEV, generator=g).half()
         ref = ref + res.float()
+    elif epilogue == "residual_f32":
+        res = torch.randn(M, N, device=DEV, generator=g) * 4
+        ref = ref + res
     out = ops.linear(a, w, b, epilogue=epilogue, residual=res)
     torch.cuda.synchronize()
-    _close(out, ref, atol=2e-3, rtol=2e-3)
+    if epilogue == "residual_f32":
+        assert out.dtype == torch.float32
+        _close(out, ref, atol=2e-4, rtol=2e-5)  # fp32 store: only the fp16 operands round
+    else:
+        _close(out, ref, atol=2e-3, rtol=2e-3)
 
 
 def test_linear_residual_in_place_and_device_row_count():

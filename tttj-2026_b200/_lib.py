@@ -24,6 +24,7 @@ DTYPE_F32 = 1
 EPI_BIAS = 0
 EPI_BIAS_GELU = 1
 EPI_BIAS_RESIDUAL = 2
+EPI_BIAS_RESIDUAL_F32 = 3
 
 # Packed weight fields (include/tttj_b200.h).
 W_QKV, W_OUT, W_FFN_IN, W_FFN_OUT = 0, 1, 2, 3

@@ -114,7 +114,7 @@ WsLayout ws_layout(const tttj_config& c) {
   WsLayout w{};
   const size_t T = (size_t)c.batch_size * c.seq_len, D = c.d_model, F = c.ffn_dim;
   size_t o = plan_layout(c.batch_size, c.seq_len, c.num_heads, &w);
-  w.resid = o; o += align_up(T * D * 2);
+  w.resid = o; o += align_up(T * D * 4);
   w.h = o; o += align_up(T * D * 2);
   w.qkv = o; o += align_up(T * 3 * D * 2);
   w.ctx = o; o += align_up(T * D * 2);
@@ -180,11 +180,12 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   if (n <= 0 || k <= 0 || rows < 0) return fail(TTTJ_ERR_INVALID, "linear: bad sizes");
   if (n % 32 != 0) return fail(TTTJ_ERR_INVALID, "linear: n=%d must be a multiple of 32", n);
   if (k % 64 != 0) return fail(TTTJ_ERR_INVALID, "linear: k=%d must be a multiple of 64", k);
-  if (lda % 8 || ldw % 8 || ldo % 8 || (epi == EPI_BIAS_RESIDUAL && ldr % 8))
+  const bool has_res = epi == EPI_BIAS_RESIDUAL || epi == EPI_BIAS_RESIDUAL_F32;
+  if (lda % 8 || ldw % 8 || ldo % 8 || (has_res && ldr % 8))
     return fail(TTTJ_ERR_INVALID, "linear: row strides must be multiples of 8 elements");
-  if (epi < EPI_BIAS || epi > EPI_BIAS_RESIDUAL)
+  if (epi < EPI_BIAS || epi > EPI_BIAS_RESIDUAL_F32)
     return fail(TTTJ_ERR_INVALID, "linear: unknown epilogue %d", epi);
-  if (epi == EPI_BIAS_RESIDUAL && residual == nullptr)
+  if (has_res && residual == nullptr)
     return fail(TTTJ_ERR_INVALID, "linear: residual epilogue needs a residual");
   if ((reinterpret_cast<uintptr_t>(bias) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
       (reinterpret_cast<uintptr_t>(residual) & 15))
@@ -208,9 +209,9 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   g->p.n = n;
   g->p.k = k;
   g->p.bias = bias;
-  g->p.out = static_cast<__half*>(out);
+  g->p.out = out;
   g->p.ldo = ldo;
-  g->p.residual = static_cast<const __half*>(residual);
+  g->p.residual = residual;
   g->p.ldr = ldr;
   g->p.status = status;
   g->p.wait_limit_ns = kWaitLimitNs;
@@ -260,7 +261,8 @@ struct tttj_plan {
   WsLayout lay;
   TokenPlan tp;
   int* status;
-  __half *resid, *h, *qkv, *ctx, *hid;
+  float* resid;  // fp32 residual stream
+  __half *h, *qkv, *ctx, *hid;
   std::vector<LayerGemms> layers;
   const float *lnf_w, *lnf_b;
   AttnParams attn;
@@ -372,7 +374,7 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   p->lay = lay;
   p->tp = token_plan_at(p->ws, lay);
   p->status = reinterpret_cast<int*>(p->ws + lay.status);
-  p->resid = reinterpret_cast<__half*>(p->ws + lay.resid);
+  p->resid = reinterpret_cast<float*>(p->ws + lay.resid);
   p->h = reinterpret_cast<__half*>(p->ws + lay.h);
   p->qkv = reinterpret_cast<__half*>(p->ws + lay.qkv);
   p->ctx = reinterpret_cast<__half*>(p->ws + lay.ctx);
@@ -399,7 +401,7 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     if (!rc)
       rc = build_gemm(&L.out, p->ctx, D, W(l, TTTJ_W_OUT), D,
                       reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
-                      T, rows_dev, D, D, EPI_BIAS_RESIDUAL, p->status, p->num_sms);
+                      T, rows_dev, D, D, EPI_BIAS_RESIDUAL_F32, p->status, p->num_sms);
     if (!rc)
       rc = build_gemm(&L.ffn_in, p->h, D, W(l, TTTJ_W_FFN_IN), D,
                       reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), p->hid, F, nullptr, 0,
@@ -407,7 +409,7 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     if (!rc)
       rc = build_gemm(&L.ffn_out, p->hid, F, W(l, TTTJ_W_FFN_OUT), F,
                       reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D, p->resid,
-                      D, T, rows_dev, D, F, EPI_BIAS_RESIDUAL, p->status, p->num_sms);
+                      D, T, rows_dev, D, F, EPI_BIAS_RESIDUAL_F32, p->status, p->num_sms);
     if (rc) {
       delete p;
       return rc;
@@ -533,12 +535,12 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     const LayerGemms& L = p->layers[l];
     if (l > 0)
       TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
-                 ln_rows_launch(p->resid, rows_dev, T, D, L.ln1_w, L.ln1_b, kLnEps, p->h, s));
+                 ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln1_w, L.ln1_b, kLnEps, p->h, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION, attention_launch(p->attn, hd, p->attn_grid, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
     TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
-               ln_rows_launch(p->resid, rows_dev, T, D, L.ln2_w, L.ln2_b, kLnEps, p->h, s));
+               ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln2_w, L.ln2_b, kLnEps, p->h, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));
   }
@@ -583,7 +585,7 @@ int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamm
   if ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out) |
        reinterpret_cast<uintptr_t>(gamma) | reinterpret_cast<uintptr_t>(beta)) & 15)
     return fail(TTTJ_ERR_INVALID, "layernorm: pointers must be 16-byte aligned");
-  TTTJ_CUDA(ln_rows_launch(static_cast<const __half*>(in), nullptr, rows, d, gamma, beta, eps,
+  TTTJ_CUDA(ln_rows_launch(in, 0, nullptr, rows, d, gamma, beta, eps,
                            static_cast<__half*>(out), static_cast<cudaStream_t>(stream)));
   return TTTJ_OK;
 }

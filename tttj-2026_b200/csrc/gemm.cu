@@ -28,6 +28,8 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
       return launch_t<BN, EPI_BIAS_GELU, STAGES>(g, stream);
     case EPI_BIAS_RESIDUAL:
       return launch_t<BN, EPI_BIAS_RESIDUAL, STAGES>(g, stream);
+    case EPI_BIAS_RESIDUAL_F32:
+      return launch_t<BN, EPI_BIAS_RESIDUAL_F32, STAGES>(g, stream);
     default:
       return cudaErrorInvalidValue;
   }

@@ -216,28 +216,42 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
             for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
           }
-          if (EPI == EPI_BIAS_RESIDUAL) {
-            const uint4* rs =
-                reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ldr + col0);
+          if (EPI == EPI_BIAS_RESIDUAL_F32) {
+            const float4* rs = reinterpret_cast<const float4*>(
+                static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                    (size_t)row * p.ldo + col0);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 rv = rs[q];
-              const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
+            for (int q = 0; q < 8; ++q) {
+              const float4 rv = rs[q];
+              dst[q] = make_float4(v[4 * q + 0] + rv.x, v[4 * q + 1] + rv.y, v[4 * q + 2] + rv.z,
+                                   v[4 * q + 3] + rv.w);
+            }
+          } else {
+            if (EPI == EPI_BIAS_RESIDUAL) {
+              const uint4* rs = reinterpret_cast<const uint4*>(
+                  static_cast<const __half*>(p.residual) + (size_t)row * p.ldr + col0);
 #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 res = unpack_half2(rr[e]);
-                v[8 * q + 2 * e + 0] += res.x;
-                v[8 * q + 2 * e + 1] += res.y;
+              for (int q = 0; q < 4; ++q) {
+                const uint4 rv = rs[q];
+                const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float2 res = unpack_half2(rr[e]);
+                  v[8 * q + 2 * e + 0] += res.x;
+                  v[8 * q + 2 * e + 1] += res.y;
+                }
               }
             }
-          }
-          uint4* dst = reinterpret_cast<uint4*>(p.out + (size_t)row * p.ldo + col0);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) +
+                                                  (size_t)row * p.ldo + col0);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            dst[q] = make_uint4(pack_half2(v[8 * q + 0], v[8 * q + 1]),
-                                pack_half2(v[8 * q + 2], v[8 * q + 3]),
-                                pack_half2(v[8 * q + 4], v[8 * q + 5]),
-                                pack_half2(v[8 * q + 6], v[8 * q + 7]));
+            for (int q = 0; q < 4; ++q) {
+              dst[q] = make_uint4(pack_half2(v[8 * q + 0], v[8 * q + 1]),
+                                  pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                                  pack_half2(v[8 * q + 4], v[8 * q + 5]),
+                                  pack_half2(v[8 * q + 6], v[8 * q + 7]));
+            }
           }
         }
       }

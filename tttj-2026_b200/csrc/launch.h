@@ -27,11 +27,12 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
                                const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, const float* gamma, const float* beta, float eps,
-                             __half* resid, __half* out, cudaStream_t stream);
-cudaError_t ln_rows_launch(const __half* in, const int* rows_dev, int rows_max, int D,
+                             float* resid, __half* out, cudaStream_t stream);
+// in_dtype: 0 = fp16 rows, 1 = fp32 rows.
+cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,
                            const float* gamma, const float* beta, float eps, __half* out,
                            cudaStream_t stream);
-cudaError_t ln_final_launch(const __half* resid, const int* dst_map, int tokens, int D,
+cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
                             const float* gamma, const float* beta, float eps, void* out,
                             int out_dtype, cudaStream_t stream);
 cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream);

@@ -28,6 +28,7 @@ enum GemmEpilogue : int {
   EPI_BIAS = 0,           // out = fp16(acc + bias)
   EPI_BIAS_GELU = 1,      // out = fp16(gelu_erf(acc + bias))
   EPI_BIAS_RESIDUAL = 2,  // out = fp16(residual + acc + bias), out may alias residual
+  EPI_BIAS_RESIDUAL_F32 = 3,  // fp32 out = fp32 residual + acc + bias (the residual stream)
 };
 
 struct GemmParams {
@@ -36,9 +37,9 @@ struct GemmParams {
   int n;                // output columns (multiple of 32)
   int k;                // reduction length (multiple of 64)
   const float* bias;    // [n] fp32
-  __half* out;          // [rows, ldo]
+  void* out;            // [rows, ldo], fp16 (fp32 for EPI_BIAS_RESIDUAL_F32)
   int ldo;
-  const __half* residual;  // [rows, ldr] (EPI_BIAS_RESIDUAL)
+  const void* residual;  // [rows, ldr], same type as out (residual epilogues)
   int ldr;
   int* status;          // device status word (nullable)
   unsigned long long wait_limit_ns;

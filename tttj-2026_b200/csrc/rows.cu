@@ -37,7 +37,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
 
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, const float* gamma, const float* beta, float eps,
-                             __half* resid, __half* out, cudaStream_t stream) {
+                             float* resid, __half* out, cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
   if (x_dtype == 0) {
@@ -52,17 +52,24 @@ cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, 
   return cudaGetLastError();
 }
 
-cudaError_t ln_rows_launch(const __half* in, const int* rows_dev, int rows_max, int D,
+cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,
                            const float* gamma, const float* beta, float eps, __half* out,
                            cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
-  TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
-                                    in, rows_dev, rows_max, D, gamma, beta, eps, out)));
+  if (in_dtype == 0) {
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                                      static_cast<const __half*>(in), rows_dev, rows_max, D, gamma,
+                                      beta, eps, out)));
+  } else {
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+                                      static_cast<const float*>(in), rows_dev, rows_max, D, gamma,
+                                      beta, eps, out)));
+  }
   return cudaGetLastError();
 }
 
-cudaError_t ln_final_launch(const __half* resid, const int* dst_map, int tokens, int D,
+cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
                             const float* gamma, const float* beta, float eps, void* out,
                             int out_dtype, cudaStream_t stream) {
   const int grid = (tokens + ROWS_PER_CTA - 1) / ROWS_PER_CTA;

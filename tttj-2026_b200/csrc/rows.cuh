@@ -9,8 +9,8 @@
 // * layernorm rows: nn.LayerNorm(d_model) (benchmarks/torch_transformer_benchmark.py:128,
 //   130, 160): biased variance, eps 1e-5, fp32 statistics, affine.
 //   - ln_gather_kernel: reads the caller's x (fp16 or fp32) at the packed rows,
-//     writes the fp16 residual stream and LN1 of layer 0.
-//   - ln_rows_kernel: LN of the packed residual stream.
+//     writes the fp32 residual stream and LN1 of layer 0.
+//   - ln_rows_kernel: LN of the packed residual stream (fp32) or of any fp16 rows.
 //   - ln_final_scatter_kernel: final LayerNorm + masked_fill(~mask, 0)
 //     (torch_transformer_benchmark.py:168-171), written back to [B, S, D] in the
 //     caller's dtype.
@@ -194,14 +194,14 @@ __device__ __forceinline__ void ln_normalise(float (&x)[VPL][8], int D, const fl
   }
 }
 
-// Layer-0 entry: gather the caller's rows into the packed fp16 residual stream and
-// write LN1 of them.
+// Layer-0 entry: gather the caller's rows into the packed fp32 residual stream and
+// write LN1 of them (fp16, the next GEMM's operand).
 template <int VPL, typename TIn>
 __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ x,
                                                         const int* __restrict__ packed_src,
                                                         const int* __restrict__ rows_dev, int D,
                                                         const float* gamma, const float* beta,
-                                                        float eps, __half* resid, __half* out) {
+                                                        float eps, float* resid, __half* out) {
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (row >= *rows_dev) return;
   const int src = packed_src[row];
@@ -212,10 +212,7 @@ __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ 
     const int c = (lane + 32 * i) * 8;
     if (c < D) {
       load8<TIn>(x + (size_t)src * D + c, v[i]);
-      // The residual stream is fp16: LN1 sees the same rounded values the later
-      // residual adds do.
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[i][e] = __half2float(__float2half_rn(v[i][e]));
+      // The residual stream is kept in fp32 between blocks.
       store8(resid + (size_t)row * D + c, v[i]);
     }
   }
@@ -227,8 +224,8 @@ __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ 
   }
 }
 
-template <int VPL>
-__global__ void __launch_bounds__(256) ln_rows_kernel(const __half* __restrict__ in,
+template <int VPL, typename TIn>
+__global__ void __launch_bounds__(256) ln_rows_kernel(const TIn* __restrict__ in,
                                                       const int* __restrict__ rows_dev,
                                                       int rows_max, int D, const float* gamma,
                                                       const float* beta, float eps,
@@ -241,7 +238,7 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const __half* __restrict__
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = (lane + 32 * i) * 8;
-    if (c < D) load8<__half>(in + (size_t)row * D + c, v[i]);
+    if (c < D) load8<TIn>(in + (size_t)row * D + c, v[i]);
   }
   ln_normalise<VPL>(v, D, gamma, beta, eps);
 #pragma unroll
@@ -253,7 +250,7 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const __half* __restrict__
 
 // Final LayerNorm over every output token; padded tokens are written as exact zeros.
 template <int VPL, typename TOut>
-__global__ void __launch_bounds__(256) ln_final_scatter_kernel(const __half* __restrict__ resid,
+__global__ void __launch_bounds__(256) ln_final_scatter_kernel(const float* __restrict__ resid,
                                                                const int* __restrict__ dst_map,
                                                                int tokens, int D,
                                                                const float* gamma,
@@ -277,7 +274,7 @@ __global__ void __launch_bounds__(256) ln_final_scatter_kernel(const __half* __r
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = (lane + 32 * i) * 8;
-    if (c < D) load8<__half>(resid + (size_t)row * D + c, v[i]);
+    if (c < D) load8<float>(resid + (size_t)row * D + c, v[i]);
   }
   ln_normalise<VPL>(v, D, gamma, beta, eps);
 #pragma unroll

@@ -33,22 +33,26 @@ def linear(a: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, *, epilogu
            rows_dev: Optional[torch.Tensor] = None, status: Optional[torch.Tensor] = None) -> torch.Tensor:
     """out = epi(a @ weight.T + bias) on the tcgen05 GEMM.
 
-    epilogue: "bias", "gelu" (exact erf GELU) or "residual" (out = residual + ...;
-    ``out`` may be ``residual`` itself).  a [M, K] fp16, weight [N, K] fp16,
-    bias [N] fp32, residual [M, N] fp16.
+    epilogue: "bias", "gelu" (exact erf GELU), "residual" (out = residual + ...;
+    ``out`` may be ``residual`` itself; fp16) or "residual_f32" (fp32 residual and
+    out, the forward's residual stream).  a [M, K] fp16, weight [N, K] fp16,
+    bias [N] fp32.
     """
-    epi = {"bias": _lib.EPI_BIAS, "gelu": _lib.EPI_BIAS_GELU, "residual": _lib.EPI_BIAS_RESIDUAL}[epilogue]
+    epi = {"bias": _lib.EPI_BIAS, "gelu": _lib.EPI_BIAS_GELU, "residual": _lib.EPI_BIAS_RESIDUAL,
+           "residual_f32": _lib.EPI_BIAS_RESIDUAL_F32}[epilogue]
     _need(a.dtype == torch.float16 and weight.dtype == torch.float16, "linear: a and weight must be fp16")
     _need(bias.dtype == torch.float32, "linear: bias must be fp32")
     _need(a.dim() == 2 and weight.dim() == 2 and a.shape[1] == weight.shape[1], "linear: shape mismatch")
     _need(a.stride(1) == 1 and weight.stride(1) == 1 and bias.is_contiguous(), "linear: inner dims must be contiguous")
     M, K = a.shape
     N = weight.shape[0]
+    out_dtype = torch.float32 if epi == _lib.EPI_BIAS_RESIDUAL_F32 else torch.float16
     if out is None:
-        out = torch.empty(M, N, dtype=torch.float16, device=a.device)
-    if epi == _lib.EPI_BIAS_RESIDUAL:
-        _need(residual is not None and residual.shape == (M, N) and residual.dtype == torch.float16,
-              "linear: residual must be fp16 [M, N]")
+        out = torch.empty(M, N, dtype=out_dtype, device=a.device)
+    _need(out.dtype == out_dtype and out.stride(1) == 1, f"linear: out must be {out_dtype} [M, N]")
+    if epi in (_lib.EPI_BIAS_RESIDUAL, _lib.EPI_BIAS_RESIDUAL_F32):
+        _need(residual is not None and residual.shape == (M, N) and residual.dtype == out_dtype,
+              f"linear: residual must be {out_dtype} [M, N]")
     rc = _lib.lib().tttj_linear(
         _ptr(a), a.stride(0), _ptr(weight), weight.stride(0), _ptr(bias), _ptr(out), out.stride(0),
         _ptr(residual), residual.stride(0) if residual is not None else 0, M, _ptr(rows_dev), N, K, epi,

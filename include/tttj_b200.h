@@ -180,6 +180,22 @@ int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int ba
                    int d_model, int num_heads, int causal, void* workspace,
                    size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of tttj_attention (no counterpart in the reference).
+ * For callers that cannot allocate device memory at call time -- code running inside
+ * an allocator or memory-pool callback, hosts that forbid cudaMalloc after start-up,
+ * runtimes that only pass pre-placed input/output buffers.  Same arguments and
+ * results as tttj_attention, minus the workspace: the token plan and work list live
+ * in a fixed device array of TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES inside the library
+ * (held on every GPU that loads the library until the process exits).  Shapes whose
+ * plan does not fit return TTTJ_ERR_INVALID without launching anything.  It calls no
+ * allocation routine.  The first call on a device looks up the array's device address
+ * (with that device current); make that first call before any stream capture.  All
+ * calls on a device share the array, so calls that overlap on the GPU race; nothing in
+ * it needs clearing between calls. */
+#define TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
+int tttj_attention_noalloc(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch,
+                           int seq_len, int d_model, int num_heads, int causal, void* stream);
+
 /* Failure-detection self test: launches a kernel whose bounded wait on an mbarrier
  * that is never signalled gives up after limit_ns and writes 0x1ff into *status_dev.
  * No counterpart in the reference (its device waits are unbounded). */

@@ -62,6 +62,9 @@ _SIGNATURES = {
         _c.c_int,
         [_vp, _vp, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp, _c.c_size_t, _vp],
     ),
+    "tttj_attention_noalloc": (
+        _c.c_int, [_vp, _vp, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp]
+    ),
     "tttj_selftest_wait_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
     "tttj_device_sm_count": (_c.c_int, [_c.c_int]),
     "tttj_plan_launch_count": (_c.c_int, [_vp]),

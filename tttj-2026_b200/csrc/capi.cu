@@ -635,3 +635,94 @@ int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream)
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free attention (tttj_attention_noalloc).
+//
+// Some callers cannot allocate device memory when they need attention: code that
+// runs inside a memory-pool or allocator callback (re-entering the allocator would
+// deadlock or recurse), hosts that forbid cudaMalloc once initialisation is over
+// (cudaMalloc can synchronise the device and fail under a fixed memory budget),
+// and runtimes that only hand a kernel its pre-placed input and output buffers.
+// For them this entry point keeps the token plan and the attention work list in a
+// fixed array of TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES that lives in the library's
+// own device memory; every GPU that loads the library holds that array until the
+// process exits.
+//
+// Host code must not pass g_attn_noalloc_scratch itself to a kernel: on the host the
+// name is only a stand-in for the device symbol.  The device address is looked up
+// once per device with cudaGetSymbolAddress, with that device current, on the first
+// call made on the device.  Because that first call does this set-up (and may make
+// the CUDA runtime load the library's device code), it should come before any stream
+// capture.
+//
+// All calls on a device share the one array and it keeps whatever the last call
+// wrote.  Nothing in it needs clearing: each call's plan kernel rewrites every value
+// its attention kernel later reads.  Calls whose kernels overlap on the GPU (for
+// example on two streams at once) race on the array and give wrong results.
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr size_t kNoallocScratchBytes = TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoallocMaxDevices] = {};
+
+// Device address of the scratch array on `device` (the current device).
+int noalloc_scratch_address(int device, void** out) {
+  if (device < 0 || device >= kNoallocMaxDevices)
+    return fail(TTTJ_ERR_INVALID, "attention_noalloc: device %d out of range", device);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[device] == nullptr) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(attention scratch)");
+    if (p == nullptr) return fail(TTTJ_ERR_CUDA, "attention_noalloc: null scratch address");
+    g_noalloc_addr[device] = p;
+  }
+  *out = g_noalloc_addr[device];
+  return TTTJ_OK;
+}
+
+}  // namespace
+
+extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, const uint8_t* valid_mask,
+                                      int batch, int seq_len, int d_model, int num_heads,
+                                      int causal, void* stream) {
+  if (!qkv || !ctx) return fail(TTTJ_ERR_INVALID, "attention_noalloc: null argument");
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads)
+    return fail(TTTJ_ERR_INVALID, "attention_noalloc: bad shape");
+  const int hd = d_model / num_heads;
+  if (hd != 32 && hd != 64)
+    return fail(TTTJ_ERR_INVALID, "attention_noalloc: head_dim=%d unsupported (32, 64)", hd);
+  if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15)
+    return fail(TTTJ_ERR_INVALID, "attention_noalloc: qkv and ctx must be 16-byte aligned");
+  WsLayout w{};
+  const size_t need = plan_layout(batch, seq_len, num_heads, &w);
+  if (need > kNoallocScratchBytes)
+    return fail(TTTJ_ERR_INVALID,
+                "attention_noalloc: batch=%d seq_len=%d num_heads=%d needs %zu bytes of scratch, "
+                "more than the built-in %zu; use tttj_attention with a caller workspace",
+                batch, seq_len, num_heads, need, kNoallocScratchBytes);
+  int dev = 0;
+  TTTJ_CUDA(cudaGetDevice(&dev));
+  void* scratch = nullptr;
+  int rc = noalloc_scratch_address(dev, &scratch);
+  if (rc) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  TokenPlan tp = token_plan_at(static_cast<uint8_t*>(scratch), w);
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, tp, s));
+  AttnParams ap;
+  ap.qkv = static_cast<const __half*>(qkv);
+  ap.ctx = static_cast<__half*>(ctx);
+  ap.seq_off = tp.seq_off;
+  ap.items = tp.items;
+  ap.item_count = tp.item_count;
+  ap.d_model = d_model;
+  ap.causal = causal ? 1 : 0;
+  ap.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  TTTJ_CUDA(attention_launch(ap, hd, (int)attn_items_max(batch, seq_len, num_heads), s));
+  return TTTJ_OK;
+}

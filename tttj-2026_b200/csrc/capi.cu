@@ -149,23 +149,32 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// 2-D fp16 row-major matrix [rows, cols] with row stride `ld` elements, loaded in
-// boxes of 64 columns (128 B, one swizzle atom) x box_rows rows, 128-byte swizzle.
-int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
-              uint32_t box_rows) {
+// 2-D row-major matrix [rows, cols] with row stride `ld` elements, moved in boxes of
+// box_cols x box_rows elements.
+int make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dtype, uint32_t elem_bytes,
+                 uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();
   if (!fn) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * elem_bytes) % 16)
     return fail(TTTJ_ERR_INVALID, "TMA operand must be 16-byte aligned with a 16-byte row stride");
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  cuuint64_t strides[1] = {ld * elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(m, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return TTTJ_OK;
+}
+
+// GEMM operand: fp16 [rows, cols], boxes of 64 columns (128 B, one swizzle atom) x
+// box_rows rows, 128-byte swizzle (the canonical K-major UMMA layout).
+int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+              uint32_t box_rows) {
+  return make_tmap_2d(m, base, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows, cols, ld, 64, box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int sm_count(int device) {
@@ -203,6 +212,15 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   int rc = make_tmap(&g->tmA, a, (uint64_t)(rows > 0 ? rows : 1), (uint64_t)k, (uint64_t)lda, GEMM_BM);
   if (rc) return rc;
   rc = make_tmap(&g->tmB, w, (uint64_t)n, (uint64_t)k, (uint64_t)ldw, (uint32_t)g->bn);
+  if (rc) return rc;
+  // Output: 32x32 boxes; fp32 rows of the box are 128 B (128-byte swizzle), fp16 rows
+  // 64 B (64-byte swizzle), matching the epilogue's staging layout.
+  if (epi == EPI_BIAS_RESIDUAL_F32)
+    rc = make_tmap_2d(&g->tmC, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(rows > 0 ? rows : 1),
+                      (uint64_t)n, (uint64_t)ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    rc = make_tmap_2d(&g->tmC, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)(rows > 0 ? rows : 1),
+                      (uint64_t)n, (uint64_t)ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   g->p.rows_dev = rows_dev;
   g->p.rows_max = rows;

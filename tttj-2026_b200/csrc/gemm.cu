@@ -6,8 +6,8 @@ namespace tttj {
 
 namespace {
 
-constexpr int STAGES_BN128 = 6;  // 6 x 32 KB ring
-constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring
+constexpr int STAGES_BN128 = 6;  // 6 x 32 KB ring (+32 KB output staging)
+constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring (+32 KB output staging)
 
 template <int BN, int EPI, int STAGES>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
@@ -15,7 +15,8 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
   constexpr int smem = GemmSmem<BN, STAGES>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<g.grid, GEMM_THREADS, smem, stream>>>(g.tmA, g.tmB, g.p);
+  static_assert(smem <= 232448, "GEMM shared memory exceeds the 227 KB per-CTA limit");
+  kern<<<g.grid, GEMM_THREADS, smem, stream>>>(g.tmA, g.tmB, g.tmC, g.p);
   return cudaGetLastError();
 }
 

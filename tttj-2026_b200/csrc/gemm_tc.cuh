@@ -8,11 +8,15 @@
 // kernels/layerwise_hybrid.py:188-192,307,324-327) for the four projections of
 // BaselineTransformerBlock (benchmarks/torch_transformer_benchmark.py:72-75,131-132).
 //
-// CTA = 6 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
-// warp 1 owns TMEM and one thread issues tcgen05.mma (M=128, N=BN, K=16), warps 2-5
+// CTA = 10 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
+// warp 1 owns TMEM and one thread issues tcgen05.mma (M=128, N=BN, K=16), warps 2-9
 // drain the double-buffered TMEM accumulator (tcgen05.ld 32x32b) through the
-// epilogue while the next tile's MMAs run.  One CTA per SM; tiles are walked
-// persistently, N-tile fastest, so the CTAs in flight share A row-blocks in L2.
+// epilogue while the next tile's MMAs run.  Two epilogue warps share each TMEM lane
+// quadrant and split the tile's columns.  Each epilogue warp stages a 32x32 output
+// block in shared memory (swizzled to match the store's tensor map) and writes it
+// with one TMA tile store; only the tile that straddles the last valid row falls back
+// to row-masked stores.  One CTA per SM; tiles are walked persistently, N-tile
+// fastest, so the CTAs in flight share A row-blocks in L2.
 // The number of valid rows is read from device memory, so one launch shape serves
 // every valid-token count (no host synchronisation on the mask).
 #pragma once
@@ -27,15 +31,16 @@ struct GemmSmem {
   static constexpr int B_BYTES = BN * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int OUT_BYTES = GEMM_EPI_WARPS * GEMM_STAGE_OUT_BYTES;
   static constexpr int BAR_BYTES = (2 * STAGES + 4 + 1) * 8 + 16;
   // +1024 so the tile ring can be aligned to the 1024-byte swizzle atom.
-  static constexpr int TOTAL = TILE_BYTES + BAR_BYTES + 1024;
+  static constexpr int TOTAL = TILE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
 };
 
 template <int BN, int EPI, int STAGES>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmParams p) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
   using L = GemmSmem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -43,7 +48,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   uint8_t* smem = smem_raw + pad;
   const uint32_t sA = smem_u32(smem);
   const uint32_t sB = sA + STAGES * L::A_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES);
+  const uint32_t sOut = sA + L::TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::TILE_BYTES + L::OUT_BYTES);
   const uint32_t bar_full = smem_u32(bars);
   const uint32_t bar_empty = bar_full + 8 * STAGES;
   const uint32_t bar_accf = bar_empty + 8 * STAGES;
@@ -65,13 +71,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8 * b, 1);
-      mbar_init(bar_acce + 8 * b, 4 * 32);
+      mbar_init(bar_acce + 8 * b, GEMM_EPI_WARPS * 32);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -178,9 +185,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue: warps 2..5 ----------------
-    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // ---------------- epilogue: warps 2..9 ----------------
+    constexpr bool OUT_F32 = EPI == EPI_BIAS_RESIDUAL_F32;
+    const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
+    const int col_half = (warp - 2) >> 2;       // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
+    const uint32_t stage_out = sOut + (uint32_t)((warp - 2) * GEMM_STAGE_OUT_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -194,55 +204,102 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const int row = m_blk * GEMM_BM + row_in_tile;
       const bool row_ok = row < rows;
+      // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
+      const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int cc = 0; cc < BN / 64; ++cc) {
+        const int c = col_half * (BN / 64) + cc;
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
         tmem_wait_ld();
         const int col0 = n_blk * BN + c * 32;
-        if (row_ok && col0 < p.n) {
-          const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
-          float v[32];
+        if (col0 >= p.n) continue;  // warp-uniform
+        const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
+        float v[32];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 bb = __ldg(b4 + q);
-            v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
-            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
-            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
-            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
-          }
-          if (EPI == EPI_BIAS_GELU) {
+        for (int q = 0; q < 8; ++q) {
+          const float4 bb = __ldg(b4 + q);
+          v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
+          v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+          v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+          v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+        }
+        if (EPI == EPI_BIAS_GELU) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
-          }
+          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+        }
+        if (row_ok) {
           if (EPI == EPI_BIAS_RESIDUAL_F32) {
             const float4* rs = reinterpret_cast<const float4*>(
                 static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
-                                                    (size_t)row * p.ldo + col0);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               const float4 rv = rs[q];
-              dst[q] = make_float4(v[4 * q + 0] + rv.x, v[4 * q + 1] + rv.y, v[4 * q + 2] + rv.z,
-                                   v[4 * q + 3] + rv.w);
+              v[4 * q + 0] += rv.x;
+              v[4 * q + 1] += rv.y;
+              v[4 * q + 2] += rv.z;
+              v[4 * q + 3] += rv.w;
             }
-          } else {
-            if (EPI == EPI_BIAS_RESIDUAL) {
-              const uint4* rs = reinterpret_cast<const uint4*>(
-                  static_cast<const __half*>(p.residual) + (size_t)row * p.ldr + col0);
+          } else if (EPI == EPI_BIAS_RESIDUAL) {
+            const uint4* rs = reinterpret_cast<const uint4*>(
+                static_cast<const __half*>(p.residual) + (size_t)row * p.ldr + col0);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const uint4 rv = rs[q];
-                const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
+            for (int q = 0; q < 4; ++q) {
+              const uint4 rv = rs[q];
+              const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float2 res = unpack_half2(rr[e]);
-                  v[8 * q + 2 * e + 0] += res.x;
-                  v[8 * q + 2 * e + 1] += res.y;
-                }
+              for (int e = 0; e < 4; ++e) {
+                const float2 res = unpack_half2(rr[e]);
+                v[8 * q + 2 * e + 0] += res.x;
+                v[8 * q + 2 * e + 1] += res.y;
               }
             }
+          }
+        }
+        if (full_tile) {
+          // The previous TMA store from this warp's staging block must have read it.
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+          if (OUT_F32) {
+            // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk j of row r at j ^ (r % 8).
+            const uint32_t rbase = stage_out + (uint32_t)(lane * 128);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const uint32_t dst = rbase + (uint32_t)(((j ^ (lane & 7)) & 7) << 4);
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
+                           "f"(v[4 * j + 0]), "f"(v[4 * j + 1]), "f"(v[4 * j + 2]),
+                           "f"(v[4 * j + 3])
+                           : "memory");
+            }
+          } else {
+            // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk j of row r at j ^ ((r / 2) % 4).
+            const uint32_t rbase = stage_out + (uint32_t)(lane * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t dst = rbase + (uint32_t)(((j ^ ((lane >> 1) & 3)) & 3) << 4);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
+                           "r"(pack_half2(v[8 * j + 0], v[8 * j + 1])),
+                           "r"(pack_half2(v[8 * j + 2], v[8 * j + 3])),
+                           "r"(pack_half2(v[8 * j + 4], v[8 * j + 5])),
+                           "r"(pack_half2(v[8 * j + 6], v[8 * j + 7]))
+                           : "memory");
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stage_out, col0, m_blk * GEMM_BM + quad * 32);
+            bulk_commit();
+          }
+        } else if (row_ok) {
+          if (OUT_F32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +
+                                                    (size_t)row * p.ldo + col0);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              dst[q] = make_float4(v[4 * q + 0], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+          } else {
             uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) +
                                                   (size_t)row * p.ldo + col0);
 #pragma unroll
@@ -260,6 +317,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+    // Stores issued by this warp must complete before the CTA exits.
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
 
   tc_fence_before();

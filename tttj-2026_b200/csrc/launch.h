@@ -10,6 +10,7 @@ namespace tttj {
 struct GemmLaunch {
   CUtensorMap tmA;
   CUtensorMap tmB;
+  CUtensorMap tmC;  // output, 32x32 boxes (TMA tile stores)
   GemmParams p;
   int bn;   // 128 or 256
   int epi;  // GemmEpilogue

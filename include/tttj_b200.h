@@ -166,9 +166,10 @@ int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamm
                    const float* beta, float eps, void* stream);
 
 /* Fused multi-head attention over the packed valid-token layout.
- *   qkv  [Tv, 3*d_model] fp16: valid tokens of sequence 0, then 1, ... in token
- *        order; columns q | k | v with head h at h*head_dim.
- *   ctx  [Tv, d_model] fp16 output (rows of valid tokens only).
+ *   qkv  [qkv_rows, 3*d_model] fp16: valid tokens of sequence 0, then 1, ... in token
+ *        order; columns q | k | v with head h at h*head_dim.  qkv_rows (>= the number
+ *        of valid tokens Tv) is the number of rows allocated in qkv and ctx.
+ *   ctx  [qkv_rows, d_model] fp16 output (rows of valid tokens are written).
  *   valid_mask [batch, seq_len] bytes or NULL (all valid) -- defines the packing.
  * Replaces packed_causal_attention / two_pass_causal_attention
  * (kernels/case8_attention.py:168, kernels/case14_attention.py:181) and the
@@ -176,8 +177,8 @@ int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamm
  * (torch_transformer_benchmark.py:97-117).  `workspace` (device, at least
  * tttj_attention_workspace_bytes) holds the token plan and work list. */
 size_t tttj_attention_workspace_bytes(int batch, int seq_len, int num_heads);
-int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch, int seq_len,
-                   int d_model, int num_heads, int causal, void* workspace,
+int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* valid_mask, int batch,
+                   int seq_len, int d_model, int num_heads, int causal, void* workspace,
                    size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of tttj_attention (no counterpart in the reference).
@@ -193,8 +194,9 @@ int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int ba
  * calls on a device share the array, so calls that overlap on the GPU race; nothing in
  * it needs clearing between calls. */
 #define TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
-int tttj_attention_noalloc(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch,
-                           int seq_len, int d_model, int num_heads, int causal, void* stream);
+int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows, const uint8_t* valid_mask,
+                           int batch, int seq_len, int d_model, int num_heads, int causal,
+                           void* stream);
 
 /* Failure-detection self test: launches a kernel whose bounded wait on an mbarrier
  * that is never signalled gives up after limit_ns and writes 0x1ff into *status_dev.

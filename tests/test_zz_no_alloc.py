@@ -41,8 +41,8 @@ def _noalloc(qkv, mask, B, S, H, causal):
     ctx = torch.full((qkv.shape[0], D), float("nan"), dtype=torch.float16, device=DEV)
     m = None if mask is None else mask.contiguous().view(torch.uint8)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = _lib.lib().tttj_attention_noalloc(_ptr(qkv), _ptr(ctx), _ptr(m), B, S, D, H,
-                                           1 if causal else 0, stream)
+    rc = _lib.lib().tttj_attention_noalloc(_ptr(qkv), _ptr(ctx), qkv.shape[0], _ptr(m), B, S, D,
+                                           H, 1 if causal else 0, stream)
     _lib.check(rc, "attention_noalloc")
     return ctx
 
@@ -82,8 +82,8 @@ def test_noalloc_repeat_and_mask_none():
 def test_noalloc_rejects_shapes_beyond_the_scratch():
     L = _lib.lib()
     # 4096 x 8192 tokens need ~270 MB of plan; nothing may be launched.
-    rc = L.tttj_attention_noalloc(ctypes.c_void_p(256), ctypes.c_void_p(256), None, 4096, 8192,
-                                  512, 8, 1, None)
+    rc = L.tttj_attention_noalloc(ctypes.c_void_p(256), ctypes.c_void_p(256), 4096 * 8192, None,
+                                  4096, 8192, 512, 8, 1, None)
     assert rc == _lib.TTTJ_ERR_INVALID
     msg = L.tttj_last_error().decode()
     assert "scratch" in msg and "tttj_attention" in msg

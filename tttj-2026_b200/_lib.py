@@ -60,10 +60,11 @@ _SIGNATURES = {
     "tttj_attention_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int]),
     "tttj_attention": (
         _c.c_int,
-        [_vp, _vp, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp, _c.c_size_t, _vp],
+        [_vp, _vp, _c.c_int, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp,
+         _c.c_size_t, _vp],
     ),
     "tttj_attention_noalloc": (
-        _c.c_int, [_vp, _vp, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp]
+        _c.c_int, [_vp, _vp, _c.c_int, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp]
     ),
     "tttj_selftest_wait_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
     "tttj_device_sm_count": (_c.c_int, [_c.c_int]),

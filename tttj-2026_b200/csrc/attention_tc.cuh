@@ -1,0 +1,418 @@
+// K2: flash attention on the 5th-generation tensor cores (tcgen05), S and P in TMEM.
+//
+// Computes, for every (sequence, head), softmax(q k^T * hd^-0.5 + mask) v over the
+// packed valid-token layout -- the score/mask/softmax/PV sequence of the reference's
+// BaselineSelfAttention.forward (benchmarks/torch_transformer_benchmark.py:97-117):
+// causal triu(1) mask (:99-103), key-padding mask (:105-108), fp32 softmax (:111),
+// probs @ v (:112).  Packing keeps token order inside a sequence, so the key-padding
+// mask is "key < valid length" and the causal mask compares packed positions.
+//
+// Work item = one (sequence, head, 256 query rows) = two 128-row query tiles.  The CTA
+// is persistent over the longest-first work list and runs 10 warps:
+//   warp 8      TMA: Q tiles (double-buffered across items), K/V tiles (STAGES ring)
+//   warp 9      one thread issues tcgen05.mma:  S_t = Q_t K_j^T  (M=128, N=128, K=hd)
+//               into TMEM, and O_t += P_t V_j with P_t read from TMEM (A operand)
+//   warps 0-3   softmax for query tile 0 (one thread = one query row = one TMEM lane)
+//   warps 4-7   softmax for query tile 1
+// While one softmax warpgroup works on its tile, the tensor core runs the other tile's
+// P V and next Q K^T, so MMA and softmax overlap.  A softmax thread loads its 128 scores
+// from TMEM, applies the masks, updates the running max (rescaling O in TMEM only when
+// the max grows by more than 2^8, lazily), writes P as packed fp16 back over the first
+// 64 columns of its S buffer, and signals the MMA warp.  At the end of an item it
+// normalises O by the row sum and stores the valid rows.
+//
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+hd) O1 [384,384+hd).
+// The ordering of tcgen05.mma operations issued by one thread guarantees that the
+// next S MMA into a buffer runs after the P V that read P from it.
+//
+// Every wait is bounded (TTTJ wait limit); on a timeout the role records
+// TTTJ_DEV_TIMEOUT_ATTN in the status word, raises the CTA abort flag and unwinds.
+//
+// Rows of other sequences inside a partial K/V tile are masked by P = 0; they are
+// finite whenever the inputs are finite (the workspace is zero-filled once and only
+// ever holds values computed from the inputs).
+#pragma once
+#include "common.cuh"
+#include "params.h"
+
+namespace tttj {
+
+template <int HD>
+struct AtcSmem {
+  static constexpr int Q_TILE = ATC_BM * HD * 2;
+  static constexpr int KV_TILE = ATC_BN * HD * 2;
+  static constexpr int STAGES = HD == 64 ? 3 : 4;
+  static constexpr int Q_BYTES = 2 * 2 * Q_TILE;  // 2 buffers x 2 tiles
+  static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
+  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 1;
+  static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + 1024;
+  static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O0 = 256, TMEM_O1 = 384;
+};
+
+struct AtcItem {
+  int b, h, seq0, len, q0;
+  int n[2];   // KV tiles streamed by query tile 0 / 1 (0 = tile empty)
+  int kv_end[2];
+  int n_kv;   // KV tiles loaded for the item
+};
+
+template <bool CAUSAL>
+__device__ __forceinline__ AtcItem atc_decode(const AtcParams& p, int it) {
+  AtcItem w;
+  const int2 e = p.items[it];
+  w.b = e.x;
+  w.h = e.y & 0xff;
+  w.q0 = (e.y >> 8) * ATC_ITEM_ROWS;
+  w.seq0 = p.seq_off[w.b];
+  w.len = p.seq_off[w.b + 1] - w.seq0;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int r0 = w.q0 + t * ATC_BM;
+    const int end = CAUSAL ? min(w.len, r0 + ATC_BM) : w.len;
+    w.kv_end[t] = end;
+    w.n[t] = (r0 < w.len) ? (end + ATC_BN - 1) / ATC_BN : 0;
+  }
+  w.n_kv = max(w.n[0], w.n[1]);
+  return w;
+}
+
+template <int HD>
+__device__ __forceinline__ uint64_t atc_desc_qk(uint32_t addr) {
+  return HD == 64 ? desc_kmajor_sw128(addr) : desc_kmajor_sw64(addr);
+}
+template <int HD>
+__device__ __forceinline__ uint64_t atc_desc_v(uint32_t addr) {
+  // V tile [128 keys][HD] is the B operand (K = keys, N = HD) stored N-contiguous.
+  return HD == 64 ? desc_mnmajor_sw128(addr, AtcSmem<HD>::KV_TILE, 1024)
+                  : desc_mnmajor_sw64(addr, AtcSmem<HD>::KV_TILE, 512);
+}
+
+template <int HD, bool CAUSAL>
+__global__ void __launch_bounds__(ATC_THREADS, 1)
+    attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const AtcParams p) {
+  using SM = AtcSmem<HD>;
+  constexpr int STAGES = SM::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t sQ = smem_u32(smem);
+  const uint32_t sKV = sQ + SM::Q_BYTES;
+  const uint32_t bar0 = sKV + SM::KV_BYTES;
+  const uint32_t bar_q_full = bar0;                     // [2]
+  const uint32_t bar_q_empty = bar0 + 16;               // [2]
+  const uint32_t bar_kv_full = bar0 + 32;               // [STAGES]
+  const uint32_t bar_kv_empty = bar_kv_full + 8 * STAGES;  // [STAGES]
+  const uint32_t bar_s_full = bar_kv_empty + 8 * STAGES;   // [2]
+  const uint32_t bar_p_full = bar_s_full + 16;             // [2]
+  const uint32_t bar_o_full = bar_p_full + 16;             // [2]
+  const uint32_t bar_o_free = bar_o_full + 16;             // [2]
+  const uint32_t bar_drain = bar_o_free + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint64_t limit = p.wait_limit_ns;
+  const int n_items = *p.item_count;
+  const int D = p.d_model;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQKV);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_q_full + 8 * i, 1);
+      mbar_init(bar_q_empty + 8 * i, 1);
+      mbar_init(bar_s_full + 8 * i, 1);
+      mbar_init(bar_p_full + 8 * i, ATC_BM);
+      mbar_init(bar_o_full + 8 * i, 1);
+      mbar_init(bar_o_free + 8 * i, ATC_BM);
+    }
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_kv_full + 8 * s, 1);
+      mbar_init(bar_kv_empty + 8 * s, 1);
+    }
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ TMA loader
+    if (lane == 0) {
+      bool ok = true;
+      long kvc = 0;  // KV tiles issued
+      int k = 0;     // items issued
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+        const AtcItem w = atc_decode<CAUSAL>(p, it);
+        const int qb = k & 1;
+        if (!mbar_wait(bar_q_empty + 8 * qb, ((k >> 1) & 1) ^ 1u, abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        const int nq = w.n[1] > 0 ? 2 : 1;
+        mbar_arrive_expect_tx(bar_q_full + 8 * qb, nq * SM::Q_TILE);
+        for (int t = 0; t < nq; ++t)
+          tma_load_2d(sQ + (qb * 2 + t) * SM::Q_TILE, &tmQKV, bar_q_full + 8 * qb, w.h * HD,
+                      w.seq0 + w.q0 + t * ATC_BM);
+        for (int j = 0; j < w.n_kv; ++j, ++kvc) {
+          const int st = (int)(kvc % STAGES);
+          if (!mbar_wait(bar_kv_empty + 8 * st, (uint32_t)((kvc / STAGES) & 1) ^ 1u, abort_flag,
+                         limit)) {
+            ok = false;
+            break;
+          }
+          const uint32_t dst = sKV + st * 2 * SM::KV_TILE;
+          mbar_arrive_expect_tx(bar_kv_full + 8 * st, 2 * SM::KV_TILE);
+          tma_load_2d(dst, &tmQKV, bar_kv_full + 8 * st, D + w.h * HD, w.seq0 + j * ATC_BN);
+          tma_load_2d(dst + SM::KV_TILE, &tmQKV, bar_kv_full + 8 * st, 2 * D + w.h * HD,
+                      w.seq0 + j * ATC_BN);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
+        // Let issued loads land before the CTA can exit.
+        for (long j = kvc > STAGES ? kvc - STAGES : 0; j < kvc; ++j)
+          mbar_wait(bar_kv_full + 8 * (int)(j % STAGES), (uint32_t)((j / STAGES) & 1), nullptr,
+                    limit);
+        for (int i = k > 2 ? k - 2 : 0; i < k; ++i)
+          mbar_wait(bar_q_full + 8 * (i & 1), (uint32_t)((i >> 1) & 1), nullptr, limit);
+      }
+    }
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16_f32(ATC_BM, ATC_BN);
+      constexpr uint32_t idesc_o = idesc_f16_f32(ATC_BM, HD, 0, 1);
+      constexpr uint32_t v_step = HD == 64 ? (2048u >> 4) : (1024u >> 4);  // 16 keys
+      bool ok = true;
+      bool issued = false;
+      long kvc = 0;             // KV tiles consumed
+      long pc[2] = {0, 0};      // p_full waits per tile
+      long oc[2] = {0, 0};      // o_free waits per tile
+      int k = 0;
+      auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+        if (!mbar_wait(bar, parity, abort_flag, limit)) {
+          ok = false;
+          return false;
+        }
+        tc_fence_after();
+        return true;
+      };
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+        const AtcItem w = atc_decode<CAUSAL>(p, it);
+        const int qb = k & 1;
+        if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
+        const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
+        const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
+        const uint32_t o_col[2] = {SM::TMEM_O0, SM::TMEM_O1};
+        long kv_waited = kvc - 1;  // highest KV tile index (global count) already waited on
+        auto ensure_kv = [&](long idx) -> bool {
+          while (kv_waited < idx) {
+            ++kv_waited;
+            if (!wait(bar_kv_full + 8 * (int)(kv_waited % STAGES),
+                      (uint32_t)((kv_waited / STAGES) & 1)))
+              return false;
+          }
+          return true;
+        };
+        auto issue_s = [&](int t, long kv_idx) {
+          const uint32_t kaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE;
+          const uint64_t qd = atc_desc_qk<HD>(qaddr[t]);
+          const uint64_t kd = atc_desc_qk<HD>(kaddr);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk)
+            mma_f16_ss(tmem + s_col[t], qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
+          mma_commit(bar_s_full + 8 * t);
+          issued = true;
+        };
+        auto issue_pv = [&](int t, long kv_idx, bool accumulate) {
+          const uint32_t vaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE + SM::KV_TILE;
+          const uint64_t vd = atc_desc_v<HD>(vaddr);
+#pragma unroll
+          for (int kk = 0; kk < ATC_BN / 16; ++kk)
+            mma_f16_ts(tmem + o_col[t], tmem + s_col[t] + (uint32_t)(kk * 8),
+                       vd + (uint64_t)(kk * v_step), idesc_o, (accumulate || kk > 0) ? 1u : 0u);
+          issued = true;
+        };
+        if (!ensure_kv(kvc)) break;
+        issue_s(0, kvc);
+        if (w.n[1] > 0) issue_s(1, kvc);
+        for (int j = 0; j < w.n_kv && ok; ++j) {
+          const long kv_j = kvc + j;
+          for (int t = 0; t < 2; ++t) {
+            if (j >= w.n[t]) continue;
+            if (!wait(bar_p_full + 8 * t, (uint32_t)(pc[t]++ & 1))) break;
+            if (j == 0 && !wait(bar_o_free + 8 * t, (uint32_t)(oc[t]++ & 1) ^ 1u)) break;
+            issue_pv(t, kv_j, j > 0);
+            if (j + 1 < w.n[t]) {
+              if (!ensure_kv(kv_j + 1)) break;
+              issue_s(t, kv_j + 1);
+            } else {
+              mma_commit(bar_o_full + 8 * t);
+            }
+          }
+          if (!ok) break;
+          mma_commit(bar_kv_empty + 8 * (int)(kv_j % STAGES));
+        }
+        kvc += w.n_kv;
+        if (ok) mma_commit(bar_q_empty + 8 * qb);
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
+        if (issued) {
+          mma_commit(bar_drain);
+          mbar_wait(bar_drain, 0, nullptr, limit);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ softmax, warps 0-7
+    const int t = warp >> 2;             // query tile of this warpgroup
+    const int quad = warp & 3;           // TMEM lane quadrant = rows 32*quad..
+    const int row = quad * 32 + lane;    // row inside the query tile
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    const uint32_t s_addr = tmem + lane_base + (t == 0 ? SM::TMEM_S0 : SM::TMEM_S1);
+    const uint32_t o_addr = tmem + lane_base + (t == 0 ? SM::TMEM_O0 : SM::TMEM_O1);
+    const float scale = p.scale_log2;
+    long sc = 0, ofc = 0;
+    bool ok = true;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const AtcItem w = atc_decode<CAUSAL>(p, it);
+      const int n = w.n[t];
+      if (n == 0) continue;
+      const int qrow = w.q0 + t * ATC_BM + row;  // query index inside the sequence
+      const int kv_end = w.kv_end[t];
+      float m_run = -INFINITY;  // running max (log2 domain) used as the exp base
+      float l_run = 0.f;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait(bar_s_full + 8 * t, (uint32_t)(sc++ & 1), abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint32_t sv[ATC_BN];  // raw fp32 scores of this thread's row
+#pragma unroll
+        for (int c = 0; c < ATC_BN / 32; ++c) {
+          uint32_t chunk[32];
+          tmem_ld_32x32b_x32(s_addr + (uint32_t)(c * 32), chunk);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) sv[c * 32 + e] = chunk[e];
+        }
+        tmem_wait_ld();
+        const int k0 = j * ATC_BN;
+        const bool need_mask =
+            (k0 + ATC_BN > kv_end) || (CAUSAL && k0 + ATC_BN - 1 > w.q0 + t * ATC_BM);
+        if (need_mask) {
+#pragma unroll
+          for (int c = 0; c < ATC_BN; ++c) {
+            const int key = k0 + c;
+            if (key >= kv_end || (CAUSAL && key > qrow)) sv[c] = __float_as_uint(-INFINITY);
+          }
+        }
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < ATC_BN; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+        const float m_tile = mx * scale;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (j == 0) {
+          m_run = m_tile;
+        } else {
+          // Lazy rescale: keep the old base unless the max grew by more than 2^8.
+          const bool grow = m_tile > m_run + 8.0f;
+          if (__any_sync(0xffffffff, grow)) {
+            const float m_new = fmaxf(m_run, m_tile);
+            alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);
+            m_run = m_new;
+            rescale = true;  // warp-uniform
+          }
+        }
+        const float base = (m_run == -INFINITY) ? 0.f : m_run;
+        float rs = 0.f;
+        // P as fp16 pairs over the first 64 columns of this tile's S buffer (the scores
+        // are already in registers), 16 columns (32 scores) per TMEM store.
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            const int i = q * 32 + 2 * c;
+            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), scale, -base));
+            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), scale, -base));
+            rs += p0 + p1;
+            pk[c] = pack_half2(p0, p1);
+          }
+          tmem_st_32x32b_x16(s_addr + (uint32_t)(q * 16), pk);
+        }
+        l_run = l_run * alpha + rs;
+        if (rescale) {
+          // O holds the previous tiles' P V (complete: the S MMA just waited on was
+          // issued after it).  Scale it in place, after the scores are consumed.
+#pragma unroll
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
+          }
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(bar_p_full + 8 * t);
+      }
+      if (!ok) break;
+      // Epilogue: O / l for the valid rows.
+      if (!mbar_wait(bar_o_full + 8 * t, (uint32_t)(ofc++ & 1), abort_flag, limit)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      __half* dst = p.ctx + (size_t)(w.seq0 + qrow) * D + w.h * HD;
+#pragma unroll
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
+        tmem_wait_ld();
+        if (qrow < w.len && w.seq0 + qrow < p.rows_max) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            d4[q] = make_uint4(pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                               pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                               pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                               pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar_o_free + 8 * t);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tttj

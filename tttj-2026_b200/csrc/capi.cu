@@ -93,7 +93,7 @@ struct WsLayout {
 };
 
 size_t attn_items_max(size_t B, size_t S, size_t H) {
-  return B * H * ((S + ATT_BM - 1) / ATT_BM);
+  return B * H * ((S + ATC_ITEM_ROWS - 1) / ATC_ITEM_ROWS);
 }
 
 // Token-plan part of the workspace (shared by the forward and tttj_attention).
@@ -177,6 +177,30 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// TMA map + parameters of the tcgen05 attention over a packed qkv buffer of
+// `qkv_rows` rows: boxes of head_dim columns x 128 rows, swizzle = the row width.
+int build_attention(CUtensorMap* tm, AtcParams* ap, int* grid, const void* qkv, void* ctx,
+                    int qkv_rows, int B, int S, int D, int H, const TokenPlan& tp, int* status,
+                    int num_sms) {
+  const int hd = D / H;
+  int rc = make_tmap_2d(tm, qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)qkv_rows,
+                        (uint64_t)(3 * D), (uint64_t)(3 * D), (uint32_t)hd, ATC_BM,
+                        hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+  if (rc) return rc;
+  ap->seq_off = tp.seq_off;
+  ap->items = tp.items;
+  ap->item_count = tp.item_count;
+  ap->ctx = static_cast<__half*>(ctx);
+  ap->rows_max = qkv_rows;
+  ap->d_model = D;
+  ap->scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
+  ap->status = status;
+  ap->wait_limit_ns = kWaitLimitNs;
+  const long items = (long)B * H * ((S + ATC_ITEM_ROWS - 1) / ATC_ITEM_ROWS);
+  *grid = (int)(items < num_sms ? items : num_sms);
+  return TTTJ_OK;
+}
+
 int sm_count(int device) {
   int n = 0;
   if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return 0;
@@ -258,7 +282,7 @@ int check_config(const tttj_config* c) {
   if (T * (long long)(c->ffn_dim > 3 * c->d_model ? c->ffn_dim : 3 * c->d_model) >= (1ll << 40) ||
       T >= (1ll << 31) - 256)
     return fail(TTTJ_ERR_INVALID, "batch_size*seq_len too large");
-  const long long plan_smem = 4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATT_BN - 1) / ATT_BN + 1);
+  const long long plan_smem = 4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATC_BN - 1) / ATC_BN + 1);
   if (plan_smem > 200 * 1024) return fail(TTTJ_ERR_INVALID, "batch_size/seq_len too large for the token plan");
   return TTTJ_OK;
 }
@@ -283,7 +307,8 @@ struct tttj_plan {
   __half *h, *qkv, *ctx, *hid;
   std::vector<LayerGemms> layers;
   const float *lnf_w, *lnf_b;
-  AttnParams attn;
+  CUtensorMap attn_tm;
+  AtcParams attn;
   int attn_grid;
   // Optional per-kernel-class timing (tttj_plan_enable_timing).
   bool timing = false;
@@ -436,16 +461,12 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
   p->lnf_b = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_B));
 
-  const int hd = D / cfg->num_heads;
-  p->attn.qkv = p->qkv;
-  p->attn.ctx = p->ctx;
-  p->attn.seq_off = p->tp.seq_off;
-  p->attn.items = p->tp.items;
-  p->attn.item_count = p->tp.item_count;
-  p->attn.d_model = D;
-  p->attn.causal = cfg->causal ? 1 : 0;
-  p->attn.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  p->attn_grid = (int)attn_items_max(B, S, cfg->num_heads);
+  rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S, D,
+                       cfg->num_heads, p->tp, p->status, p->num_sms);
+  if (rc) {
+    delete p;
+    return rc;
+  }
   *out_plan = p;
   return TTTJ_OK;
 }
@@ -545,7 +566,8 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     TTTJ_CUDA(tock());             \
   } while (0)
 
-  TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal, p->tp, s));
+  TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
+                                                  ATC_ITEM_ROWS, ATC_BN, p->tp, s));
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->layers[0].ln1_w,
                               p->layers[0].ln1_b, kLnEps, p->resid, p->h, s));
@@ -555,7 +577,8 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
       TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
                  ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln1_w, L.ln1_b, kLnEps, p->h, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
-    TTTJ_TIMED(TTTJ_KCLASS_ATTENTION, attention_launch(p->attn, hd, p->attn_grid, s));
+    TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
+               attention_tc_launch(p->attn_tm, p->attn, hd, c.causal, p->attn_grid, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
     TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
                ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln2_w, L.ln2_b, kLnEps, p->h, s));
@@ -614,11 +637,12 @@ size_t tttj_attention_workspace_bytes(int batch, int seq_len, int num_heads) {
   return plan_layout(batch, seq_len, num_heads, &w);
 }
 
-int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int batch, int seq_len,
-                   int d_model, int num_heads, int causal, void* workspace,
+int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* valid_mask, int batch,
+                   int seq_len, int d_model, int num_heads, int causal, void* workspace,
                    size_t workspace_bytes, void* stream) {
   if (!qkv || !ctx || !workspace) return fail(TTTJ_ERR_INVALID, "attention: null argument");
-  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads)
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads ||
+      qkv_rows <= 0)
     return fail(TTTJ_ERR_INVALID, "attention: bad shape");
   const int hd = d_model / num_heads;
   if (hd != 32 && hd != 64)
@@ -629,20 +653,20 @@ int tttj_attention(const void* qkv, void* ctx, const uint8_t* valid_mask, int ba
   const size_t need = plan_layout(batch, seq_len, num_heads, &w);
   if (workspace_bytes < need)
     return fail(TTTJ_ERR_INVALID, "attention: workspace too small: %zu < %zu", workspace_bytes, need);
+  int dev = 0;
+  TTTJ_CUDA(cudaGetDevice(&dev));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* base = static_cast<uint8_t*>(workspace);
   TokenPlan tp = token_plan_at(base, w);
-  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, tp, s));
-  AttnParams ap;
-  ap.qkv = static_cast<const __half*>(qkv);
-  ap.ctx = static_cast<__half*>(ctx);
-  ap.seq_off = tp.seq_off;
-  ap.items = tp.items;
-  ap.item_count = tp.item_count;
-  ap.d_model = d_model;
-  ap.causal = causal ? 1 : 0;
-  ap.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  TTTJ_CUDA(attention_launch(ap, hd, (int)attn_items_max(batch, seq_len, num_heads), s));
+  CUtensorMap tm;
+  AtcParams ap;
+  int grid = 0;
+  int rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, d_model,
+                           num_heads, tp, nullptr, sm_count(dev));
+  if (rc) return rc;
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, ATC_ITEM_ROWS,
+                               ATC_BN, tp, s));
+  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
   return TTTJ_OK;
 }
 
@@ -706,11 +730,12 @@ int noalloc_scratch_address(int device, void** out) {
 
 }  // namespace
 
-extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, const uint8_t* valid_mask,
-                                      int batch, int seq_len, int d_model, int num_heads,
-                                      int causal, void* stream) {
+extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows,
+                                      const uint8_t* valid_mask, int batch, int seq_len,
+                                      int d_model, int num_heads, int causal, void* stream) {
   if (!qkv || !ctx) return fail(TTTJ_ERR_INVALID, "attention_noalloc: null argument");
-  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads)
+  if (batch <= 0 || seq_len <= 0 || num_heads <= 0 || num_heads > 255 || d_model % num_heads ||
+      qkv_rows <= 0)
     return fail(TTTJ_ERR_INVALID, "attention_noalloc: bad shape");
   const int hd = d_model / num_heads;
   if (hd != 32 && hd != 64)
@@ -731,16 +756,14 @@ extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, const uint8_t*
   if (rc) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   TokenPlan tp = token_plan_at(static_cast<uint8_t*>(scratch), w);
-  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, tp, s));
-  AttnParams ap;
-  ap.qkv = static_cast<const __half*>(qkv);
-  ap.ctx = static_cast<__half*>(ctx);
-  ap.seq_off = tp.seq_off;
-  ap.items = tp.items;
-  ap.item_count = tp.item_count;
-  ap.d_model = d_model;
-  ap.causal = causal ? 1 : 0;
-  ap.scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
-  TTTJ_CUDA(attention_launch(ap, hd, (int)attn_items_max(batch, seq_len, num_heads), s));
+  CUtensorMap tm;
+  AtcParams ap;
+  int grid = 0;
+  rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, d_model, num_heads,
+                       tp, nullptr, sm_count(dev));
+  if (rc) return rc;
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, ATC_ITEM_ROWS,
+                               ATC_BN, tp, s));
+  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
   return TTTJ_OK;
 }

@@ -232,6 +232,27 @@ __device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_
       : "memory");
 }
 
+// 32 lanes x 32 bits, 32 consecutive columns, store registers to TMEM.
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// 2^x on the SFU (ex2.approx, flush-to-zero); 2^-inf = +0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ---------------------------------------------------------------------------
 // UMMA descriptors
 // ---------------------------------------------------------------------------
@@ -245,14 +266,30 @@ __device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t smem_addr) {
          ((uint64_t)(1024u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
-// Same for an MN-major operand (the MN dimension contiguous): 64-element MN rows of
-// 128 B, 8 K-rows per 1024-byte swizzle atom.  `lbo` is the byte distance between
-// atoms along MN, `sbo` between atoms along K.
+// K-major operand with 64-byte swizzle: rows of 32 fp16 (64 B), 8-row groups 512 B
+// apart, swizzle mode 4 (64 B).
+__device__ __forceinline__ uint64_t desc_kmajor_sw64(uint32_t smem_addr) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) |
+         ((uint64_t)(512u >> 4) << 32) | ((uint64_t)1u << 46) | ((uint64_t)4u << 61);
+}
+
+// MN-major operand (the MN dimension contiguous) with 128-byte swizzle: 64-element
+// MN rows of 128 B, 8 K-rows per 1024-byte atom.  `lbo` is the byte distance between
+// atoms along MN, `sbo` between 8-row groups along K.
 __device__ __forceinline__ uint64_t desc_mnmajor_sw128(uint32_t smem_addr, uint32_t lbo,
                                                        uint32_t sbo) {
   return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
          ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1u << 46) |
          ((uint64_t)2u << 61);
+}
+
+// MN-major operand with 64-byte swizzle: 32-element MN rows of 64 B, 8 K-rows per
+// 512-byte atom.
+__device__ __forceinline__ uint64_t desc_mnmajor_sw64(uint32_t smem_addr, uint32_t lbo,
+                                                      uint32_t sbo) {
+  return (uint64_t)((smem_addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | ((uint64_t)1u << 46) |
+         ((uint64_t)4u << 61);
 }
 
 // Instruction descriptor for kind::f16 with fp16 A and B, fp32 D, both operands

@@ -22,10 +22,13 @@ struct GemmLaunch {
 int gemm_choose_bn(int rows, int n, int num_sms);
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
-cudaError_t attention_launch(const AttnParams& p, int head_dim, int grid, cudaStream_t stream);
+// tcgen05 attention (256-query items, plan with q_block ATC_ITEM_ROWS, kv_block ATC_BN).
+// tmQKV: fp16 [rows, 3D] map, box {head_dim, 128}, swizzle 128 B (hd 64) / 64 B (hd 32).
+cudaError_t attention_tc_launch(const CUtensorMap& tmQKV, const AtcParams& p, int head_dim,
+                                int causal, int grid, cudaStream_t stream);
 
-cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal,
-                               const TokenPlan& plan, cudaStream_t stream);
+cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
+                               int kv_block, const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, const float* gamma, const float* beta, float eps,
                              float* resid, __half* out, cudaStream_t stream);

@@ -51,27 +51,13 @@ constexpr int GEMM_EPI_WARPS = 8;  // two per TMEM lane quadrant, each owning ha
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_STAGE_OUT_BYTES = 32 * 32 * 4;  // per-warp staging: 32 rows x 32 fp32
 
-struct AttnParams {
-  const __half* qkv;     // [rows, 3*D]: q | k | v, head h at columns h*hd
-  __half* ctx;           // [rows, D]
-  const int* seq_off;    // [B+1] first packed row of each sequence
-  const int2* items;     // work list: {b, (q_tile << 8) | h}
-  const int* item_count; // number of valid items
-  int d_model;
-  int causal;
-  float scale_log2;      // hd^-0.5 * log2(e)
-};
-
-constexpr int ATT_BM = 128;
-constexpr int ATT_BN = 64;
-constexpr int ATT_THREADS = 256;
 
 struct TokenPlan {
   int* seq_len;     // [B]
   int* seq_off;     // [B+1]; seq_off[B] = number of valid tokens
   int* packed_src;  // [B*S] packed row -> b*S + s
   int* dst_map;     // [B*S] b*S + s -> packed row, or -1
-  int2* items;      // [B*H*ceil(S/128)] attention work list
+  int2* items;      // [B*H*ceil(S/256)] attention work list
   int* item_count;  // [1]
 };
 

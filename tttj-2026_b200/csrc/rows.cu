@@ -10,16 +10,16 @@ constexpr int ROWS_PER_CTA = 8;  // one warp per row, 256 threads
 inline int ln_vpl(int D) { return (D + 255) / 256; }
 }  // namespace
 
-cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal,
-                               const TokenPlan& plan, cudaStream_t stream) {
-  const int nkeys = (S + ATT_BN - 1) / ATT_BN + 1;
+cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
+                               int kv_block, const TokenPlan& plan, cudaStream_t stream) {
+  const int nkeys = (S + kv_block - 1) / kv_block + 1;
   const size_t smem = sizeof(int) * (size_t)(2 * B + 1 + nkeys + 1);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(plan_tokens_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  plan_tokens_kernel<<<1, PLAN_THREADS, smem, stream>>>(mask, B, S, H, causal, ATT_BM, ATT_BN,
+  plan_tokens_kernel<<<1, PLAN_THREADS, smem, stream>>>(mask, B, S, H, causal, q_block, kv_block,
                                                         plan);
   return cudaGetLastError();
 }

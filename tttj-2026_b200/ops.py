@@ -90,7 +90,7 @@ def attention(qkv: torch.Tensor, valid_token_mask: Optional[torch.Tensor], batch
     mask = None
     if valid_token_mask is not None:
         mask = valid_token_mask.to(torch.bool).contiguous().view(torch.uint8)
-    rc = _lib.lib().tttj_attention(_ptr(qkv), _ptr(ctx), _ptr(mask), batch, seq_len, D, num_heads,
+    rc = _lib.lib().tttj_attention(_ptr(qkv), _ptr(ctx), qkv.shape[0], _ptr(mask), batch, seq_len, D, num_heads,
                                    1 if causal else 0, _ptr(workspace), workspace.numel(),
                                    _stream(qkv.device))
     _lib.check(rc, "attention")

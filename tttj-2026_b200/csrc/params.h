@@ -51,6 +51,22 @@ constexpr int GEMM_EPI_WARPS = 8;  // two per TMEM lane quadrant, each owning ha
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_STAGE_OUT_BYTES = 32 * 32 * 4;  // per-warp staging: 32 rows x 32 fp32
 
+// tcgen05 attention: work items of 2 query tiles x 128 rows, 128-key KV tiles.
+struct AtcParams {
+  const int* seq_off;     // [B+1] first packed row of each sequence
+  const int2* items;      // work list: {b, (query pair << 8) | h}
+  const int* item_count;  // number of valid items
+  __half* ctx;            // [rows_max, D]
+  int rows_max;           // rows allocated in qkv / ctx (stores past it are dropped)
+  int d_model;
+  float scale_log2;       // hd^-0.5 * log2(e)
+  int* status;            // device status word (nullable)
+  unsigned long long wait_limit_ns;
+};
+constexpr int ATC_BM = 128;         // query rows per tile = TMEM lanes
+constexpr int ATC_BN = 128;         // keys per KV tile
+constexpr int ATC_ITEM_ROWS = 256;  // two query tiles per work item
+constexpr int ATC_THREADS = 320;    // warps 0-3 / 4-7 softmax tile 0 / 1, warp 8 TMA, warp 9 MMA
 
 struct TokenPlan {
   int* seq_len;     // [B]

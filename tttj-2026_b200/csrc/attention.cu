@@ -12,8 +12,7 @@ cudaError_t launch_tc(const CUtensorMap& tm, const AtcParams& p, int grid, cudaS
   static_assert(smem <= 232448, "attention shared memory exceeds the 227 KB per-CTA limit");
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, ATC_THREADS, smem, stream>>>(tm, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(ATC_THREADS), smem, stream, tm, p);
 }
 }  // namespace
 

@@ -114,7 +114,6 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const int warp = warp_id();
   const int lane = lane_id();
   const uint64_t limit = p.wait_limit_ns;
-  const int n_items = *p.item_count;
   const int D = p.d_model;
 
   if (threadIdx.x == 0) {
@@ -144,6 +143,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  griddep_wait();
+  griddep_launch();
+  const int n_items = *p.item_count;
 
   if (warp == 8) {
     // ------------------------------------------------------------ TMA loader

@@ -36,6 +36,20 @@ __device__ __forceinline__ bool elect_one() {
   return pred != 0;
 }
 
+// Programmatic dependent launch.  Kernels of the forward are launched with
+// programmatic stream serialization: a kernel may start while its predecessor in the
+// stream is still running, so it does only private set-up (shared memory, barriers,
+// TMEM, descriptor prefetch) before griddep_wait(), which returns once every earlier
+// kernel of the stream has completed and its memory is visible.  griddep_launch()
+// then lets the next kernel begin its own set-up.  Both are no-ops for a kernel
+// launched without the attribute.
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Record the first error code seen by any CTA of any kernel sharing `status`.
 __device__ __forceinline__ void report_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);

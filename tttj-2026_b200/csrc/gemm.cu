@@ -16,8 +16,7 @@ cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the 227 KB per-CTA limit");
-  kern<<<g.grid, GEMM_THREADS, smem, stream>>>(g.tmA, g.tmB, g.tmC, g.p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(g.grid), dim3(GEMM_THREADS), smem, stream, g.tmA, g.tmB, g.tmC, g.p);
 }
 
 template <int BN, int STAGES>

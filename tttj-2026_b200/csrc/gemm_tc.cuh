@@ -61,10 +61,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int warp = warp_id();
   const int lane = lane_id();
 
-  const int rows = p.rows_dev ? min(*p.rows_dev, p.rows_max) : p.rows_max;
-  const int m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
   const int n_tiles = p.n / BN + ((p.n % BN) ? 1 : 0);
-  const int num_tiles = m_tiles * n_tiles;
   const int k_iters = p.k / GEMM_BK;
   const uint64_t limit = p.wait_limit_ns;
 
@@ -93,6 +90,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  griddep_wait();
+  griddep_launch();
+  const int rows = p.rows_dev ? min(*p.rows_dev, p.rows_max) : p.rows_max;
+  const int m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
+  const int num_tiles = m_tiles * n_tiles;
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------

@@ -19,9 +19,8 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  plan_tokens_kernel<<<1, PLAN_THREADS, smem, stream>>>(mask, B, S, H, causal, q_block, kv_block,
-                                                        plan);
-  return cudaGetLastError();
+  return launch_pdl(plan_tokens_kernel, dim3(1), dim3(PLAN_THREADS), smem, stream, mask, B, S, H,
+                    causal, q_block, kv_block, plan);
 }
 
 #define TTTJ_VPL_DISPATCH(VPL_EXPR, CALL) \
@@ -40,16 +39,17 @@ cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, 
                              float* resid, __half* out, cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
   if (x_dtype == 0) {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_gather_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, __half>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
                                       static_cast<const __half*>(x), packed_src, rows_dev, D, gamma,
                                       beta, eps, resid, out)));
   } else {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_gather_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, float>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
                                       static_cast<const float*>(x), packed_src, rows_dev, D, gamma,
                                       beta, eps, resid, out)));
   }
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,
@@ -57,16 +57,17 @@ cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, in
                            cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
   if (in_dtype == 0) {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_rows_kernel<V, __half>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
                                       static_cast<const __half*>(in), rows_dev, rows_max, D, gamma,
                                       beta, eps, out)));
   } else {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (ln_rows_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_rows_kernel<V, float>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
                                       static_cast<const float*>(in), rows_dev, rows_max, D, gamma,
                                       beta, eps, out)));
   }
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
@@ -74,16 +75,19 @@ cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, 
                             int out_dtype, cudaStream_t stream) {
   const int grid = (tokens + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
+  cudaError_t e = cudaSuccess;
   if (out_dtype == 0) {
     TTTJ_VPL_DISPATCH(ln_vpl(D),
-                      (ln_final_scatter_kernel<V, __half><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
-                          resid, dst_map, tokens, D, gamma, beta, eps, static_cast<__half*>(out))));
+                      (e = launch_pdl(ln_final_scatter_kernel<V, __half>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0,
+                                     stream, resid, dst_map, tokens, D, gamma, beta, eps,
+                                     static_cast<__half*>(out))));
   } else {
     TTTJ_VPL_DISPATCH(ln_vpl(D),
-                      (ln_final_scatter_kernel<V, float><<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(
-                          resid, dst_map, tokens, D, gamma, beta, eps, static_cast<float*>(out))));
+                      (e = launch_pdl(ln_final_scatter_kernel<V, float>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0,
+                                     stream, resid, dst_map, tokens, D, gamma, beta, eps,
+                                     static_cast<float*>(out))));
   }
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream) {

@@ -25,6 +25,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
                                                                    int B, int S, int H, int causal,
                                                                    int q_block, int kv_block,
                                                                    TokenPlan plan) {
+  griddep_wait();
+  griddep_launch();
   extern __shared__ int sh[];
   int* cnt = sh;             // [B]
   int* off = sh + B;         // [B+1]
@@ -202,6 +204,8 @@ __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ 
                                                         const int* __restrict__ rows_dev, int D,
                                                         const float* gamma, const float* beta,
                                                         float eps, float* resid, __half* out) {
+  griddep_wait();
+  griddep_launch();
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (row >= *rows_dev) return;
   const int src = packed_src[row];
@@ -230,6 +234,8 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const TIn* __restrict__ in
                                                       int rows_max, int D, const float* gamma,
                                                       const float* beta, float eps,
                                                       __half* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   const int rows = rows_dev ? min(*rows_dev, rows_max) : rows_max;
   if (row >= rows) return;
@@ -256,6 +262,8 @@ __global__ void __launch_bounds__(256) ln_final_scatter_kernel(const float* __re
                                                                const float* gamma,
                                                                const float* beta, float eps,
                                                                TOut* __restrict__ out) {
+  griddep_wait();
+  griddep_launch();
   const int tok = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (tok >= tokens) return;
   const int lane = lane_id();

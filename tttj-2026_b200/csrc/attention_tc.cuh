@@ -45,7 +45,8 @@ struct AtcSmem {
   static constexpr int Q_BYTES = 2 * 2 * Q_TILE;  // 2 buffers x 2 tiles
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
   static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 1;
-  static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + 1024;
+  static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
+  static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + 1024;
   static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O0 = 256, TMEM_O1 = 384;
 };
 
@@ -55,6 +56,7 @@ struct AtcItem {
   int kv_end[2];
   int n_kv;   // KV tiles loaded for the item
 };
+static_assert(sizeof(AtcItem) <= 64, "item info slot is 64 bytes");
 
 template <bool CAUSAL>
 __device__ __forceinline__ AtcItem atc_decode(const AtcParams& p, int it) {
@@ -110,6 +112,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const uint32_t bar_drain = bar_o_free + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // Decoded work item per Q buffer, written by the loader before it arms q_full, read
+  // by the MMA and softmax warps after they waited on q_full (one global decode per item).
+  AtcItem* info = reinterpret_cast<AtcItem*>(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8 + 16);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -120,7 +125,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     tma_prefetch_desc(&tmQKV);
     for (int i = 0; i < 2; ++i) {
       mbar_init(bar_q_full + 8 * i, 1);
-      mbar_init(bar_q_empty + 8 * i, 1);
+      // Released by the MMA warp's commit after the item's last Q K^T and by every
+      // softmax thread once it copied the item's decoded info out of the slot.
+      mbar_init(bar_q_empty + 8 * i, 1 + 2 * ATC_BM);
       mbar_init(bar_s_full + 8 * i, 1);
       mbar_init(bar_p_full + 8 * i, ATC_BM);
       mbar_init(bar_o_full + 8 * i, 1);
@@ -162,6 +169,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           break;
         }
         const int nq = w.n[1] > 0 ? 2 : 1;
+        info[qb] = w;  // published by the release of the arrive below
         mbar_arrive_expect_tx(bar_q_full + 8 * qb, nq * SM::Q_TILE);
         for (int t = 0; t < nq; ++t)
           tma_load_2d(sQ + (qb * 2 + t) * SM::Q_TILE, &tmQKV, bar_q_full + 8 * qb, w.h * HD,
@@ -212,9 +220,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         return true;
       };
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
-        const AtcItem w = atc_decode<CAUSAL>(p, it);
         const int qb = k & 1;
         if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
+        const AtcItem w = info[qb];
         const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
         const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
         const uint32_t o_col[2] = {SM::TMEM_O0, SM::TMEM_O1};
@@ -291,8 +299,15 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     const float scale = p.scale_log2;
     long sc = 0, ofc = 0;
     bool ok = true;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-      const AtcItem w = atc_decode<CAUSAL>(p, it);
+    int k = 0;
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+      const int qb = k & 1;
+      if (!mbar_wait(bar_q_full + 8 * qb, (uint32_t)((k >> 1) & 1), abort_flag, limit)) {
+        ok = false;
+        break;
+      }
+      const AtcItem w = info[qb];
+      mbar_arrive(bar_q_empty + 8 * qb);  // this thread no longer needs the info slot
       const int n = w.n[t];
       if (n == 0) continue;
       const int qrow = w.q0 + t * ATC_BM + row;  // query index inside the sequence
@@ -318,15 +333,20 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         const bool need_mask =
             (k0 + ATC_BN > kv_end) || (CAUSAL && k0 + ATC_BN - 1 > w.q0 + t * ATC_BM);
         if (need_mask) {
+          // Column c of this tile is masked when c > lim (key >= kv_end, or key > query).
+          const int lim = (CAUSAL ? min(kv_end - 1, qrow) : kv_end - 1) - k0;
 #pragma unroll
-          for (int c = 0; c < ATC_BN; ++c) {
-            const int key = k0 + c;
-            if (key >= kv_end || (CAUSAL && key > qrow)) sv[c] = __float_as_uint(-INFINITY);
-          }
+          for (int c = 0; c < ATC_BN; ++c)
+            if (c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
-        float mx = -INFINITY;
+        // Row max with 8 independent partial maxima (short dependency chains).
+        float pm[8];
 #pragma unroll
-        for (int c = 0; c < ATC_BN; ++c) mx = fmaxf(mx, __uint_as_float(sv[c]));
+        for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sv[i]);
+#pragma unroll
+        for (int c = 8; c < ATC_BN; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sv[c]));
+        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
         const float m_tile = mx * scale;
         float alpha = 1.f;
         bool rescale = false;
@@ -343,7 +363,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           }
         }
         const float base = (m_run == -INFINITY) ? 0.f : m_run;
-        float rs = 0.f;
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial row sums
         // P as fp16 pairs over the first 64 columns of this tile's S buffer (the scores
         // are already in registers), 16 columns (32 scores) per TMEM store.
 #pragma unroll
@@ -354,11 +374,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             const int i = q * 32 + 2 * c;
             const float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), scale, -base));
             const float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), scale, -base));
-            rs += p0 + p1;
+            ps[c & 3] += p0 + p1;
             pk[c] = pack_half2(p0, p1);
           }
           tmem_st_32x32b_x16(s_addr + (uint32_t)(q * 16), pk);
         }
+        const float rs = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         l_run = l_run * alpha + rs;
         if (rescale) {
           // O holds the previous tiles' P V (complete: the S MMA just waited on was

@@ -107,3 +107,15 @@ def test_other_batch_shapes_and_no_device_error():
     torch.cuda.synchronize()
     assert torch.equal(full[3:9], part)
     assert opt.device_status() == 0
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_multi_device_matches_single_device():
+    cfg, model, x, mask = _case("C3")
+    single = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        ref = single(x, mask)
+        multi = tb.MultiDeviceTransformer(model, [0, 1])
+        out = multi(x, mask)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)

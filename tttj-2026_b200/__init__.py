@@ -9,15 +9,20 @@ Public surface:
   * TransformerConfig, TransformerParameters (weights container with the reference
     organizer model's module tree)
   * ops: per-kernel wrappers (linear, layernorm, attention)
+  * sharding: batch data parallelism (LPT shards, one process per GPU or one
+    process driving several GPUs)
 """
 from __future__ import annotations
 
-from . import _lib, ops
+from . import _lib, ops, sharding
 from .model import B200Transformer, pack_weights, validate_model_config
+from .sharding import MultiDeviceTransformer, distributed_forward
 from .spec import TransformerConfig, TransformerParameters, generate_inputs, make_parameter_model
 
 __all__ = [
     "B200Transformer",
+    "MultiDeviceTransformer",
+    "distributed_forward",
     "TransformerConfig",
     "TransformerParameters",
     "generate_inputs",
@@ -25,6 +30,7 @@ __all__ = [
     "make_parameter_model",
     "ops",
     "pack_weights",
+    "sharding",
     "validate_model_config",
 ]
 

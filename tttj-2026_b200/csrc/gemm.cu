@@ -6,6 +6,7 @@ namespace tttj {
 
 namespace {
 
+constexpr int STAGES_BN64 = 8;   // 8 x 24 KB ring (+32 KB output staging)
 constexpr int STAGES_BN128 = 6;  // 6 x 32 KB ring (+32 KB output staging)
 constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring (+32 KB output staging)
 
@@ -38,21 +39,23 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 int gemm_choose_bn(int rows, int n, int num_sms) {
+  // The widest column tile whose tile count still fills >= 90% of the SMs: wider
+  // tiles re-read A less and amortise the epilogue over a longer MMA, but a tile count
+  // below the SM count leaves SMs idle.  (Measured on B200 over the projection shapes
+  // of the BASELINE configurations: BN 256 wins every large GEMM by up to 1.4x over
+  // BN 128; the narrow tiles win only when 256-wide tiles cannot fill the machine.)
   const long m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
-  auto cost = [&](int bn) {
-    const long tiles = m_tiles * ((n + bn - 1) / bn);
-    const long waves = (tiles + num_sms - 1) / num_sms;
-    // A tile's time grows with its width plus a fixed per-tile overhead (prologue,
-    // epilogue drain), modelled as 32 columns.
-    return waves * (bn + 32);
-  };
-  if (n % 256 != 0) return 128;
-  return cost(256) <= cost(128) ? 256 : 128;
+  const long need = (long)num_sms * 9 / 10;
+  for (int bn : {256, 128}) {
+    if (n % bn == 0 && m_tiles * (n / bn) >= need) return bn;
+  }
+  return 64;
 }
 
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream) {
   if (g.bn == 256) return launch_bn<256, STAGES_BN256>(g, stream);
   if (g.bn == 128) return launch_bn<128, STAGES_BN128>(g, stream);
+  if (g.bn == 64) return launch_bn<64, STAGES_BN64>(g, stream);
   return cudaErrorInvalidValue;
 }
 

@@ -448,6 +448,8 @@ def main(argv=None) -> int:
     if args.impl == "reference":
         return run_reference(args, rank, world)
     if world > 1:
+        # Keep rank 0's stdout to the one JSON line (no NCCL version banner).
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         import torch
         import torch.distributed as dist
 

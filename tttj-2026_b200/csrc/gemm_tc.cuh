@@ -210,26 +210,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
       const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      // fp32 residual of the next chunk, loaded one chunk ahead so its latency hides
-      // behind the TMEM load and the math of the current chunk.
-      float4 res_next[8];
-      auto load_res = [&](int c) {
-        const int col = n_blk * BN + c * 32;
-        if (EPI == EPI_BIAS_RESIDUAL_F32 && row_ok && col < p.n) {
-          const float4* rs = reinterpret_cast<const float4*>(
-              static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col);
-#pragma unroll
-          for (int q = 0; q < 8; ++q) res_next[q] = rs[q];
-        }
-      };
-      load_res(col_half * (BN / 64));
 #pragma unroll 1
       for (int cc = 0; cc < BN / 64; ++cc) {
         const int c = col_half * (BN / 64) + cc;
-        float4 res_cur[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) res_cur[q] = res_next[q];
-        if (cc + 1 < BN / 64) load_res(c + 1);
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
         tmem_wait_ld();
@@ -251,12 +234,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (row_ok) {
           if (EPI == EPI_BIAS_RESIDUAL_F32) {
+            const float4* rs = reinterpret_cast<const float4*>(
+                static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              v[4 * q + 0] += res_cur[q].x;
-              v[4 * q + 1] += res_cur[q].y;
-              v[4 * q + 2] += res_cur[q].z;
-              v[4 * q + 3] += res_cur[q].w;
+              const float4 rv = rs[q];
+              v[4 * q + 0] += rv.x;
+              v[4 * q + 1] += rv.y;
+              v[4 * q + 2] += rv.z;
+              v[4 * q + 3] += rv.w;
             }
           } else if (EPI == EPI_BIAS_RESIDUAL) {
             const uint4* rs = reinterpret_cast<const uint4*>(

@@ -88,14 +88,18 @@ int tttj_weight_offset(const tttj_config* cfg, int layer, int field, size_t* off
                        size_t* bytes);
 
 /* Device workspace the forward needs (activations of the packed valid tokens,
- * token plan, device status word).  It must be zero-filled once before the first
+ * LayerNorm statistics, the LayerNorm-folded QKV / ffn_in weights, token plan, device
+ * status word).  It must be zero-filled once before the first
  * forward (the plan never reads a byte the same call did not write, except rows of
  * earlier calls, which stay finite). */
 size_t tttj_workspace_bytes(const tttj_config* cfg);
 
 /* A plan binds a configuration to one device, one packed weight buffer and one
- * workspace (all owned by the caller), and pre-builds every TMA descriptor.
- * Replaces SequenceResidentTransformer.prepare (kernels/sequence_resident.py:143-150). */
+ * workspace (all owned by the caller), and pre-builds every TMA descriptor.  It also
+ * folds each block's LayerNorm affine into a copy of the QKV / ffn_in weights kept in
+ * the workspace (one-time kernels on the legacy default stream, which it synchronises;
+ * the weight buffer must be complete when it is called).  Replaces
+ * SequenceResidentTransformer.prepare (kernels/sequence_resident.py:143-150). */
 typedef struct tttj_plan tttj_plan;
 int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
                      size_t workspace_bytes, tttj_plan** out_plan);

@@ -88,9 +88,35 @@ bool weight_offset(const tttj_config& c, int layer, int field, size_t* off, size
 // ---------------------------------------------------------------- workspace layout
 struct WsLayout {
   size_t seq_len, seq_off, packed_src, dst_map, items, item_count, status;
-  size_t resid, h, qkv, ctx, hid;
+  size_t resid, x16, qkv, ctx, hid, stats;
+  size_t fold;        // LayerNorm-folded QKV / ffn_in weights, per layer
+  size_t fold_layer;  // bytes per layer in the fold region
   size_t total;
 };
+
+// Per-layer fold region: Wqkv' [3D, D] fp16, W1' [F, D] fp16, then fp32 vectors
+// bqkv' [3D], colsum_qkv [3D], b1' [F], colsum_1 [F].
+struct FoldLayout {
+  size_t wqkv, w1, bqkv, cqkv, b1, c1, total;
+};
+// Statistics partials per row produced by a residual GEMM (N = d_model): two column
+// halves per column tile.  The tile width is the widest dividing d_model (the same
+// rule the residual GEMMs use when they fill the machine; 64 always divides).
+int stats_parts(const tttj_config& c) { return 2 * (c.d_model / 64); }  // upper bound
+
+FoldLayout fold_layout(const tttj_config& c) {
+  const size_t D = c.d_model, F = c.ffn_dim;
+  FoldLayout f{};
+  size_t o = 0;
+  f.wqkv = o; o += align_up(3 * D * D * 2);
+  f.w1 = o; o += align_up(F * D * 2);
+  f.bqkv = o; o += align_up(3 * D * 4);
+  f.cqkv = o; o += align_up(3 * D * 4);
+  f.b1 = o; o += align_up(F * 4);
+  f.c1 = o; o += align_up(F * 4);
+  f.total = o;
+  return f;
+}
 
 size_t attn_items_max(size_t B, size_t S, size_t H) {
   return B * H * ((S + ATC_ITEM_ROWS - 1) / ATC_ITEM_ROWS);
@@ -115,10 +141,13 @@ WsLayout ws_layout(const tttj_config& c) {
   const size_t T = (size_t)c.batch_size * c.seq_len, D = c.d_model, F = c.ffn_dim;
   size_t o = plan_layout(c.batch_size, c.seq_len, c.num_heads, &w);
   w.resid = o; o += align_up(T * D * 4);
-  w.h = o; o += align_up(T * D * 2);
+  w.x16 = o; o += align_up(T * D * 2);
   w.qkv = o; o += align_up(T * 3 * D * 2);
   w.ctx = o; o += align_up(T * D * 2);
   w.hid = o; o += align_up(T * F * 2);
+  w.stats = o; o += align_up((size_t)2 * T * stats_parts(c) * 8);
+  w.fold_layer = fold_layout(c).total;
+  w.fold = o; o += (size_t)c.num_layers * w.fold_layer;
   w.total = o;
   return w;
 }
@@ -213,10 +242,11 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   if (n <= 0 || k <= 0 || rows < 0) return fail(TTTJ_ERR_INVALID, "linear: bad sizes");
   if (n % 32 != 0) return fail(TTTJ_ERR_INVALID, "linear: n=%d must be a multiple of 32", n);
   if (k % 64 != 0) return fail(TTTJ_ERR_INVALID, "linear: k=%d must be a multiple of 64", k);
-  const bool has_res = epi == EPI_BIAS_RESIDUAL || epi == EPI_BIAS_RESIDUAL_F32;
+  const bool has_res = epi == EPI_BIAS_RESIDUAL || epi == EPI_BIAS_RESIDUAL_F32 ||
+                       epi == EPI_RESIDUAL_F32_STATS;
   if (lda % 8 || ldw % 8 || ldo % 8 || (has_res && ldr % 8))
     return fail(TTTJ_ERR_INVALID, "linear: row strides must be multiples of 8 elements");
-  if (epi < EPI_BIAS || epi > EPI_BIAS_RESIDUAL_F32)
+  if (epi < EPI_BIAS || epi > EPI_LN_FOLD_GELU)
     return fail(TTTJ_ERR_INVALID, "linear: unknown epilogue %d", epi);
   if (has_res && residual == nullptr)
     return fail(TTTJ_ERR_INVALID, "linear: residual epilogue needs a residual");
@@ -239,7 +269,7 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   if (rc) return rc;
   // Output: 32x32 boxes; fp32 rows of the box are 128 B (128-byte swizzle), fp16 rows
   // 64 B (64-byte swizzle), matching the epilogue's staging layout.
-  if (epi == EPI_BIAS_RESIDUAL_F32)
+  if (epi == EPI_BIAS_RESIDUAL_F32 || epi == EPI_RESIDUAL_F32_STATS)
     rc = make_tmap_2d(&g->tmC, out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)(rows > 0 ? rows : 1),
                       (uint64_t)n, (uint64_t)ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_128B);
   else
@@ -304,7 +334,9 @@ struct tttj_plan {
   TokenPlan tp;
   int* status;
   float* resid;  // fp32 residual stream
-  __half *h, *qkv, *ctx, *hid;
+  __half *x16, *qkv, *ctx, *hid;  // x16: fp16 copy of the residual stream (GEMM A operand)
+  float2* stats;  // [2][T][parts] LayerNorm statistics partials: LN1 (next QKV), LN2 (ffn_in)
+  int parts;
   std::vector<LayerGemms> layers;
   const float *lnf_w, *lnf_b;
   CUtensorMap attn_tm;
@@ -333,7 +365,7 @@ struct DeviceGuard {
 };
 }  // namespace
 
-int launches_per_forward(const tttj_config& c) { return 7 * c.num_layers + 2; }
+int launches_per_forward(const tttj_config& c) { return 5 * c.num_layers + 3; }
 
 // Fold the events of the previous timed forward into the per-class totals.
 int collect_timing(tttj_plan* p) {
@@ -418,7 +450,8 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   p->tp = token_plan_at(p->ws, lay);
   p->status = reinterpret_cast<int*>(p->ws + lay.status);
   p->resid = reinterpret_cast<float*>(p->ws + lay.resid);
-  p->h = reinterpret_cast<__half*>(p->ws + lay.h);
+  p->x16 = reinterpret_cast<__half*>(p->ws + lay.x16);
+  p->stats = reinterpret_cast<float2*>(p->ws + lay.stats);
   p->qkv = reinterpret_cast<__half*>(p->ws + lay.qkv);
   p->ctx = reinterpret_cast<__half*>(p->ws + lay.ctx);
   p->hid = reinterpret_cast<__half*>(p->ws + lay.hid);
@@ -426,36 +459,90 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   const int B = cfg->batch_size, S = cfg->seq_len, D = cfg->d_model, F = cfg->ffn_dim;
   const int T = B * S;
   const int* rows_dev = p->tp.seq_off + B;  // number of valid tokens
+  // Statistics partials actually produced: two column halves per column tile of the
+  // residual GEMMs (N = d_model), whose tile width is fixed by (T, d_model).
+  p->parts = 2 * (D / gemm_choose_bn(T, D, p->num_sms));
   auto W = [&](int layer, int field) -> const uint8_t* {
     size_t off = 0, bytes = 0;
     weight_offset(*cfg, layer, field, &off, &bytes);
     return p->weights + off;
   };
   p->layers.resize(cfg->num_layers);
+  const FoldLayout fl = fold_layout(*cfg);
   for (int l = 0; l < cfg->num_layers; ++l) {
     LayerGemms& L = p->layers[l];
     L.ln1_w = reinterpret_cast<const float*>(W(l, TTTJ_LN1_W));
     L.ln1_b = reinterpret_cast<const float*>(W(l, TTTJ_LN1_B));
     L.ln2_w = reinterpret_cast<const float*>(W(l, TTTJ_LN2_W));
     L.ln2_b = reinterpret_cast<const float*>(W(l, TTTJ_LN2_B));
-    rc = build_gemm(&L.qkv, p->h, D, W(l, TTTJ_W_QKV), D,
-                    reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)), p->qkv, 3 * D, nullptr, 0, T,
-                    rows_dev, 3 * D, D, EPI_BIAS, p->status, p->num_sms);
+    // LayerNorm folds: LN1 into the QKV weights, LN2 into ffn_in (one-time kernels).
+    uint8_t* fb = p->ws + lay.fold + (size_t)l * lay.fold_layer;
+    __half* wqkv_f = reinterpret_cast<__half*>(fb + fl.wqkv);
+    __half* w1_f = reinterpret_cast<__half*>(fb + fl.w1);
+    float* bqkv_f = reinterpret_cast<float*>(fb + fl.bqkv);
+    float* cqkv = reinterpret_cast<float*>(fb + fl.cqkv);
+    float* b1_f = reinterpret_cast<float*>(fb + fl.b1);
+    float* c1 = reinterpret_cast<float*>(fb + fl.c1);
+    cudaError_t fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_QKV)),
+                                    reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)), L.ln1_w,
+                                    L.ln1_b, 3 * D, D, wqkv_f, bqkv_f, cqkv, 0);
+    if (fe == cudaSuccess)
+      fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_FFN_IN)),
+                          reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), L.ln2_w, L.ln2_b, F,
+                          D, w1_f, b1_f, c1, 0);
+    if (fe != cudaSuccess) {
+      delete p;
+      return cuda_fail(fe, "fold_ln_launch");
+    }
+    // Two statistics buffers, reused by every layer: ffn_out(l-1) / the gather write
+    // LN1 for qkv(l); out_proj(l) writes LN2 for ffn_in(l).
+    float2* st_ln1 = p->stats;
+    float2* st_ln2 = p->stats + (size_t)T * p->parts;
+    rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * D, nullptr, 0, T, rows_dev,
+                    3 * D, D, EPI_LN_FOLD, p->status, p->num_sms);
+    L.qkv.p.stats_in = st_ln1;
+    L.qkv.p.stats_parts = p->parts;
+    L.qkv.p.colsum = cqkv;
+    L.qkv.p.ln_eps = kLnEps;
     if (!rc)
       rc = build_gemm(&L.out, p->ctx, D, W(l, TTTJ_W_OUT), D,
                       reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
-                      T, rows_dev, D, D, EPI_BIAS_RESIDUAL_F32, p->status, p->num_sms);
+                      T, rows_dev, D, D, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
+    L.out.p.out16 = p->x16;
+    L.out.p.ld16 = D;
+    L.out.p.stats_out = st_ln2;
+    L.out.p.stats_parts = p->parts;
     if (!rc)
-      rc = build_gemm(&L.ffn_in, p->h, D, W(l, TTTJ_W_FFN_IN), D,
-                      reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), p->hid, F, nullptr, 0,
-                      T, rows_dev, F, D, EPI_BIAS_GELU, p->status, p->num_sms);
+      rc = build_gemm(&L.ffn_in, p->x16, D, w1_f, D, b1_f, p->hid, F, nullptr, 0, T, rows_dev, F,
+                      D, EPI_LN_FOLD_GELU, p->status, p->num_sms);
+    L.ffn_in.p.stats_in = st_ln2;
+    L.ffn_in.p.stats_parts = p->parts;
+    L.ffn_in.p.colsum = c1;
+    L.ffn_in.p.ln_eps = kLnEps;
+    const bool last = l + 1 == cfg->num_layers;
     if (!rc)
       rc = build_gemm(&L.ffn_out, p->hid, F, W(l, TTTJ_W_FFN_OUT), F,
                       reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D, p->resid,
-                      D, T, rows_dev, D, F, EPI_BIAS_RESIDUAL_F32, p->status, p->num_sms);
+                      D, T, rows_dev, D, F, last ? EPI_BIAS_RESIDUAL_F32 : EPI_RESIDUAL_F32_STATS,
+                      p->status, p->num_sms);
+    if (!rc && (L.out.bn != 2 * D / p->parts || L.ffn_out.bn != 2 * D / p->parts))
+      rc = fail(TTTJ_ERR_INVALID, "internal: residual GEMM tile width mismatch");
+    if (!last) {
+      L.ffn_out.p.out16 = p->x16;
+      L.ffn_out.p.ld16 = D;
+      L.ffn_out.p.stats_out = st_ln1;  // LN1 of layer l+1
+      L.ffn_out.p.stats_parts = p->parts;
+    }
     if (rc) {
       delete p;
       return rc;
+    }
+  }
+  {
+    cudaError_t fe = cudaStreamSynchronize(0);  // folded weights ready before any forward
+    if (fe != cudaSuccess) {
+      delete p;
+      return cuda_fail(fe, "cudaStreamSynchronize(fold)");
     }
   }
   p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
@@ -569,19 +656,16 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
   TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
                                                   ATC_ITEM_ROWS, ATC_BN, p->tp, s));
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
-             ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->layers[0].ln1_w,
-                              p->layers[0].ln1_b, kLnEps, p->resid, p->h, s));
+             ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
+                              p->stats, p->parts, s));
   for (int l = 0; l < c.num_layers; ++l) {
+    // Every LayerNorm is folded into the GEMM that consumes it; the statistics come
+    // from the gather (layer 0) or the preceding residual epilogue.
     const LayerGemms& L = p->layers[l];
-    if (l > 0)
-      TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
-                 ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln1_w, L.ln1_b, kLnEps, p->h, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
                attention_tc_launch(p->attn_tm, p->attn, hd, c.causal, p->attn_grid, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
-    TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
-               ln_rows_launch(p->resid, 1, rows_dev, T, D, L.ln2_w, L.ln2_b, kLnEps, p->h, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));
   }
@@ -609,6 +693,8 @@ int tttj_linear(const void* a, int lda, const void* w, int ldw, const float* bia
                 int ldo, const void* residual, int ldr, int rows, const int* rows_dev, int n, int k,
                 int epilogue, int* status_dev, void* stream) {
   if (!a || !w || !bias || !out) return fail(TTTJ_ERR_INVALID, "linear: null argument");
+  if (epilogue < TTTJ_EPI_BIAS || epilogue > TTTJ_EPI_BIAS_RESIDUAL_F32)
+    return fail(TTTJ_ERR_INVALID, "linear: unknown epilogue %d", epilogue);
   if (rows == 0) return TTTJ_OK;
   GemmLaunch g;
   int rc = build_gemm(&g, a, lda, w, ldw, bias, out, ldo, residual, ldr, rows, rows_dev, n, k,

@@ -31,6 +31,12 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
       return launch_t<BN, EPI_BIAS_RESIDUAL, STAGES>(g, stream);
     case EPI_BIAS_RESIDUAL_F32:
       return launch_t<BN, EPI_BIAS_RESIDUAL_F32, STAGES>(g, stream);
+    case EPI_RESIDUAL_F32_STATS:
+      return launch_t<BN, EPI_RESIDUAL_F32_STATS, STAGES>(g, stream);
+    case EPI_LN_FOLD:
+      return launch_t<BN, EPI_LN_FOLD, STAGES>(g, stream);
+    case EPI_LN_FOLD_GELU:
+      return launch_t<BN, EPI_LN_FOLD_GELU, STAGES>(g, stream);
     default:
       return cudaErrorInvalidValue;
   }

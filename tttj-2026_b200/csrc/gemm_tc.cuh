@@ -189,7 +189,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else {
     // ---------------- epilogue: warps 2..9 ----------------
-    constexpr bool OUT_F32 = EPI == EPI_BIAS_RESIDUAL_F32;
+    constexpr bool RES_F32 = EPI == EPI_BIAS_RESIDUAL_F32 || EPI == EPI_RESIDUAL_F32_STATS;
+    constexpr bool OUT_F32 = RES_F32;
+    constexpr bool FOLD = EPI == EPI_LN_FOLD || EPI == EPI_LN_FOLD_GELU;
     const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
     const int col_half = (warp - 2) >> 2;       // which half of the tile's columns
     const int row_in_tile = quad * 32 + lane;
@@ -207,6 +209,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       tc_fence_after();
       const int row = m_blk * GEMM_BM + row_in_tile;
       const bool row_ok = row < rows;
+      float ln_mean = 0.f, ln_rstd = 0.f;
+      if (FOLD && row_ok) {
+        float ssum = 0.f, ssq = 0.f;
+        const float2* st = p.stats_in + (size_t)row * p.stats_parts;
+        for (int j = 0; j < p.stats_parts; ++j) {  // fixed order: deterministic
+          const float2 v2 = st[j];
+          ssum += v2.x;
+          ssq += v2.y;
+        }
+        const float inv_k = 1.0f / (float)p.k;
+        ln_mean = ssum * inv_k;
+        const float var = fmaxf(ssq * inv_k - ln_mean * ln_mean, 0.f);
+        ln_rstd = rsqrtf(var + p.ln_eps);
+      }
+      float row_sum = 0.f, row_sq = 0.f;  // EPI_RESIDUAL_F32_STATS
       // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
       const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
@@ -220,20 +237,34 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (col0 >= p.n) continue;  // warp-uniform
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
         float v[32];
+        if (FOLD) {
+          const float4* c4 = reinterpret_cast<const float4*>(p.colsum + col0);
+          const float nm = -ln_mean;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const float4 bb = __ldg(b4 + q);
-          v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
-          v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
-          v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
-          v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            const float4 cs = __ldg(c4 + q);
+            v[4 * q + 0] = fmaf(fmaf(nm, cs.x, __uint_as_float(r[4 * q + 0])), ln_rstd, bb.x);
+            v[4 * q + 1] = fmaf(fmaf(nm, cs.y, __uint_as_float(r[4 * q + 1])), ln_rstd, bb.y);
+            v[4 * q + 2] = fmaf(fmaf(nm, cs.z, __uint_as_float(r[4 * q + 2])), ln_rstd, bb.z);
+            v[4 * q + 3] = fmaf(fmaf(nm, cs.w, __uint_as_float(r[4 * q + 3])), ln_rstd, bb.w);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 bb = __ldg(b4 + q);
+            v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+          }
         }
-        if (EPI == EPI_BIAS_GELU) {
+        if (EPI == EPI_BIAS_GELU || EPI == EPI_LN_FOLD_GELU) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
         }
         if (row_ok) {
-          if (EPI == EPI_BIAS_RESIDUAL_F32) {
+          if (RES_F32) {
             const float4* rs = reinterpret_cast<const float4*>(
                 static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
 #pragma unroll
@@ -259,6 +290,24 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               }
             }
           }
+        }
+        if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
+          float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            s4[i & 3] += v[i];
+            q4[i & 3] = fmaf(v[i], v[i], q4[i & 3]);
+          }
+          row_sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+          row_sq += (q4[0] + q4[1]) + (q4[2] + q4[3]);
+          // fp16 copy of the new residual: the next (LayerNorm-folded) GEMM's A operand.
+          uint4* d16 = reinterpret_cast<uint4*>(p.out16 + (size_t)row * p.ld16 + col0);
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            d16[q] = make_uint4(pack_half2(v[8 * q + 0], v[8 * q + 1]),
+                                pack_half2(v[8 * q + 2], v[8 * q + 3]),
+                                pack_half2(v[8 * q + 4], v[8 * q + 5]),
+                                pack_half2(v[8 * q + 6], v[8 * q + 7]));
         }
         if (full_tile) {
           // The previous TMA store from this warp's staging block must have read it.
@@ -319,6 +368,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_arrive(bar_acce + 8 * acc);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      if (EPI == EPI_RESIDUAL_F32_STATS && row_ok)
+        p.stats_out[(size_t)row * p.stats_parts + 2 * n_blk + col_half] =
+            make_float2(row_sum, row_sq);
     }
     // Stores issued by this warp must complete before the CTA exits.
     if (lane == 0) bulk_wait_all();

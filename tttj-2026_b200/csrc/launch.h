@@ -49,8 +49,11 @@ cudaError_t attention_tc_launch(const CUtensorMap& tmQKV, const AtcParams& p, in
 cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
                                int kv_block, const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
-                             int rows_max, int D, const float* gamma, const float* beta, float eps,
-                             float* resid, __half* out, cudaStream_t stream);
+                             int rows_max, int D, float* resid, __half* x16, float2* stats,
+                             int n_parts, cudaStream_t stream);
+cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,
+                           int rows, int k, __half* w_out, float* b_out, float* colsum,
+                           cudaStream_t stream);
 // in_dtype: 0 = fp16 rows, 1 = fp32 rows.
 cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,
                            const float* gamma, const float* beta, float eps, __half* out,

@@ -29,6 +29,14 @@ enum GemmEpilogue : int {
   EPI_BIAS_GELU = 1,      // out = fp16(gelu_erf(acc + bias))
   EPI_BIAS_RESIDUAL = 2,  // out = fp16(residual + acc + bias), out may alias residual
   EPI_BIAS_RESIDUAL_F32 = 3,  // fp32 out = fp32 residual + acc + bias (the residual stream)
+  // EPI_BIAS_RESIDUAL_F32 that also writes out16 = fp16(out) and adds each row's
+  // (sum, sum of squares) of out into stats_out[row] (the next LayerNorm's statistics).
+  EPI_RESIDUAL_F32_STATS = 4,
+  // LayerNorm folded into the GEMM: A = fp16 x, W = W * gamma (per K column), and
+  // out = fp16(rstd * (acc - mean * colsum[n]) + bias[n]) with mean/rstd of each row
+  // from stats_in[row] = (sum, sum of squares) over K, bias = b + W beta.
+  EPI_LN_FOLD = 5,
+  EPI_LN_FOLD_GELU = 6,  // the same followed by exact erf-GELU
 };
 
 struct GemmParams {
@@ -43,6 +51,15 @@ struct GemmParams {
   int ldr;
   int* status;          // device status word (nullable)
   unsigned long long wait_limit_ns;
+  // EPI_RESIDUAL_F32_STATS
+  __half* out16;        // [rows, ld16] fp16 copy of out
+  int ld16;
+  float2* stats_out;    // [rows][stats_parts] (sum, sum of squares) partials
+  // EPI_LN_FOLD*
+  const float2* stats_in;  // [rows][stats_parts] partials of the LayerNorm input rows
+  int stats_parts;
+  const float* colsum;     // [n] sum over K of the folded weight row
+  float ln_eps;
 };
 
 constexpr int GEMM_BM = 128;

@@ -35,21 +35,33 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
   }
 
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
-                             int rows_max, int D, const float* gamma, const float* beta, float eps,
-                             float* resid, __half* out, cudaStream_t stream) {
+                             int rows_max, int D, float* resid, __half* x16, float2* stats,
+                             int n_parts, cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
   if (x_dtype == 0) {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, __half>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
-                                      static_cast<const __half*>(x), packed_src, rows_dev, D, gamma,
-                                      beta, eps, resid, out)));
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, __half>, dim3(grid),
+                                                 dim3(32 * ROWS_PER_CTA), 0, stream,
+                                                 static_cast<const __half*>(x), packed_src,
+                                                 rows_dev, D, resid, x16, stats, n_parts)));
   } else {
-    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, float>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0, stream,
-                                      static_cast<const float*>(x), packed_src, rows_dev, D, gamma,
-                                      beta, eps, resid, out)));
+    TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, float>, dim3(grid),
+                                                 dim3(32 * ROWS_PER_CTA), 0, stream,
+                                                 static_cast<const float*>(x), packed_src,
+                                                 rows_dev, D, resid, x16, stats, n_parts)));
   }
   return e;
+}
+
+cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,
+                           int rows, int k, __half* w_out, float* b_out, float* colsum,
+                           cudaStream_t stream) {
+  const int grid = (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+  if (grid == 0) return cudaSuccess;
+  fold_ln_kernel<<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(w, b, gamma, beta, rows, k, w_out, b_out,
+                                                          colsum);
+  return cudaGetLastError();
 }
 
 cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,

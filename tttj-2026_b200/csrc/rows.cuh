@@ -9,8 +9,10 @@
 // * layernorm rows: nn.LayerNorm(d_model) (benchmarks/torch_transformer_benchmark.py:128,
 //   130, 160): biased variance, eps 1e-5, fp32 statistics, affine.
 //   - ln_gather_kernel: reads the caller's x (fp16 or fp32) at the packed rows,
-//     writes the fp32 residual stream and LN1 of layer 0.
-//   - ln_rows_kernel: LN of the packed residual stream (fp32) or of any fp16 rows.
+//     writes the fp32 residual stream, its fp16 copy and layer 0's LN1 statistics.
+//     Every other LayerNorm of the stack is folded into the GEMM that consumes it
+//     (fold_ln_kernel prepares the weights once per plan).
+//   - ln_rows_kernel: LN of fp16 rows (the per-kernel layernorm entry point).
 //   - ln_final_scatter_kernel: final LayerNorm + masked_fill(~mask, 0)
 //     (torch_transformer_benchmark.py:168-171), written back to [B, S, D] in the
 //     caller's dtype.
@@ -196,35 +198,80 @@ __device__ __forceinline__ void ln_normalise(float (&x)[VPL][8], int D, const fl
   }
 }
 
-// Layer-0 entry: gather the caller's rows into the packed fp32 residual stream and
-// write LN1 of them (fp16, the next GEMM's operand).
+// Layer-0 entry: gather the caller's rows into the packed fp32 residual stream, write
+// its fp16 copy (A operand of the LayerNorm-folded QKV GEMM) and the row's
+// (sum, sum of squares) as partial 0 of the row's n_parts statistics partials
+// (the others zero).
 template <int VPL, typename TIn>
 __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ x,
                                                         const int* __restrict__ packed_src,
                                                         const int* __restrict__ rows_dev, int D,
-                                                        const float* gamma, const float* beta,
-                                                        float eps, float* resid, __half* out) {
+                                                        float* resid, __half* x16, float2* stats,
+                                                        int n_parts) {
   griddep_wait();
   griddep_launch();
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (row >= *rows_dev) return;
   const int src = packed_src[row];
   const int lane = lane_id();
-  float v[VPL][8];
+  float sum = 0.f, sq = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = (lane + 32 * i) * 8;
     if (c < D) {
-      load8<TIn>(x + (size_t)src * D + c, v[i]);
-      // The residual stream is kept in fp32 between blocks.
-      store8(resid + (size_t)row * D + c, v[i]);
+      float v[8];
+      load8<TIn>(x + (size_t)src * D + c, v);
+      store8(resid + (size_t)row * D + c, v);
+      store8(x16 + (size_t)row * D + c, v);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        sum += v[e];
+        sq = fmaf(v[e], v[e], sq);
+      }
     }
   }
-  ln_normalise<VPL>(v, D, gamma, beta, eps);
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffff, sum, o);
+    sq += __shfl_xor_sync(0xffffffff, sq, o);
+  }
+  for (int j = lane; j < n_parts; j += 32)
+    stats[(size_t)row * n_parts + j] = j == 0 ? make_float2(sum, sq) : make_float2(0.f, 0.f);
+}
+
+// One-time LayerNorm fold of a weight matrix W [rows, k] (fp16) consumed by
+// LayerNorm(x) @ W^T + b:  W' = W * gamma (per column k, fp16), colsum[r] = sum_k W'[r, k]
+// (of the fp16 values), b'[r] = b[r] + sum_k W[r, k] * beta[k].  One warp per row.
+__global__ void __launch_bounds__(256) fold_ln_kernel(const __half* __restrict__ w,
+                                                      const float* __restrict__ b,
+                                                      const float* __restrict__ gamma,
+                                                      const float* __restrict__ beta, int rows,
+                                                      int k, __half* __restrict__ w_out,
+                                                      float* __restrict__ b_out,
+                                                      float* __restrict__ colsum) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
+  if (row >= rows) return;
+  const int lane = lane_id();
+  double cs = 0.0, bb = 0.0;
+  for (int c = lane * 8; c < k; c += 256) {
+    float wv[8], g[8], be[8], wf[8];
+    load8<__half>(w + (size_t)row * k + c, wv);
+    load8<float>(gamma + c, g);
+    load8<float>(beta + c, be);
 #pragma unroll
-  for (int i = 0; i < VPL; ++i) {
-    const int c = (lane + 32 * i) * 8;
-    if (c < D) store8(out + (size_t)row * D + c, v[i]);
+    for (int e = 0; e < 8; ++e) {
+      wf[e] = __half2float(__float2half_rn(wv[e] * g[e]));
+      cs += (double)wf[e];
+      bb += (double)wv[e] * (double)be[e];
+    }
+    store8(w_out + (size_t)row * k + c, wf);
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    cs += __shfl_xor_sync(0xffffffff, cs, o);
+    bb += __shfl_xor_sync(0xffffffff, bb, o);
+  }
+  if (lane == 0) {
+    colsum[row] = (float)cs;
+    b_out[row] = (float)((double)b[row] + bb);
   }
 }
 

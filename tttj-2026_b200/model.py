@@ -93,6 +93,9 @@ class _Plan:
             _lib.check(L.tttj_validate_config(ctypes.byref(self.c)), "plan")
         # Zero-filled once: rows a call does not write stay finite for later calls.
         self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
+        # Plan creation runs one-time weight-folding kernels on the legacy default
+        # stream; the packed weights and the workspace must be complete first.
+        torch.cuda.synchronize(device)
         handle = ctypes.c_void_p()
         _lib.check(
             L.tttj_plan_create(ctypes.byref(self.c), device.index, ctypes.c_void_p(weights.data_ptr()),

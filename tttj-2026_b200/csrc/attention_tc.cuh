@@ -54,7 +54,7 @@ struct AtcItem {
   int b, h, seq0, len, q0;
   int n[2];   // KV tiles streamed by query tile 0 / 1 (0 = tile empty)
   int kv_end[2];
-  int n_kv;   // KV tiles loaded for the item
+  int n_kv;   // KV tiles loaded for the item; -1 marks "no more items"
 };
 static_assert(sizeof(AtcItem) <= 64, "item info slot is 64 bytes");
 
@@ -160,16 +160,30 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     if (lane == 0) {
       bool ok = true;
       long kvc = 0;  // KV tiles issued
-      int k = 0;     // items issued
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
-        const AtcItem w = atc_decode<CAUSAL>(p, it);
+      int k = 0;     // items issued (including the final "no more items" marker)
+      for (;; ++k) {
+        // Dynamic scheduling: the next item of the longest-first list goes to the
+        // first CTA that asks for it.
+        const int it = atomicAdd(p.work_counter, 1);
+        const bool stop = it >= n_items;
+        AtcItem w;
+        if (!stop) {
+          w = atc_decode<CAUSAL>(p, it);
+        } else {
+          w.n_kv = -1;
+          w.n[0] = w.n[1] = 0;
+        }
         const int qb = k & 1;
         if (!mbar_wait(bar_q_empty + 8 * qb, ((k >> 1) & 1) ^ 1u, abort_flag, limit)) {
           ok = false;
           break;
         }
-        const int nq = w.n[1] > 0 ? 2 : 1;
         info[qb] = w;  // published by the release of the arrive below
+        if (stop) {
+          mbar_arrive(bar_q_full + 8 * qb);
+          break;
+        }
+        const int nq = w.n[1] > 0 ? 2 : 1;
         mbar_arrive_expect_tx(bar_q_full + 8 * qb, nq * SM::Q_TILE);
         for (int t = 0; t < nq; ++t)
           tma_load_2d(sQ + (qb * 2 + t) * SM::Q_TILE, &tmQKV, bar_q_full + 8 * qb, w.h * HD,
@@ -187,6 +201,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           tma_load_2d(dst + SM::KV_TILE, &tmQKV, bar_kv_full + 8 * st, 2 * D + w.h * HD,
                       w.seq0 + j * ATC_BN);
         }
+        if (!ok) break;
       }
       if (!ok) {
         *abort_flag = 1;
@@ -219,10 +234,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         tc_fence_after();
         return true;
       };
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+      for (; ok; ++k) {
         const int qb = k & 1;
         if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
         const AtcItem w = info[qb];
+        if (w.n_kv < 0) break;  // no more items
         const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
         const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
         const uint32_t o_col[2] = {SM::TMEM_O0, SM::TMEM_O1};
@@ -300,13 +316,14 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     long sc = 0, ofc = 0;
     bool ok = true;
     int k = 0;
-    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x, ++k) {
+    for (; ok; ++k) {
       const int qb = k & 1;
       if (!mbar_wait(bar_q_full + 8 * qb, (uint32_t)((k >> 1) & 1), abort_flag, limit)) {
         ok = false;
         break;
       }
       const AtcItem w = info[qb];
+      if (w.n_kv < 0) break;  // no more items
       mbar_arrive(bar_q_empty + 8 * qb);  // this thread no longer needs the info slot
       const int n = w.n[t];
       if (n == 0) continue;

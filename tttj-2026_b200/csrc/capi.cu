@@ -87,7 +87,7 @@ bool weight_offset(const tttj_config& c, int layer, int field, size_t* off, size
 
 // ---------------------------------------------------------------- workspace layout
 struct WsLayout {
-  size_t seq_len, seq_off, packed_src, dst_map, items, item_count, status;
+  size_t seq_len, seq_off, packed_src, dst_map, items, item_count, counters, status;
   size_t resid, x16, qkv, ctx, hid, stats;
   size_t fold;        // LayerNorm-folded QKV / ffn_in weights, per layer
   size_t fold_layer;  // bytes per layer in the fold region
@@ -132,6 +132,7 @@ size_t plan_layout(size_t B, size_t S, size_t H, WsLayout* w) {
   w->dst_map = o; o += align_up(T * 4);
   w->items = o; o += align_up(attn_items_max(B, S, H) * 8);
   w->item_count = o; o += align_up(4);
+  w->counters = o; o += align_up(4 * PLAN_COUNTERS);
   w->status = o; o += align_up(4);
   return o;
 }
@@ -160,6 +161,7 @@ TokenPlan token_plan_at(uint8_t* base, const WsLayout& w) {
   tp.dst_map = reinterpret_cast<int*>(base + w.dst_map);
   tp.items = reinterpret_cast<int2*>(base + w.items);
   tp.item_count = reinterpret_cast<int*>(base + w.item_count);
+  tp.counters = reinterpret_cast<int*>(base + w.counters);
   return tp;
 }
 
@@ -219,6 +221,7 @@ int build_attention(CUtensorMap* tm, AtcParams* ap, int* grid, const void* qkv, 
   ap->seq_off = tp.seq_off;
   ap->items = tp.items;
   ap->item_count = tp.item_count;
+  ap->work_counter = tp.counters;  // the forward points layer l at counters[l]
   ap->ctx = static_cast<__half*>(ctx);
   ap->rows_max = qkv_rows;
   ap->d_model = D;
@@ -308,6 +311,8 @@ int check_config(const tttj_config* c) {
                 c->d_model, c->ffn_dim);
   if (c->d_model > 2048) return fail(TTTJ_ERR_INVALID, "d_model=%d exceeds 2048", c->d_model);
   if (c->num_heads > 255) return fail(TTTJ_ERR_INVALID, "num_heads=%d exceeds 255", c->num_heads);
+  if (c->num_layers > PLAN_COUNTERS)
+    return fail(TTTJ_ERR_INVALID, "num_layers=%d exceeds %d", c->num_layers, PLAN_COUNTERS);
   const long long T = (long long)c->batch_size * c->seq_len;
   if (T * (long long)(c->ffn_dim > 3 * c->d_model ? c->ffn_dim : 3 * c->d_model) >= (1ll << 40) ||
       T >= (1ll << 31) - 256)
@@ -663,8 +668,10 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     // from the gather (layer 0) or the preceding residual epilogue.
     const LayerGemms& L = p->layers[l];
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
+    AtcParams ap = p->attn;
+    ap.work_counter = p->tp.counters + l;
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
-               attention_tc_launch(p->attn_tm, p->attn, hd, c.causal, p->attn_grid, s));
+               attention_tc_launch(p->attn_tm, ap, hd, c.causal, p->attn_grid, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));

@@ -73,6 +73,7 @@ struct AtcParams {
   const int* seq_off;     // [B+1] first packed row of each sequence
   const int2* items;      // work list: {b, (query pair << 8) | h}
   const int* item_count;  // number of valid items
+  int* work_counter;      // zeroed before the launch; CTAs take items with atomicAdd
   __half* ctx;            // [rows_max, D]
   int rows_max;           // rows allocated in qkv / ctx (stores past it are dropped)
   int d_model;
@@ -92,7 +93,10 @@ struct TokenPlan {
   int* dst_map;     // [B*S] b*S + s -> packed row, or -1
   int2* items;      // [B*H*ceil(S/256)] attention work list
   int* item_count;  // [1]
+  int* counters;    // [PLAN_COUNTERS] dynamic work counters, zeroed by the plan kernel
 };
+
+constexpr int PLAN_COUNTERS = 256;  // one per attention launch of a forward (layers)
 
 constexpr int PLAN_THREADS = 1024;
 

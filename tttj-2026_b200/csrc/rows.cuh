@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
   const int nwarps = blockDim.x >> 5;
 
   for (int i = threadIdx.x; i <= nkeys; i += blockDim.x) hist[i] = 0;
+  for (int i = threadIdx.x; i < PLAN_COUNTERS; i += blockDim.x) plan.counters[i] = 0;
   for (int b = warp; b < B; b += nwarps) {
     int c = 0;
     if (mask == nullptr) {

@@ -44,6 +44,24 @@ def test_linear_matches_torch(M, N, K, epilogue):
         _close(out, ref, atol=2e-3, rtol=2e-3)
 
 
+def test_gelu_epilogue_accuracy_over_a_dense_range():
+    """Drive the GELU epilogue through an identity GEMM: every pre-activation in
+    [-12, 12] (step ~1e-3) must come out as fp16(GELU(x)) up to fp16 rounding,
+    comparing with torch's exact-erf GELU in fp32."""
+    N = 256
+    vals = torch.linspace(-12, 12, 128 * 100 * N // 4, device=DEV)
+    M = vals.numel() // N
+    x = vals[: M * N].view(M, N).half()
+    eye = torch.eye(N, device=DEV).half()
+    zero = torch.zeros(N, device=DEV)
+    out = ops.linear(x, eye, zero, epilogue="gelu")
+    torch.cuda.synchronize()
+    ref = torch.nn.functional.gelu(x.float())
+    err = (out.float() - ref).abs()
+    ulp = torch.clamp(ref.abs(), min=2.0**-14) * 2.0**-10  # one fp16 ulp (or subnormal step)
+    assert bool((err <= 0.5 * ulp + 1e-6).all()), float((err / ulp).max())
+
+
 def test_linear_residual_in_place_and_device_row_count():
     M, N, K = 640, 512, 256
     g = torch.Generator(device=DEV).manual_seed(3)

@@ -147,6 +147,13 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Hint: bring `bytes` (a multiple of 16, 16-byte aligned address) of global memory into
+// L2.  No completion tracking; a later ordinary load of the range finds it in L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gptr, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(gptr)),
+               "r"(bytes)
+               : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA, commit, loads

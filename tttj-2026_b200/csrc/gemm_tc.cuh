@@ -198,17 +198,68 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const uint32_t stage_out = sOut + (uint32_t)((warp - 2) * GEMM_STAGE_OUT_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // This warp's columns of a tile are one contiguous run of BN/2: chunks
+    // col_half*(BN/64) .. +BN/64-1 of 32 columns each.
+    constexpr int CHUNKS = BN / 64;
+    // Residual reads are the epilogue's long-latency operand.  Each warp asks L2 for
+    // its rows' segment of the NEXT tile while the current one is drained, loads the
+    // first chunk of the current tile before the accumulator is ready, and loads chunk
+    // c + 1 as soon as chunk c's values are consumed.
+    auto prefetch_residual = [&](int t) {
+      if (!(RES_F32 || EPI == EPI_BIAS_RESIDUAL) || t >= num_tiles) return;
+      const int mb = t / n_tiles;
+      const int c0 = (t - mb * n_tiles) * BN + col_half * (BN / 2);
+      const int r = mb * GEMM_BM + row_in_tile;
+      const int esize = RES_F32 ? 4 : 2;
+      const uint32_t bytes = (uint32_t)(min(BN / 2, p.n - c0) * esize) & ~15u;
+      if (r < rows && c0 < p.n && bytes > 0)
+        bulk_prefetch_l2(static_cast<const uint8_t*>(p.residual) +
+                             ((size_t)r * p.ldr + c0) * esize, bytes);
+    };
+    // Residual of the chunk being drained, in one of two register layouts.  Full tiles
+    // of the fp32 epilogues use the "coalesced" one: element q of lane l is row
+    // 4q + l/8 of the warp's 32 rows, columns 4(l%8)..+3, so each load instruction
+    // reads four whole 128-byte row segments; the values reach their row's lane through
+    // the staging block.  Otherwise lane l holds row l's 32 columns ("by row").
+    float4 rc[8];
+    auto load_res = [&](bool coalesced, int row0, int row, int col0) {
+      if (RES_F32 && coalesced) {
+        const float* base = static_cast<const float*>(p.residual) +
+                            (size_t)(row0 + (lane >> 3)) * p.ldr + col0 + 4 * (lane & 7);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          rc[q] = *reinterpret_cast<const float4*>(base + (size_t)(4 * q) * p.ldr);
+      } else if (RES_F32) {
+        const float4* rs = reinterpret_cast<const float4*>(
+            static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) rc[q] = rs[q];
+      } else if (EPI == EPI_BIAS_RESIDUAL) {
+        const uint4* rs = reinterpret_cast<const uint4*>(
+            static_cast<const __half*>(p.residual) + (size_t)row * p.ldr + col0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 x = rs[q];
+          const float2 a = unpack_half2(x.x), b = unpack_half2(x.y);
+          const float2 c = unpack_half2(x.z), d = unpack_half2(x.w);
+          rc[2 * q] = make_float4(a.x, a.y, b.x, b.y);
+          rc[2 * q + 1] = make_float4(c.x, c.y, d.x, d.y);
+        }
+      }
+    };
+    prefetch_residual(blockIdx.x);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int m_blk = tile / n_tiles;
       const int n_blk = tile - m_blk * n_tiles;
-      if (!mbar_wait(bar_accf + 8 * acc, acc_phase, abort_flag, limit)) {
-        *abort_flag = 1;
-        report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);
-        break;
-      }
-      tc_fence_after();
-      const int row = m_blk * GEMM_BM + row_in_tile;
+      prefetch_residual(tile + (int)gridDim.x);
+      const int row0 = m_blk * GEMM_BM + quad * 32;  // first of this warp's 32 rows
+      const int row = row0 + lane;
       const bool row_ok = row < rows;
+      // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
+      const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
+      const bool staged_res = RES_F32 && full_tile;
+      // Everything that does not depend on the accumulator is fetched before waiting
+      // for it: the LayerNorm statistics of this row and the first residual chunk.
       float ln_mean = 0.f, ln_rstd = 0.f;
       if (FOLD && row_ok) {
         float ssum = 0.f, ssq = 0.f;
@@ -223,73 +274,136 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const float var = fmaxf(ssq * inv_k - ln_mean * ln_mean, 0.f);
         ln_rstd = rsqrtf(var + p.ln_eps);
       }
+      const int seg0 = n_blk * BN + col_half * (BN / 2);
+      if (seg0 < p.n && (staged_res || row_ok)) load_res(staged_res, row0, row, seg0);
+      if (!mbar_wait(bar_accf + 8 * acc, acc_phase, abort_flag, limit)) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);
+        break;
+      }
+      tc_fence_after();
       float row_sum = 0.f, row_sq = 0.f;  // EPI_RESIDUAL_F32_STATS
-      // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
-      const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int cc = 0; cc < BN / 64; ++cc) {
-        const int c = col_half * (BN / 64) + cc;
+      for (int cc = 0; cc < CHUNKS; ++cc) {
+        const int c = col_half * CHUNKS + cc;
+        const int col0 = n_blk * BN + c * 32;
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);
-        tmem_wait_ld();
-        const int col0 = n_blk * BN + c * 32;
-        if (col0 >= p.n) continue;  // warp-uniform
+        if (col0 >= p.n) {  // warp-uniform
+          tmem_wait_ld();
+          continue;
+        }
+        // Per-column operands, loaded while the TMEM read is in flight.
+        float4 bb[8], cs[8];
         const float4* b4 = reinterpret_cast<const float4*>(p.bias + col0);
-        float v[32];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) bb[q] = __ldg(b4 + q);
         if (FOLD) {
           const float4* c4 = reinterpret_cast<const float4*>(p.colsum + col0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) cs[q] = __ldg(c4 + q);
+        }
+        tmem_wait_ld();
+        float v[32];
+        if (FOLD) {
           const float nm = -ln_mean;
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 bb = __ldg(b4 + q);
-            const float4 cs = __ldg(c4 + q);
-            v[4 * q + 0] = fmaf(fmaf(nm, cs.x, __uint_as_float(r[4 * q + 0])), ln_rstd, bb.x);
-            v[4 * q + 1] = fmaf(fmaf(nm, cs.y, __uint_as_float(r[4 * q + 1])), ln_rstd, bb.y);
-            v[4 * q + 2] = fmaf(fmaf(nm, cs.z, __uint_as_float(r[4 * q + 2])), ln_rstd, bb.z);
-            v[4 * q + 3] = fmaf(fmaf(nm, cs.w, __uint_as_float(r[4 * q + 3])), ln_rstd, bb.w);
+            v[4 * q + 0] = fmaf(fmaf(nm, cs[q].x, __uint_as_float(r[4 * q + 0])), ln_rstd, bb[q].x);
+            v[4 * q + 1] = fmaf(fmaf(nm, cs[q].y, __uint_as_float(r[4 * q + 1])), ln_rstd, bb[q].y);
+            v[4 * q + 2] = fmaf(fmaf(nm, cs[q].z, __uint_as_float(r[4 * q + 2])), ln_rstd, bb[q].z);
+            v[4 * q + 3] = fmaf(fmaf(nm, cs[q].w, __uint_as_float(r[4 * q + 3])), ln_rstd, bb[q].w);
           }
         } else {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 bb = __ldg(b4 + q);
-            v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb.x;
-            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb.y;
-            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb.z;
-            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb.w;
+            v[4 * q + 0] = __uint_as_float(r[4 * q + 0]) + bb[q].x;
+            v[4 * q + 1] = __uint_as_float(r[4 * q + 1]) + bb[q].y;
+            v[4 * q + 2] = __uint_as_float(r[4 * q + 2]) + bb[q].z;
+            v[4 * q + 3] = __uint_as_float(r[4 * q + 3]) + bb[q].w;
           }
         }
         if (EPI == EPI_BIAS_GELU || EPI == EPI_LN_FOLD_GELU) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
         }
-        if (row_ok) {
-          if (RES_F32) {
-            const float4* rs = reinterpret_cast<const float4*>(
-                static_cast<const float*>(p.residual) + (size_t)row * p.ldr + col0);
+        const bool more = cc + 1 < CHUNKS && col0 + 32 < p.n;
+        if (staged_res) {
+          // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk j of row r at j ^ (r % 8).
+          // The previous TMA store from this warp's staging block must have read it.
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // residual in, transposed by position
+            const int rr = 4 * q + (lane >> 3), j = lane & 7;
+            const uint32_t dst = stage_out + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(rc[q].x),
+                         "f"(rc[q].y), "f"(rc[q].z), "f"(rc[q].w)
+                         : "memory");
+          }
+          __syncwarp();
+          const uint32_t rbase = stage_out + (uint32_t)(lane * 128);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {  // this row's residual; the sum goes to the same slot
+            const uint32_t a = rbase + (uint32_t)(((j ^ (lane & 7)) & 7) << 4);
+            float4 x;
+            asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                         : "r"(a)
+                         : "memory");
+            v[4 * j + 0] += x.x;
+            v[4 * j + 1] += x.y;
+            v[4 * j + 2] += x.z;
+            v[4 * j + 3] += x.w;
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(v[4 * j + 0]),
+                         "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
+                         : "memory");
+          }
+          if (more) load_res(true, row0, row, col0 + 32);
+          if (EPI == EPI_RESIDUAL_F32_STATS) {
+            float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              s4[i & 3] += v[i];
+              q4[i & 3] = fmaf(v[i], v[i], q4[i & 3]);
+            }
+            row_sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
+            row_sq += (q4[0] + q4[1]) + (q4[2] + q4[3]);
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stage_out, col0, row0);
+            bulk_commit();
+          }
+          if (EPI == EPI_RESIDUAL_F32_STATS) {
+            // fp16 copy of the new residual (the next LayerNorm-folded GEMM's A operand),
+            // read back from the staging block four whole rows per instruction.
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
-              const float4 rv = rs[q];
-              v[4 * q + 0] += rv.x;
-              v[4 * q + 1] += rv.y;
-              v[4 * q + 2] += rv.z;
-              v[4 * q + 3] += rv.w;
-            }
-          } else if (EPI == EPI_BIAS_RESIDUAL) {
-            const uint4* rs = reinterpret_cast<const uint4*>(
-                static_cast<const __half*>(p.residual) + (size_t)row * p.ldr + col0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              const uint4 rv = rs[q];
-              const uint32_t rr[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const float2 res = unpack_half2(rr[e]);
-                v[8 * q + 2 * e + 0] += res.x;
-                v[8 * q + 2 * e + 1] += res.y;
-              }
+              const int rr = 4 * q + (lane >> 3), j = lane & 7;
+              const uint32_t a = stage_out + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
+              float4 x;
+              asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                           : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
+                           : "r"(a)
+                           : "memory");
+              *reinterpret_cast<uint2*>(p.out16 + (size_t)(row0 + rr) * p.ld16 + col0 + 4 * j) =
+                  make_uint2(pack_half2(x.x, x.y), pack_half2(x.z, x.w));
             }
           }
+          continue;
+        }
+        if ((RES_F32 || EPI == EPI_BIAS_RESIDUAL) && row_ok) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            v[4 * q + 0] += rc[q].x;
+            v[4 * q + 1] += rc[q].y;
+            v[4 * q + 2] += rc[q].z;
+            v[4 * q + 3] += rc[q].w;
+          }
+          if (more) load_res(false, row0, row, col0 + 32);
         }
         if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
           float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
@@ -300,7 +414,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           row_sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
           row_sq += (q4[0] + q4[1]) + (q4[2] + q4[3]);
-          // fp16 copy of the new residual: the next (LayerNorm-folded) GEMM's A operand.
           uint4* d16 = reinterpret_cast<uint4*>(p.out16 + (size_t)row * p.ld16 + col0);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -341,7 +454,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stage_out, col0, m_blk * GEMM_BM + quad * 32);
+            tma_store_2d(&tmC, stage_out, col0, row0);
             bulk_commit();
           }
         } else if (row_ok) {

@@ -264,11 +264,13 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
     if (num_sms <= 0) return fail(TTTJ_ERR_CUDA, "could not query the SM count");
   }
   std::memset(g, 0, sizeof(*g));
-  g->bn = gemm_choose_bn(rows, n, num_sms);
+  gemm_choose(rows, n, k, epi, num_sms, &g->bn, &g->pair);
   g->epi = epi;
   int rc = make_tmap(&g->tmA, a, (uint64_t)(rows > 0 ? rows : 1), (uint64_t)k, (uint64_t)lda, GEMM_BM);
   if (rc) return rc;
-  rc = make_tmap(&g->tmB, w, (uint64_t)n, (uint64_t)k, (uint64_t)ldw, (uint32_t)g->bn);
+  // B boxes: bn rows, or bn / 2 per CTA of a pair.
+  rc = make_tmap(&g->tmB, w, (uint64_t)n, (uint64_t)k, (uint64_t)ldw,
+                 (uint32_t)(g->pair ? g->bn / 2 : g->bn));
   if (rc) return rc;
   // Output: 32x32 boxes; fp32 rows of the box are 128 B (128-byte swizzle), fp16 rows
   // 64 B (64-byte swizzle), matching the epilogue's staging layout.
@@ -290,8 +292,14 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   g->p.ldr = ldr;
   g->p.status = status;
   g->p.wait_limit_ns = kWaitLimitNs;
-  const long tiles = (long)((rows + GEMM_BM - 1) / GEMM_BM) * ((n + g->bn - 1) / g->bn);
-  g->grid = (int)(tiles < num_sms ? tiles : num_sms);
+  const long tm = g->pair ? 2 * GEMM_BM : GEMM_BM;
+  const long tiles = (long)((rows + tm - 1) / tm) * ((n + g->bn - 1) / g->bn);
+  if (g->pair) {
+    const long pairs = num_sms / 2;
+    g->grid = 2 * (int)(tiles < pairs ? tiles : pairs);
+  } else {
+    g->grid = (int)(tiles < num_sms ? tiles : num_sms);
+  }
   return TTTJ_OK;
 }
 

@@ -9,34 +9,40 @@ namespace {
 constexpr int STAGES_BN64 = 8;   // 8 x 24 KB ring (+32 KB output staging)
 constexpr int STAGES_BN128 = 6;  // 6 x 32 KB ring (+32 KB output staging)
 constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring (+32 KB output staging)
+// CTA pairs hold half of B per CTA: the same shared memory buys deeper rings.
+constexpr int STAGES_PAIR_BN128 = 8;  // 8 x 24 KB
+constexpr int STAGES_PAIR_BN256 = 6;  // 6 x 32 KB
 
-template <int BN, int EPI, int STAGES>
+template <int BN, int EPI, int STAGES, bool PAIR>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-  auto kern = gemm_tc_kernel<BN, EPI, STAGES>;
-  constexpr int smem = GemmSmem<BN, STAGES>::TOTAL;
+  auto kern = gemm_tc_kernel<BN, EPI, STAGES, PAIR>;
+  constexpr int smem = GemmSmem<BN, STAGES, PAIR>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the 227 KB per-CTA limit");
+  if (PAIR)
+    return launch_pdl_cluster(kern, dim3(g.grid), dim3(GEMM_THREADS), smem, stream, 2, g.tmA,
+                              g.tmB, g.tmC, g.p);
   return launch_pdl(kern, dim3(g.grid), dim3(GEMM_THREADS), smem, stream, g.tmA, g.tmB, g.tmC, g.p);
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool PAIR>
 cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
   switch (g.epi) {
     case EPI_BIAS:
-      return launch_t<BN, EPI_BIAS, STAGES>(g, stream);
+      return launch_t<BN, EPI_BIAS, STAGES, PAIR>(g, stream);
     case EPI_BIAS_GELU:
-      return launch_t<BN, EPI_BIAS_GELU, STAGES>(g, stream);
+      return launch_t<BN, EPI_BIAS_GELU, STAGES, PAIR>(g, stream);
     case EPI_BIAS_RESIDUAL:
-      return launch_t<BN, EPI_BIAS_RESIDUAL, STAGES>(g, stream);
+      return launch_t<BN, EPI_BIAS_RESIDUAL, STAGES, PAIR>(g, stream);
     case EPI_BIAS_RESIDUAL_F32:
-      return launch_t<BN, EPI_BIAS_RESIDUAL_F32, STAGES>(g, stream);
+      return launch_t<BN, EPI_BIAS_RESIDUAL_F32, STAGES, PAIR>(g, stream);
     case EPI_RESIDUAL_F32_STATS:
-      return launch_t<BN, EPI_RESIDUAL_F32_STATS, STAGES>(g, stream);
+      return launch_t<BN, EPI_RESIDUAL_F32_STATS, STAGES, PAIR>(g, stream);
     case EPI_LN_FOLD:
-      return launch_t<BN, EPI_LN_FOLD, STAGES>(g, stream);
+      return launch_t<BN, EPI_LN_FOLD, STAGES, PAIR>(g, stream);
     case EPI_LN_FOLD_GELU:
-      return launch_t<BN, EPI_LN_FOLD_GELU, STAGES>(g, stream);
+      return launch_t<BN, EPI_LN_FOLD_GELU, STAGES, PAIR>(g, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -45,11 +51,12 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
 }  // namespace
 
 int gemm_choose_bn(int rows, int n, int num_sms) {
-  // The widest column tile whose tile count still fills >= 90% of the SMs: wider
-  // tiles re-read A less and amortise the epilogue over a longer MMA, but a tile count
-  // below the SM count leaves SMs idle.  (Measured on B200 over the projection shapes
-  // of the BASELINE configurations: BN 256 wins every large GEMM by up to 1.4x over
-  // BN 128; the narrow tiles win only when 256-wide tiles cannot fill the machine.)
+  // The widest column tile whose tile count (128-row tiles) still fills >= 90% of the
+  // SMs: wider tiles re-read A less and amortise the epilogue over a longer MMA, but a
+  // tile count below the SM count leaves SMs idle.  (Measured on B200 over the
+  // projection shapes of the benchmark configurations: BN 256 wins every large GEMM by
+  // up to 1.4x over BN 128; the narrow tiles win only when 256-wide tiles cannot fill
+  // the machine.)
   const long m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
   const long need = (long)num_sms * 9 / 10;
   for (int bn : {256, 128}) {
@@ -58,10 +65,31 @@ int gemm_choose_bn(int rows, int n, int num_sms) {
   return 64;
 }
 
+void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair) {
+  *bn = gemm_choose_bn(rows, n, num_sms);
+  // CTA pairs (256-row tiles) cut each SM's operand traffic by a third and deepen the
+  // ring, which pays where the main loop dominates: long K, and enough tiles that the
+  // doubled tile size does not cost a partial wave.  They lose (measured) where the
+  // erf-GELU epilogue is the longer stage, and on short-K / few-wave GEMMs where the
+  // pair's coupling and ramp-up outweigh the feed.
+  const bool gelu = epi == EPI_BIAS_GELU || epi == EPI_LN_FOLD_GELU;
+  *pair = 0;
+  if (*bn == 128 || *bn == 256) {
+    const double units = (double)(num_sms / 2);
+    const double waves = (double)((rows + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * (n / *bn) / units;
+    if ((k >= 2048 && waves >= 3.0) || (k >= 1024 && !gelu && waves >= 6.0)) *pair = 1;
+  }
+}
+
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream) {
-  if (g.bn == 256) return launch_bn<256, STAGES_BN256>(g, stream);
-  if (g.bn == 128) return launch_bn<128, STAGES_BN128>(g, stream);
-  if (g.bn == 64) return launch_bn<64, STAGES_BN64>(g, stream);
+  if (g.pair) {
+    if (g.bn == 256) return launch_bn<256, STAGES_PAIR_BN256, true>(g, stream);
+    if (g.bn == 128) return launch_bn<128, STAGES_PAIR_BN128, true>(g, stream);
+    return cudaErrorInvalidValue;
+  }
+  if (g.bn == 256) return launch_bn<256, STAGES_BN256, false>(g, stream);
+  if (g.bn == 128) return launch_bn<128, STAGES_BN128, false>(g, stream);
+  if (g.bn == 64) return launch_bn<64, STAGES_BN64, false>(g, stream);
   return cudaErrorInvalidValue;
 }
 

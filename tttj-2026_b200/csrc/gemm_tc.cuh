@@ -17,6 +17,11 @@
 // with one TMA tile store; only the tile that straddles the last valid row falls back
 // to row-masked stores.  One CTA per SM; tiles are walked persistently, N-tile
 // fastest, so the CTAs in flight share A row-blocks in L2.
+// Large GEMMs run on CTA pairs (PAIR, a cluster of 2): the even CTA issues M=256
+// tcgen05.mma.cta_group::2 over both CTAs' shared memory, each CTA loads its 128 rows
+// of A and half of the tile's B columns (its loads complete on the leader's barrier),
+// and each drains its own 128 x BN accumulator.  Per SM that is two thirds of the
+// operand bytes of a 128 x BN tile, and the freed shared memory deepens the ring.
 // The number of valid rows is read from device memory, so one launch shape serves
 // every valid-token count (no host synchronisation on the mask).
 #pragma once
@@ -25,10 +30,13 @@
 
 namespace tttj {
 
-template <int BN, int STAGES>
+// PAIR: the tile is 256 x BN, computed by a CTA pair (cluster of 2) with cta_group::2
+// MMAs; each CTA holds 128 rows of A and BN/2 rows of B per stage and drains its own
+// 128 x BN accumulator.
+template <int BN, int STAGES, bool PAIR = false>
 struct GemmSmem {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
-  static constexpr int B_BYTES = BN * GEMM_BK * 2;
+  static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int OUT_BYTES = GEMM_EPI_WARPS * GEMM_STAGE_OUT_BYTES;
@@ -37,11 +45,17 @@ struct GemmSmem {
   static constexpr int TOTAL = TILE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int EPI, int STAGES>
+template <int BN, int EPI, int STAGES, bool PAIR>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using L = GemmSmem<BN, STAGES>;
+  using L = GemmSmem<BN, STAGES, PAIR>;
+  constexpr int CTAS = PAIR ? 2 : 1;
+  constexpr int TM = GEMM_BM * CTAS;  // rows of a tile
+  // Scheduling unit: the CTA, or the CTA pair (CTAs 2c and 2c+1 form cluster c).
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int n_units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw_addr & 1023u)) & 1023u;
@@ -75,7 +89,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8 * b, 1);
-      mbar_init(bar_acce + 8 * b, GEMM_EPI_WARPS * 32);
+      // One arrival per epilogue warp of each CTA (a pair's leader counts both CTAs).
+      mbar_init(bar_acce + 8 * b, GEMM_EPI_WARPS * CTAS);
     }
     mbar_init(bar_drain, 1);
     *abort_flag = 0;
@@ -83,18 +98,27 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 2 * BN);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(smem_u32(tmem_slot), 2 * BN);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_u32(tmem_slot), 2 * BN);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  // A pair's barriers receive arrivals from the peer CTA: both must be initialised first.
+  if (PAIR)
+    cluster_sync_all();
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   griddep_wait();
   griddep_launch();
   const int rows = p.rows_dev ? min(*p.rows_dev, p.rows_max) : p.rows_max;
-  const int m_tiles = (rows + GEMM_BM - 1) / GEMM_BM;
+  const int m_tiles = (rows + TM - 1) / TM;
   const int num_tiles = m_tiles * n_tiles;
 
   if (warp == 0) {
@@ -104,19 +128,28 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t phase = 0;
       long issued = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
         const int m_blk = tile / n_tiles;
         const int n_blk = tile - m_blk * n_tiles;
+        const int a_row = m_blk * TM + (int)rank * GEMM_BM;
+        const int b_row = n_blk * BN + (int)rank * (BN / CTAS);
         for (int kk = 0; kk < k_iters; ++kk) {
           if (!mbar_wait(bar_empty + 8 * stage, phase ^ 1u, abort_flag, limit)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(bar_full + 8 * stage, L::STAGE_BYTES);
-          tma_load_2d(sA + stage * L::A_BYTES, &tmA, bar_full + 8 * stage, kk * GEMM_BK,
-                      m_blk * GEMM_BM);
-          tma_load_2d(sB + stage * L::B_BYTES, &tmB, bar_full + 8 * stage, kk * GEMM_BK,
-                      n_blk * BN);
+          if (PAIR) {
+            // Both CTAs' loads complete on the leader's full barrier, which the leader
+            // arms for the bytes of both.
+            const uint32_t full_leader = map_to_cta(bar_full + 8 * stage, 0);
+            if (rank == 0) mbar_arrive_expect_tx(bar_full + 8 * stage, 2 * L::STAGE_BYTES);
+            tma_load_2d_pair(sA + stage * L::A_BYTES, &tmA, full_leader, kk * GEMM_BK, a_row);
+            tma_load_2d_pair(sB + stage * L::B_BYTES, &tmB, full_leader, kk * GEMM_BK, b_row);
+          } else {
+            mbar_arrive_expect_tx(bar_full + 8 * stage, L::STAGE_BYTES);
+            tma_load_2d(sA + stage * L::A_BYTES, &tmA, bar_full + 8 * stage, kk * GEMM_BK, a_row);
+            tma_load_2d(sB + stage * L::B_BYTES, &tmB, bar_full + 8 * stage, kk * GEMM_BK, b_row);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
@@ -127,24 +160,30 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!ok) {
         *abort_flag = 1;
         report_status(p.status, TTTJ_DEV_TIMEOUT_PRODUCER);
-        // Let the loads already issued land before the CTA can exit.
-        for (long j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j) {
-          mbar_wait(bar_full + 8 * (int)(j % STAGES), (uint32_t)((j / STAGES) & 1), nullptr,
-                    limit);
+        // Let the loads already issued land before the CTA can exit.  (A pair's
+        // follower cannot observe its loads, which complete on the leader's barrier;
+        // both CTAs meet at the final cluster barrier, after every other role has given
+        // up waiting, by which time they have landed.)
+        if (!PAIR || rank == 0) {
+          for (long j = (issued > STAGES ? issued - STAGES : 0); j < issued; ++j) {
+            mbar_wait(bar_full + 8 * (int)(j % STAGES), (uint32_t)((j / STAGES) & 1), nullptr,
+                      limit);
+          }
         }
       }
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16_f32(GEMM_BM, BN);
+    // A pair's MMAs are issued by its leader only (they cover both CTAs' tiles).
+    if (lane == 0 && (!PAIR || rank == 0)) {
+      constexpr uint32_t idesc = idesc_f16_f32(TM, BN);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
         if (!mbar_wait(bar_acce + 8 * acc, acc_phase ^ 1u, abort_flag, limit)) {
           ok = false;
           break;
@@ -162,18 +201,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int j = 0; j < GEMM_BK / 16; ++j) {
             // Advance 16 fp16 (32 B) along K inside the 128-byte swizzle atom.
-            mma_f16_ss(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
-                       (kk | j) != 0 ? 1u : 0u);
+            if (PAIR)
+              mma_f16_ss_pair(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
+                              (kk | j) != 0 ? 1u : 0u);
+            else
+              mma_f16_ss(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
+                         (kk | j) != 0 ? 1u : 0u);
           }
           issued_any = true;
-          mma_commit(bar_empty + 8 * stage);
+          // Frees the stage in both CTAs of a pair.
+          if (PAIR)
+            mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+          else
+            mma_commit(bar_empty + 8 * stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        mma_commit(bar_accf + 8 * acc);
+        if (PAIR)
+          mma_commit_pair_mc(bar_accf + 8 * acc, 0x3);
+        else
+          mma_commit(bar_accf + 8 * acc);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
@@ -182,7 +232,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         report_status(p.status, TTTJ_DEV_TIMEOUT_MMA);
         if (issued_any) {
           // Wait for the MMAs already issued before TMEM is released.
-          mma_commit(bar_drain);
+          if (PAIR)
+            mma_commit_pair(bar_drain);
+          else
+            mma_commit(bar_drain);
           mbar_wait(bar_drain, 0, nullptr, limit);
         }
       }
@@ -209,7 +262,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       if (!(RES_F32 || EPI == EPI_BIAS_RESIDUAL) || t >= num_tiles) return;
       const int mb = t / n_tiles;
       const int c0 = (t - mb * n_tiles) * BN + col_half * (BN / 2);
-      const int r = mb * GEMM_BM + row_in_tile;
+      const int r = mb * TM + (int)rank * GEMM_BM + row_in_tile;
       const int esize = RES_F32 ? 4 : 2;
       const uint32_t bytes = (uint32_t)(min(BN / 2, p.n - c0) * esize) & ~15u;
       if (r < rows && c0 < p.n && bytes > 0)
@@ -247,16 +300,17 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     };
-    prefetch_residual(blockIdx.x);
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    prefetch_residual(unit);
+    for (int tile = unit; tile < num_tiles; tile += n_units) {
       const int m_blk = tile / n_tiles;
       const int n_blk = tile - m_blk * n_tiles;
-      prefetch_residual(tile + (int)gridDim.x);
-      const int row0 = m_blk * GEMM_BM + quad * 32;  // first of this warp's 32 rows
+      prefetch_residual(tile + n_units);
+      const int cta_row0 = m_blk * TM + (int)rank * GEMM_BM;  // this CTA's 128 rows
+      const int row0 = cta_row0 + quad * 32;  // first of this warp's 32 rows
       const int row = row0 + lane;
       const bool row_ok = row < rows;
-      // Every row of the tile is valid: stage + TMA store.  Otherwise masked stores.
-      const bool full_tile = (m_blk + 1) * GEMM_BM <= rows;
+      // Every row of the CTA's tile is valid: stage + TMA store.  Otherwise masked stores.
+      const bool full_tile = cta_row0 + GEMM_BM <= rows;
       const bool staged_res = RES_F32 && full_tile;
       // Everything that does not depend on the accumulator is fetched before waiting
       // for it: the LayerNorm statistics of this row and the first residual chunk.
@@ -477,8 +531,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       }
+      // The warp's TMEM reads are complete (tcgen05.wait::ld in every lane): release
+      // the accumulator to the (leader's) MMA thread.
       tc_fence_before();
-      mbar_arrive(bar_acce + 8 * acc);
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR)
+          mbar_arrive_cluster(map_to_cta(bar_acce + 8 * acc, 0));
+        else
+          mbar_arrive(bar_acce + 8 * acc);
+      }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
       if (EPI == EPI_RESIDUAL_F32_STATS && row_ok)
@@ -491,10 +553,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 
   tc_fence_before();
-  __syncthreads();
+  // A pair's CTAs leave together: the leader's MMAs write the follower's TMEM, and the
+  // follower's loads and arrivals target the leader's barriers.
+  if (PAIR)
+    cluster_sync_all();
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, 2 * BN);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, 2 * BN);
+    else
+      tmem_dealloc(tmem_base, 2 * BN);
   }
 }
 

@@ -26,19 +26,43 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
 }
 
+// launch_pdl for a kernel launched in clusters of `cluster_x` CTAs along x.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t stream, int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Args&&>(args)...);
+}
+
 struct GemmLaunch {
   CUtensorMap tmA;
   CUtensorMap tmB;
   CUtensorMap tmC;  // output, 32x32 boxes (TMA tile stores)
   GemmParams p;
-  int bn;   // 128 or 256
-  int epi;  // GemmEpilogue
-  int grid; // persistent CTAs
+  int bn;    // 64, 128 or 256
+  int pair;  // 1: 256 x bn tiles on CTA pairs (cta_group::2), 0: 128 x bn tiles per CTA
+  int epi;   // GemmEpilogue
+  int grid;  // persistent CTAs (even for pairs)
 };
 
-// Column-tile width for a GEMM of `rows` x `n` on `num_sms` SMs: the one with the
-// smaller (waves x tile cost) estimate.
+// Tile shape for a GEMM of `rows` x `n` x `k` with epilogue `epi` on `num_sms` SMs:
+// column width (a function of rows and n only, so every GEMM with the same output
+// shape uses the same width) and whether CTA pairs compute it (see gemm.cu).
 int gemm_choose_bn(int rows, int n, int num_sms);
+void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair);
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
 // tcgen05 attention (256-query items, plan with q_block ATC_ITEM_ROWS, kv_block ATC_BN).

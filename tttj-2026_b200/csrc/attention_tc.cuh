@@ -14,16 +14,17 @@
 //               into TMEM, and O_t += P_t V_j with P_t read from TMEM (A operand)
 //   warps 0-3   softmax for query tile 0 (one thread = one query row = one TMEM lane)
 //   warps 4-7   softmax for query tile 1
-// While one softmax warpgroup works on its tile, the tensor core runs the other tile's
-// P V and next Q K^T, so MMA and softmax overlap.  A softmax thread loads its 128 scores
-// from TMEM, applies the masks, updates the running max (rescaling O in TMEM only when
-// the max grows by more than 2^8, lazily), writes P as packed fp16 back over the first
-// 64 columns of its S buffer, and signals the MMA warp.  At the end of an item it
-// normalises O by the row sum and stores the valid rows.
+// P has its own TMEM buffer, so S_t(j+1) is issued as soon as the softmax threads have
+// read S_t(j) into registers (s_free): the tensor core computes the next scores while
+// the softmax works on the current ones, and neither warpgroup waits for an MMA in the
+// steady state -- the exponentials (MUFU) set the pace.  A softmax thread loads its 128
+// scores, releases the S buffer, applies the masks, updates the running max (rescaling
+// O in TMEM only when the max grows by more than 2^8, lazily), waits until the previous
+// P V has read the P buffer (pv_done), writes P as packed fp16 and signals the MMA warp
+// (p_full).  At the end of an item it normalises O by the row sum and stores the rows.
 //
-// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+hd) O1 [384,384+hd).
-// The ordering of tcgen05.mma operations issued by one thread guarantees that the
-// next S MMA into a buffer runs after the P V that read P from it.
+// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
+//                     O0 [384,384+hd) O1 [448,448+hd).
 //
 // Every wait is bounded (TTTJ wait limit); on a timeout the role records
 // TTTJ_DEV_TIMEOUT_ATTN in the status word, raises the CTA abort flag and unwinds.
@@ -44,10 +45,11 @@ struct AtcSmem {
   static constexpr int STAGES = HD == 64 ? 3 : 4;
   static constexpr int Q_BYTES = 2 * 2 * Q_TILE;  // 2 buffers x 2 tiles
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
-  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 1;
+  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 1;
   static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
   static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + 1024;
-  static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_O0 = 256, TMEM_O1 = 384;
+  static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_P0 = 256, TMEM_P1 = 320,
+                            TMEM_O0 = 384, TMEM_O1 = 448;
 };
 
 struct AtcItem {
@@ -109,7 +111,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const uint32_t bar_p_full = bar_s_full + 16;             // [2]
   const uint32_t bar_o_full = bar_p_full + 16;             // [2]
   const uint32_t bar_o_free = bar_o_full + 16;             // [2]
-  const uint32_t bar_drain = bar_o_free + 16;
+  const uint32_t bar_s_free = bar_o_free + 16;             // [2] scores read by softmax
+  const uint32_t bar_pv_done = bar_s_free + 16;            // [2] P V complete
+  const uint32_t bar_drain = bar_pv_done + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // Decoded work item per Q buffer, written by the loader before it arms q_full, read
@@ -132,6 +136,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       mbar_init(bar_p_full + 8 * i, ATC_BM);
       mbar_init(bar_o_full + 8 * i, 1);
       mbar_init(bar_o_free + 8 * i, ATC_BM);
+      mbar_init(bar_s_free + 8 * i, ATC_BM);
+      mbar_init(bar_pv_done + 8 * i, 1);
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_kv_full + 8 * s, 1);
@@ -224,6 +230,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       bool issued = false;
       long kvc = 0;             // KV tiles consumed
       long pc[2] = {0, 0};      // p_full waits per tile
+      long sfc[2] = {0, 0};     // s_free waits per tile
       long oc[2] = {0, 0};      // o_free waits per tile
       int k = 0;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
@@ -241,6 +248,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (w.n_kv < 0) break;  // no more items
         const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
         const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
+        const uint32_t p_col[2] = {SM::TMEM_P0, SM::TMEM_P1};
         const uint32_t o_col[2] = {SM::TMEM_O0, SM::TMEM_O1};
         long kv_waited = kvc - 1;  // highest KV tile index (global count) already waited on
         auto ensure_kv = [&](long idx) -> bool {
@@ -268,8 +276,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           const uint64_t vd = atc_desc_v<HD>(vaddr);
 #pragma unroll
           for (int kk = 0; kk < ATC_BN / 16; ++kk)
-            mma_f16_ts(tmem + o_col[t], tmem + s_col[t] + (uint32_t)(kk * 8),
+            mma_f16_ts(tmem + o_col[t], tmem + p_col[t] + (uint32_t)(kk * 8),
                        vd + (uint64_t)(kk * v_step), idesc_o, (accumulate || kk > 0) ? 1u : 0u);
+          mma_commit(bar_pv_done + 8 * t);
           issued = true;
         };
         if (!ensure_kv(kvc)) break;
@@ -277,17 +286,21 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (w.n[1] > 0) issue_s(1, kvc);
         for (int j = 0; j < w.n_kv && ok; ++j) {
           const long kv_j = kvc + j;
-          for (int t = 0; t < 2; ++t) {
+          // Next scores first: each tile's S buffer is free once its softmax threads have
+          // read S(j) (s_free), long before they publish P(j).
+          for (int t = 0; t < 2 && ok; ++t) {
+            if (j + 1 >= w.n[t]) continue;
+            if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc[t]++ & 1))) break;
+            if (!ensure_kv(kv_j + 1)) break;
+            issue_s(t, kv_j + 1);
+          }
+          for (int t = 0; t < 2 && ok; ++t) {
             if (j >= w.n[t]) continue;
             if (!wait(bar_p_full + 8 * t, (uint32_t)(pc[t]++ & 1))) break;
+            // The first P V of an item overwrites O: the previous item's O must be read.
             if (j == 0 && !wait(bar_o_free + 8 * t, (uint32_t)(oc[t]++ & 1) ^ 1u)) break;
             issue_pv(t, kv_j, j > 0);
-            if (j + 1 < w.n[t]) {
-              if (!ensure_kv(kv_j + 1)) break;
-              issue_s(t, kv_j + 1);
-            } else {
-              mma_commit(bar_o_full + 8 * t);
-            }
+            if (j + 1 == w.n[t]) mma_commit(bar_o_full + 8 * t);
           }
           if (!ok) break;
           mma_commit(bar_kv_empty + 8 * (int)(kv_j % STAGES));
@@ -311,9 +324,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     const int row = quad * 32 + lane;    // row inside the query tile
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t s_addr = tmem + lane_base + (t == 0 ? SM::TMEM_S0 : SM::TMEM_S1);
+    const uint32_t p_addr = tmem + lane_base + (t == 0 ? SM::TMEM_P0 : SM::TMEM_P1);
     const uint32_t o_addr = tmem + lane_base + (t == 0 ? SM::TMEM_O0 : SM::TMEM_O1);
     const float scale = p.scale_log2;
     long sc = 0, ofc = 0;
+    long pv_before = 0;  // P V MMAs of this tile issued before the current item
     bool ok = true;
     int k = 0;
     for (; ok; ++k) {
@@ -346,6 +361,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           for (int e = 0; e < 32; ++e) sv[c * 32 + e] = chunk[e];
         }
         tmem_wait_ld();
+        // The scores are in registers: the S buffer may take the next tile's scores.
+        if (j + 1 < n) {
+          tc_fence_before();
+          mbar_arrive(bar_s_free + 8 * t);
+        }
         const int k0 = j * ATC_BN;
         const bool need_mask =
             (k0 + ATC_BN > kv_end) || (CAUSAL && k0 + ATC_BN - 1 > w.q0 + t * ATC_BM);
@@ -356,14 +376,16 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           for (int c = 0; c < ATC_BN; ++c)
             if (c > lim) sv[c] = __float_as_uint(-INFINITY);
         }
-        // Row max with 8 independent partial maxima (short dependency chains).
+        // Row max: 8 independent chains of three-input maxima.
         float pm[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) pm[i] = __uint_as_float(sv[i]);
 #pragma unroll
-        for (int c = 8; c < ATC_BN; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(sv[c]));
-        const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        for (int c = 8; c < ATC_BN; c += 2)
+          pm[(c >> 1) & 7] =
+              fmax3f(pm[(c >> 1) & 7], __uint_as_float(sv[c]), __uint_as_float(sv[c + 1]));
+        const float mx = fmax3f(fmax3f(pm[0], pm[1], pm[2]), fmax3f(pm[3], pm[4], pm[5]),
+                                fmaxf(pm[6], pm[7]));
         const float m_tile = mx * scale;
         float alpha = 1.f;
         bool rescale = false;
@@ -380,27 +402,40 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           }
         }
         const float base = (m_run == -INFINITY) ? 0.f : m_run;
+        // P(j) replaces P(j-1) in the P buffer, and O is rescaled below: P V(j-1) must
+        // be complete.  (It was issued when this thread published P(j-1); completion
+        // number pv_before + j - 1 of pv_done.  P V(j) cannot exist yet, and completion
+        // j - 2 (or the previous item's last, via o_full) was observed already, so the
+        // parity is unambiguous.)  At j == 0 the previous item's o_full covered it.
+        if (j > 0) {
+          if (!mbar_wait(bar_pv_done + 8 * t, (uint32_t)((pv_before + j - 1) & 1), abort_flag,
+                         limit)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+        }
+        const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(-base, -base);
         float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial row sums
-        // P as fp16 pairs over the first 64 columns of this tile's S buffer (the scores
-        // are already in registers), 16 columns (32 scores) per TMEM store.
+        // P as fp16 pairs: 128 keys -> 64 columns, 16 columns (32 scores) per TMEM store.
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           uint32_t pk[16];
 #pragma unroll
           for (int c = 0; c < 16; ++c) {
             const int i = q * 32 + 2 * c;
-            const float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), scale, -base));
-            const float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), scale, -base));
+            const float2 x = ffma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])),
+                                   sc2, nb2);
+            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
             ps[c & 3] += p0 + p1;
             pk[c] = pack_half2(p0, p1);
           }
-          tmem_st_32x32b_x16(s_addr + (uint32_t)(q * 16), pk);
+          tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), pk);
         }
         const float rs = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         l_run = l_run * alpha + rs;
         if (rescale) {
-          // O holds the previous tiles' P V (complete: the S MMA just waited on was
-          // issued after it).  Scale it in place, after the scores are consumed.
+          // O holds P V of the key tiles < j (complete, see above): scale it in place.
 #pragma unroll
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
@@ -415,6 +450,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         tc_fence_before();
         mbar_arrive(bar_p_full + 8 * t);
       }
+      pv_before += n;
       if (!ok) break;
       // Epilogue: O / l for the valid rows.
       if (!mbar_wait(bar_o_full + 8 * t, (uint32_t)(ofc++ & 1), abort_flag, limit)) {

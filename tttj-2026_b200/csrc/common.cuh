@@ -97,6 +97,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Non-blocking test of the same condition (mbarrier.test_wait never suspends the
+// thread, unlike try_wait): for a thread that polls several barriers in turn.
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait until the phase with parity `parity` of `bar` has completed.  The wait is
 // bounded: it gives up after `limit_ns` or as soon as `*abort` becomes non-zero and
 // returns false.  `abort` points to a shared-memory flag that a role sets when it

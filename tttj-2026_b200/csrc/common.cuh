@@ -427,6 +427,30 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// Packed fp32 pairs kept in one 64-bit register (sm_100 f32x2 arithmetic, round to
+// nearest like the scalar instructions).
+__device__ __forceinline__ unsigned long long pk2(float a, float b) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ unsigned long long fma2p(unsigned long long a, unsigned long long b,
+                                                    unsigned long long c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ unsigned long long mul2p(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // ---------------------------------------------------------------------------
 // numerics
 // ---------------------------------------------------------------------------
@@ -447,6 +471,36 @@ __device__ __forceinline__ float gelu_erf(float v) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(-z * z * 1.4426950408889634f));
   const float e = copysignf(fmaf(-poly, y, 1.0f), v);
   return 0.5f * v * (1.0f + e);
+}
+
+// gelu_erf on two values at once: the same formula, with the FMA-pipe arithmetic in
+// f32x2 pairs (half the instructions); the two reciprocals and exp2s stay scalar.
+// The last step is h + h e (one rounding) instead of h (1 + e) (two).
+__device__ __forceinline__ float2 gelu_erf2(float v0, float v1) {
+  const unsigned long long c_rs2 = pk2(0.70710678118654752440f, 0.70710678118654752440f);
+  const unsigned long long c_p = pk2(0.3275911f, 0.3275911f), one = pk2(1.0f, 1.0f);
+  // Negated Horner coefficients: poly_neg = -(a1 t + ... + a5 t^5).
+  const unsigned long long n1 = pk2(-0.254829592f, -0.254829592f);
+  const unsigned long long n2 = pk2(0.284496736f, 0.284496736f);
+  const unsigned long long n3 = pk2(-1.421413741f, -1.421413741f);
+  const unsigned long long n4 = pk2(1.453152027f, 1.453152027f);
+  const unsigned long long n5 = pk2(-1.061405429f, -1.061405429f);
+  const unsigned long long c_nl2e = pk2(-1.4426950408889634f, -1.4426950408889634f);
+  const unsigned long long z = mul2p(pk2(fabsf(v0), fabsf(v1)), c_rs2);
+  const float2 d = upk2(fma2p(c_p, z, one));
+  const unsigned long long t = pk2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
+  unsigned long long pn = fma2p(t, n5, n4);
+  pn = fma2p(t, pn, n3);
+  pn = fma2p(t, pn, n2);
+  pn = fma2p(t, pn, n1);
+  pn = mul2p(t, pn);
+  const float2 arg = upk2(mul2p(mul2p(z, z), c_nl2e));
+  float y0, y1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y0) : "f"(arg.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y1) : "f"(arg.y));
+  const float2 q = upk2(fma2p(pn, pk2(y0, y1), one));  // erf(|v| / sqrt 2)
+  const unsigned long long h = mul2p(pk2(v0, v1), pk2(0.5f, 0.5f));
+  return upk2(fma2p(h, pk2(copysignf(q.x, v0), copysignf(q.y, v1)), h));
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {

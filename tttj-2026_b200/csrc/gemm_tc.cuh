@@ -361,13 +361,20 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_wait_ld();
         float v[32];
         if (FOLD) {
-          const float nm = -ln_mean;
+          // v = rstd (acc - mean c) + b', in f32x2 pairs.
+          const unsigned long long nm2 = pk2(-ln_mean, -ln_mean), rs2 = pk2(ln_rstd, ln_rstd);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            v[4 * q + 0] = fmaf(fmaf(nm, cs[q].x, __uint_as_float(r[4 * q + 0])), ln_rstd, bb[q].x);
-            v[4 * q + 1] = fmaf(fmaf(nm, cs[q].y, __uint_as_float(r[4 * q + 1])), ln_rstd, bb[q].y);
-            v[4 * q + 2] = fmaf(fmaf(nm, cs[q].z, __uint_as_float(r[4 * q + 2])), ln_rstd, bb[q].z);
-            v[4 * q + 3] = fmaf(fmaf(nm, cs[q].w, __uint_as_float(r[4 * q + 3])), ln_rstd, bb[q].w);
+            const float2 lo = upk2(fma2p(fma2p(nm2, pk2(cs[q].x, cs[q].y),
+                                               pk2(__uint_as_float(r[4 * q + 0]), __uint_as_float(r[4 * q + 1]))),
+                                         rs2, pk2(bb[q].x, bb[q].y)));
+            const float2 hi = upk2(fma2p(fma2p(nm2, pk2(cs[q].z, cs[q].w),
+                                               pk2(__uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]))),
+                                         rs2, pk2(bb[q].z, bb[q].w)));
+            v[4 * q + 0] = lo.x;
+            v[4 * q + 1] = lo.y;
+            v[4 * q + 2] = hi.x;
+            v[4 * q + 3] = hi.y;
           }
         } else {
 #pragma unroll
@@ -380,7 +387,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (EPI == EPI_BIAS_GELU || EPI == EPI_LN_FOLD_GELU) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = gelu_erf(v[i]);
+          for (int i = 0; i < 32; i += 2) {
+            const float2 g = gelu_erf2(v[i], v[i + 1]);
+            v[i] = g.x;
+            v[i + 1] = g.y;
+          }
         }
         const bool more = cc + 1 < CHUNKS && col0 + 32 < p.n;
         if (staged_res) {

@@ -402,6 +402,19 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           }
         }
         const float base = (m_run == -INFINITY) ? 0.f : m_run;
+        const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(-base, -base);
+        float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial row sums
+        // P as fp16 pairs (128 keys -> 64 packed registers, each replacing two scores)
+        // computed before waiting for the previous P V, so the exponentials overlap it.
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float2 x = ffma2(make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])),
+                                 sc2, nb2);
+          const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
+          ps[c & 3] += p0 + p1;
+          pk[c] = pack_half2(p0, p1);
+        }
         // P(j) replaces P(j-1) in the P buffer, and O is rescaled below: P V(j-1) must
         // be complete.  (It was issued when this thread published P(j-1); completion
         // number pv_before + j - 1 of pv_done.  P V(j) cannot exist yet, and completion
@@ -415,22 +428,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           }
           tc_fence_after();
         }
-        const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(-base, -base);
-        float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial row sums
-        // P as fp16 pairs: 128 keys -> 64 columns, 16 columns (32 scores) per TMEM store.
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t pk[16];
+          uint32_t chunk[16];
 #pragma unroll
-          for (int c = 0; c < 16; ++c) {
-            const int i = q * 32 + 2 * c;
-            const float2 x = ffma2(make_float2(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])),
-                                   sc2, nb2);
-            const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
-            ps[c & 3] += p0 + p1;
-            pk[c] = pack_half2(p0, p1);
-          }
-          tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), pk);
+          for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
+          tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), chunk);
         }
         const float rs = (ps[0] + ps[1]) + (ps[2] + ps[3]);
         l_run = l_run * alpha + rs;

@@ -125,4 +125,9 @@ def test_multi_device_matches_single_device():
         multi = tb.MultiDeviceTransformer(model, [0, 1])
         out = multi(x, mask)
     torch.cuda.synchronize()
-    assert torch.equal(out, ref)
+    # Each device runs a sub-batch, whose GEMM tile width (hence the grouping of the
+    # LayerNorm statistics) may differ from the full batch's: rows agree to about two
+    # fp16 ulps, and padded rows stay exactly zero.
+    r = ref.float()
+    assert bool(((out.float() - r).abs() <= 2e-3 + 2e-3 * r.abs()).all())
+    assert bool((out[~mask] == 0).all())

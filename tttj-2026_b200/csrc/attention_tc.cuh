@@ -10,8 +10,9 @@
 // Work item = one (sequence, head, 256 query rows) = two 128-row query tiles.  The CTA
 // is persistent over the longest-first work list and runs 10 warps:
 //   warp 8      TMA: Q tiles (double-buffered across items), K/V tiles (STAGES ring)
-//   warp 9      one thread issues tcgen05.mma:  S_t = Q_t K_j^T  (M=128, N=128, K=hd)
-//               into TMEM, and O_t += P_t V_j with P_t read from TMEM (A operand)
+//   warp 9      issues tcgen05.mma (the whole warp runs the loop, one elected lane
+//               issues): S_t = Q_t K_j^T (M=128, N=128, K=hd) into TMEM, and
+//               O_t += P_t V_j with P_t read from TMEM (A operand)
 //   warps 0-3   softmax for query tile 0 (one thread = one query row = one TMEM lane)
 //   warps 4-7   softmax for query tile 1
 // P has its own TMEM buffer, so S_t(j+1) is issued as soon as the softmax threads have
@@ -222,7 +223,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     }
   } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the issue loop (barrier results combined with a vote, item
+    // fields broadcast from lane 0, so descriptors stay warp-uniform); one elected lane
+    // issues each tcgen05.mma / commit.
+    constexpr unsigned FULL = 0xffffffffu;
+    {
       constexpr uint32_t idesc_s = idesc_f16_f32(ATC_BM, ATC_BN);
       constexpr uint32_t idesc_o = idesc_f16_f32(ATC_BM, HD, 0, 1);
       constexpr uint32_t v_step = HD == 64 ? (2048u >> 4) : (1024u >> 4);  // 16 keys
@@ -234,7 +239,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       long oc[2] = {0, 0};      // o_free waits per tile
       int k = 0;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
-        if (!mbar_wait(bar, parity, abort_flag, limit)) {
+        if (!__all_sync(FULL, mbar_wait(bar, parity, abort_flag, limit))) {
           ok = false;
           return false;
         }
@@ -244,8 +249,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       for (; ok; ++k) {
         const int qb = k & 1;
         if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
-        const AtcItem w = info[qb];
-        if (w.n_kv < 0) break;  // no more items
+        const int n_kv = __shfl_sync(FULL, info[qb].n_kv, 0);
+        if (n_kv < 0) break;  // no more items
+        const int wn[2] = {__shfl_sync(FULL, info[qb].n[0], 0), __shfl_sync(FULL, info[qb].n[1], 0)};
         const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
         const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
         const uint32_t p_col[2] = {SM::TMEM_P0, SM::TMEM_P1};
@@ -266,9 +272,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           const uint64_t kd = atc_desc_qk<HD>(kaddr);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk)
-            mma_f16_ss(tmem + s_col[t], qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk), idesc_s,
-                       kk > 0 ? 1u : 0u);
-          mma_commit(bar_s_full + 8 * t);
+            mma_f16_ss_warp(tmem + s_col[t], qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk),
+                            idesc_s, kk > 0 ? 1u : 0u);
+          mma_commit_warp(bar_s_full + 8 * t);
           issued = true;
         };
         auto issue_pv = [&](int t, long kv_idx, bool accumulate) {
@@ -276,43 +282,45 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           const uint64_t vd = atc_desc_v<HD>(vaddr);
 #pragma unroll
           for (int kk = 0; kk < ATC_BN / 16; ++kk)
-            mma_f16_ts(tmem + o_col[t], tmem + p_col[t] + (uint32_t)(kk * 8),
-                       vd + (uint64_t)(kk * v_step), idesc_o, (accumulate || kk > 0) ? 1u : 0u);
-          mma_commit(bar_pv_done + 8 * t);
+            mma_f16_ts_warp(tmem + o_col[t], tmem + p_col[t] + (uint32_t)(kk * 8),
+                            vd + (uint64_t)(kk * v_step), idesc_o, (accumulate || kk > 0) ? 1u : 0u);
+          mma_commit_warp(bar_pv_done + 8 * t);
           issued = true;
         };
         if (!ensure_kv(kvc)) break;
         issue_s(0, kvc);
-        if (w.n[1] > 0) issue_s(1, kvc);
-        for (int j = 0; j < w.n_kv && ok; ++j) {
+        if (wn[1] > 0) issue_s(1, kvc);
+        for (int j = 0; j < n_kv && ok; ++j) {
           const long kv_j = kvc + j;
           // Next scores first: each tile's S buffer is free once its softmax threads have
           // read S(j) (s_free), long before they publish P(j).
           for (int t = 0; t < 2 && ok; ++t) {
-            if (j + 1 >= w.n[t]) continue;
+            if (j + 1 >= wn[t]) continue;
             if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc[t]++ & 1))) break;
             if (!ensure_kv(kv_j + 1)) break;
             issue_s(t, kv_j + 1);
           }
           for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= w.n[t]) continue;
+            if (j >= wn[t]) continue;
             if (!wait(bar_p_full + 8 * t, (uint32_t)(pc[t]++ & 1))) break;
             // The first P V of an item overwrites O: the previous item's O must be read.
             if (j == 0 && !wait(bar_o_free + 8 * t, (uint32_t)(oc[t]++ & 1) ^ 1u)) break;
             issue_pv(t, kv_j, j > 0);
-            if (j + 1 == w.n[t]) mma_commit(bar_o_full + 8 * t);
+            if (j + 1 == wn[t]) mma_commit_warp(bar_o_full + 8 * t);
           }
           if (!ok) break;
-          mma_commit(bar_kv_empty + 8 * (int)(kv_j % STAGES));
+          mma_commit_warp(bar_kv_empty + 8 * (int)(kv_j % STAGES));
         }
-        kvc += w.n_kv;
-        if (ok) mma_commit(bar_q_empty + 8 * qb);
+        kvc += n_kv;
+        if (ok) mma_commit_warp(bar_q_empty + 8 * qb);
       }
       if (!ok) {
-        *abort_flag = 1;
-        report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
+        if (lane == 0) {
+          *abort_flag = 1;
+          report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
+        }
         if (issued) {
-          mma_commit(bar_drain);
+          mma_commit_warp(bar_drain);
           mbar_wait(bar_drain, 0, nullptr, limit);
         }
       }
@@ -403,16 +411,26 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
         const float base = (m_run == -INFINITY) ? 0.f : m_run;
         const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(-base, -base);
-        float ps[4] = {0.f, 0.f, 0.f, 0.f};  // 4 independent partial row sums
+        unsigned long long ps2[2] = {0ull, 0ull};  // partial row sums, f32x2 pairs
         // P as fp16 pairs (128 keys -> 64 packed registers, each replacing two scores)
         // computed before waiting for the previous P V, so the exponentials overlap it.
+        // One pair in four takes its exponentials from the FMA pipe (exp2_fma2): the
+        // MUFU (16 per clock per SM) is the tighter resource at head_dim 64.
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
           const float2 x = ffma2(make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])),
                                  sc2, nb2);
-          const float p0 = ex2_approx(x.x), p1 = ex2_approx(x.y);
-          ps[c & 3] += p0 + p1;
+          float p0, p1;
+          if ((c & 3) == 3) {
+            const float2 e = exp2_fma2(x);
+            p0 = e.x;
+            p1 = e.y;
+          } else {
+            p0 = ex2_approx(x.x);
+            p1 = ex2_approx(x.y);
+          }
+          ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
           pk[c] = pack_half2(p0, p1);
         }
         // P(j) replaces P(j-1) in the P buffer, and O is rescaled below: P V(j-1) must
@@ -435,8 +453,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
           tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), chunk);
         }
-        const float rs = (ps[0] + ps[1]) + (ps[2] + ps[3]);
-        l_run = l_run * alpha + rs;
+        const float2 rs2 = upk2(add2p(ps2[0], ps2[1]));
+        l_run = l_run * alpha + (rs2.x + rs2.y);
         if (rescale) {
           // O holds P V of the key tiles < j (complete, see above): scale it in place.
 #pragma unroll

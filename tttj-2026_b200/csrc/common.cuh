@@ -221,6 +221,39 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
       : "memory");
 }
 
+// Warp-wide forms of mma / commit: the whole (converged) warp executes them with
+// warp-uniform operands and one elected lane issues.  Issuing from a one-lane branch
+// makes every operand a per-thread value that must be moved to uniform registers for
+// each MMA; with descriptors that change every step this cost ~40% of the tensor
+// core's rate in a microbenchmark of the attention's MMA mix.
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_warp(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // CTA pairs (cluster of 2) for the cta_group::2 MMA: the even CTA of a pair issues
 // M=256 MMAs that read A and B halves from both CTAs' shared memory and write each
@@ -459,6 +492,28 @@ __device__ __forceinline__ unsigned long long mul2p(unsigned long long a, unsign
   unsigned long long d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+
+// 2^x for a pair of x <= 8 on the FMA pipe instead of the MUFU (for kernels whose
+// exponentials outnumber what the MUFU issues).  Cody-Waite style range reduction
+// x = j + f, j = rint(x) (the 1.5 * 2^23 rounding constant), f in [-0.5, 0.5], then a
+// degree-4 polynomial for 2^f whose coefficients were fitted for this library by a
+// Remez exchange on the relative error (max relative error 2.7e-6 in fp32 Horner
+// arithmetic), and 2^j added into the exponent field.  x is clamped to >= -126 so the
+// exponent never wraps (the result is then ~1e-38, 0 after any fp16 conversion).
+__device__ __forceinline__ float2 exp2_fma2(float2 x) {
+  const unsigned long long xm = pk2(fmaxf(x.x, -126.0f), fmaxf(x.y, -126.0f));
+  const unsigned long long magic = pk2(12582912.0f, 12582912.0f);
+  const unsigned long long t = add2p(xm, magic);  // rint(x) in the low mantissa bits
+  const unsigned long long f = sub2p(xm, sub2p(t, magic));
+  unsigned long long p = fma2p(f, pk2(9.570102207e-03f, 9.570102207e-03f),
+                               pk2(5.591785908e-02f, 5.591785908e-02f));
+  p = fma2p(f, p, pk2(2.402474433e-01f, 2.402474433e-01f));
+  p = fma2p(f, p, pk2(6.931217909e-01f, 6.931217909e-01f));
+  p = fma2p(f, p, pk2(9.999992847e-01f, 9.999992847e-01f));
+  const float2 tf = upk2(t), pf = upk2(p);
+  return make_float2(__int_as_float(__float_as_int(pf.x) + (__float_as_int(tf.x) << 23)),
+                     __int_as_float(__float_as_int(pf.y) + (__float_as_int(tf.y) << 23)));
 }
 
 // ---------------------------------------------------------------------------

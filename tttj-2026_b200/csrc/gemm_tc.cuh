@@ -9,7 +9,7 @@
 // BaselineTransformerBlock (benchmarks/torch_transformer_benchmark.py:72-75,131-132).
 //
 // CTA = 10 warps: warp 0 issues TMA loads into a STAGES-deep shared-memory ring,
-// warp 1 owns TMEM and one thread issues tcgen05.mma (M=128, N=BN, K=16), warps 2-9
+// warp 1 owns TMEM and issues tcgen05.mma (M=128, N=BN, K=16; one elected lane), warps 2-9
 // drain the double-buffered TMEM accumulator (tcgen05.ld 32x32b) through the
 // epilogue while the next tile's MMAs run.  Two epilogue warps share each TMEM lane
 // quadrant and split the tile's columns.  Each epilogue warp stages a 32x32 output
@@ -174,8 +174,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
-    // A pair's MMAs are issued by its leader only (they cover both CTAs' tiles).
-    if (lane == 0 && (!PAIR || rank == 0)) {
+    // The whole warp runs the loop (waits combined with a vote, so the stage
+    // descriptors stay warp-uniform) and one elected lane issues each MMA / commit:
+    // issued from a one-lane branch, every MMA would first move its operands into
+    // uniform registers.  A pair's MMAs are issued by its leader only.
+    constexpr unsigned FULL = 0xffffffffu;
+    if (!PAIR || rank == 0) {
       constexpr uint32_t idesc = idesc_f16_f32(TM, BN);
       int stage = 0;
       uint32_t phase = 0;
@@ -184,14 +188,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       bool ok = true;
       bool issued_any = false;
       for (int tile = unit; tile < num_tiles && ok; tile += n_units) {
-        if (!mbar_wait(bar_acce + 8 * acc, acc_phase ^ 1u, abort_flag, limit)) {
+        if (!__all_sync(FULL, mbar_wait(bar_acce + 8 * acc, acc_phase ^ 1u, abort_flag, limit))) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kk = 0; kk < k_iters; ++kk) {
-          if (!mbar_wait(bar_full + 8 * stage, phase, abort_flag, limit)) {
+          if (!__all_sync(FULL, mbar_wait(bar_full + 8 * stage, phase, abort_flag, limit))) {
             ok = false;
             break;
           }
@@ -202,18 +206,18 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           for (int j = 0; j < GEMM_BK / 16; ++j) {
             // Advance 16 fp16 (32 B) along K inside the 128-byte swizzle atom.
             if (PAIR)
-              mma_f16_ss_pair(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
-                              (kk | j) != 0 ? 1u : 0u);
+              mma_f16_ss_pair_warp(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j),
+                                   idesc, (kk | j) != 0 ? 1u : 0u);
             else
-              mma_f16_ss(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
-                         (kk | j) != 0 ? 1u : 0u);
+              mma_f16_ss_warp(d_tmem, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), idesc,
+                              (kk | j) != 0 ? 1u : 0u);
           }
           issued_any = true;
           // Frees the stage in both CTAs of a pair.
           if (PAIR)
-            mma_commit_pair_mc(bar_empty + 8 * stage, 0x3);
+            mma_commit_pair_mc_warp(bar_empty + 8 * stage, 0x3);
           else
-            mma_commit(bar_empty + 8 * stage);
+            mma_commit_warp(bar_empty + 8 * stage);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -221,21 +225,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         if (!ok) break;
         if (PAIR)
-          mma_commit_pair_mc(bar_accf + 8 * acc, 0x3);
+          mma_commit_pair_mc_warp(bar_accf + 8 * acc, 0x3);
         else
-          mma_commit(bar_accf + 8 * acc);
+          mma_commit_warp(bar_accf + 8 * acc);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
       }
       if (!ok) {
-        *abort_flag = 1;
-        report_status(p.status, TTTJ_DEV_TIMEOUT_MMA);
+        if (lane == 0) {
+          *abort_flag = 1;
+          report_status(p.status, TTTJ_DEV_TIMEOUT_MMA);
+        }
         if (issued_any) {
           // Wait for the MMAs already issued before TMEM is released.
           if (PAIR)
-            mma_commit_pair(bar_drain);
+            mma_commit_pair_warp(bar_drain);
           else
-            mma_commit(bar_drain);
+            mma_commit_warp(bar_drain);
           mbar_wait(bar_drain, 0, nullptr, limit);
         }
       }

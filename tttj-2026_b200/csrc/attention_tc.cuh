@@ -8,11 +8,11 @@
 // mask is "key < valid length" and the causal mask compares packed positions.
 //
 // Work item = one (sequence, head, 256 query rows) = two 128-row query tiles.  The CTA
-// is persistent over the longest-first work list and runs 10 warps:
+// is persistent over the longest-first work list and runs 11 warps:
 //   warp 8      TMA: Q tiles (double-buffered across items), K/V tiles (STAGES ring)
-//   warp 9      issues tcgen05.mma (the whole warp runs the loop, one elected lane
-//               issues): S_t = Q_t K_j^T (M=128, N=128, K=hd) into TMEM, and
-//               O_t += P_t V_j with P_t read from TMEM (A operand)
+//   warps 9/10  issue tcgen05.mma for query tile 0 / 1 (the whole warp runs the loop,
+//               one elected lane issues): S_t = Q_t K_j^T (M=128, N=128, K=hd) into
+//               TMEM, and O_t += P_t V_j with P_t read from TMEM (A operand)
 //   warps 0-3   softmax for query tile 0 (one thread = one query row = one TMEM lane)
 //   warps 4-7   softmax for query tile 1
 // P has its own TMEM buffer, so S_t(j+1) is issued as soon as the softmax threads have
@@ -46,7 +46,7 @@ struct AtcSmem {
   static constexpr int STAGES = HD == 64 ? 3 : 4;
   static constexpr int Q_BYTES = 2 * 2 * Q_TILE;  // 2 buffers x 2 tiles
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
-  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 1;
+  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 2;
   static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
   static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + 1024;
   static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_P0 = 256, TMEM_P1 = 320,
@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       mbar_init(bar_q_full + 8 * i, 1);
       // Released by the MMA warp's commit after the item's last Q K^T and by every
       // softmax thread once it copied the item's decoded info out of the slot.
-      mbar_init(bar_q_empty + 8 * i, 1 + 2 * ATC_BM);
+      mbar_init(bar_q_empty + 8 * i, 2 + 2 * ATC_BM);
       mbar_init(bar_s_full + 8 * i, 1);
       mbar_init(bar_p_full + 8 * i, ATC_BM);
       mbar_init(bar_o_full + 8 * i, 1);
@@ -142,9 +142,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_kv_full + 8 * s, 1);
-      mbar_init(bar_kv_empty + 8 * s, 1);
+      mbar_init(bar_kv_empty + 8 * s, 2);  // one arrival per MMA warp
     }
     mbar_init(bar_drain, 1);
+    mbar_init(bar_drain + 8, 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -221,22 +222,30 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           mbar_wait(bar_q_full + 8 * (i & 1), (uint32_t)((i >> 1) & 1), nullptr, limit);
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
-    // The whole warp runs the issue loop (barrier results combined with a vote, item
-    // fields broadcast from lane 0, so descriptors stay warp-uniform); one elected lane
-    // issues each tcgen05.mma / commit.
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers
+    // One issuing warp per query tile, each following only its own tile's events, so
+    // neither tile's MMAs wait for the other tile's softmax (a single issuer serving
+    // both in a fixed order keeps the two softmax warpgroups in lockstep).  The whole
+    // warp runs the loop (barrier results combined with a vote, item fields broadcast
+    // from lane 0, so descriptors stay warp-uniform); one elected lane issues each
+    // tcgen05.mma / commit.  A K/V stage is released by both warps (two arrivals); a
+    // K/V tile a query tile does not use is released after it landed, which keeps the
+    // releases in stage order.
     constexpr unsigned FULL = 0xffffffffu;
+    const int t = warp - 9;
     {
       constexpr uint32_t idesc_s = idesc_f16_f32(ATC_BM, ATC_BN);
       constexpr uint32_t idesc_o = idesc_f16_f32(ATC_BM, HD, 0, 1);
       constexpr uint32_t v_step = HD == 64 ? (2048u >> 4) : (1024u >> 4);  // 16 keys
+      const uint32_t s_col = t == 0 ? SM::TMEM_S0 : SM::TMEM_S1;
+      const uint32_t p_col = t == 0 ? SM::TMEM_P0 : SM::TMEM_P1;
+      const uint32_t o_col = t == 0 ? SM::TMEM_O0 : SM::TMEM_O1;
       bool ok = true;
       bool issued = false;
-      long kvc = 0;             // KV tiles consumed
-      long pc[2] = {0, 0};      // p_full waits per tile
-      long sfc[2] = {0, 0};     // s_free waits per tile
-      long oc[2] = {0, 0};      // o_free waits per tile
+      long kvc = 0;        // KV tiles of all items so far (global count)
+      long kv_waited = -1;  // highest KV tile index whose arrival this warp observed
+      long pc = 0, sfc = 0, oc = 0;  // p_full / s_free / o_free waits
       int k = 0;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
         if (!__all_sync(FULL, mbar_wait(bar, parity, abort_flag, limit))) {
@@ -246,73 +255,71 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         tc_fence_after();
         return true;
       };
+      auto ensure_kv = [&](long idx) -> bool {
+        while (kv_waited < idx) {
+          ++kv_waited;
+          if (!wait(bar_kv_full + 8 * (int)(kv_waited % STAGES), (uint32_t)((kv_waited / STAGES) & 1)))
+            return false;
+        }
+        return true;
+      };
       for (; ok; ++k) {
         const int qb = k & 1;
         if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
         const int n_kv = __shfl_sync(FULL, info[qb].n_kv, 0);
         if (n_kv < 0) break;  // no more items
-        const int wn[2] = {__shfl_sync(FULL, info[qb].n[0], 0), __shfl_sync(FULL, info[qb].n[1], 0)};
-        const uint32_t qaddr[2] = {sQ + (qb * 2) * SM::Q_TILE, sQ + (qb * 2 + 1) * SM::Q_TILE};
-        const uint32_t s_col[2] = {SM::TMEM_S0, SM::TMEM_S1};
-        const uint32_t p_col[2] = {SM::TMEM_P0, SM::TMEM_P1};
-        const uint32_t o_col[2] = {SM::TMEM_O0, SM::TMEM_O1};
-        long kv_waited = kvc - 1;  // highest KV tile index (global count) already waited on
-        auto ensure_kv = [&](long idx) -> bool {
-          while (kv_waited < idx) {
-            ++kv_waited;
-            if (!wait(bar_kv_full + 8 * (int)(kv_waited % STAGES),
-                      (uint32_t)((kv_waited / STAGES) & 1)))
-              return false;
-          }
-          return true;
-        };
-        auto issue_s = [&](int t, long kv_idx) {
+        const int n = __shfl_sync(FULL, info[qb].n[t], 0);
+        const uint32_t qaddr = sQ + (qb * 2 + t) * SM::Q_TILE;
+        auto issue_s = [&](long kv_idx) {
           const uint32_t kaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE;
-          const uint64_t qd = atc_desc_qk<HD>(qaddr[t]);
+          const uint64_t qd = atc_desc_qk<HD>(qaddr);
           const uint64_t kd = atc_desc_qk<HD>(kaddr);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk)
-            mma_f16_ss_warp(tmem + s_col[t], qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk),
-                            idesc_s, kk > 0 ? 1u : 0u);
+            mma_f16_ss_warp(tmem + s_col, qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk), idesc_s,
+                            kk > 0 ? 1u : 0u);
           mma_commit_warp(bar_s_full + 8 * t);
           issued = true;
         };
-        auto issue_pv = [&](int t, long kv_idx, bool accumulate) {
+        auto issue_pv = [&](long kv_idx, bool accumulate) {
           const uint32_t vaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE + SM::KV_TILE;
           const uint64_t vd = atc_desc_v<HD>(vaddr);
 #pragma unroll
           for (int kk = 0; kk < ATC_BN / 16; ++kk)
-            mma_f16_ts_warp(tmem + o_col[t], tmem + p_col[t] + (uint32_t)(kk * 8),
+            mma_f16_ts_warp(tmem + o_col, tmem + p_col + (uint32_t)(kk * 8),
                             vd + (uint64_t)(kk * v_step), idesc_o, (accumulate || kk > 0) ? 1u : 0u);
           mma_commit_warp(bar_pv_done + 8 * t);
           issued = true;
         };
-        if (!ensure_kv(kvc)) break;
-        issue_s(0, kvc);
-        if (wn[1] > 0) issue_s(1, kvc);
+        if (n > 0) {
+          if (!ensure_kv(kvc)) break;
+          issue_s(kvc);
+        }
         for (int j = 0; j < n_kv && ok; ++j) {
           const long kv_j = kvc + j;
-          // Next scores first: each tile's S buffer is free once its softmax threads have
-          // read S(j) (s_free), long before they publish P(j).
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j + 1 >= wn[t]) continue;
-            if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc[t]++ & 1))) break;
-            if (!ensure_kv(kv_j + 1)) break;
-            issue_s(t, kv_j + 1);
-          }
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j >= wn[t]) continue;
-            if (!wait(bar_p_full + 8 * t, (uint32_t)(pc[t]++ & 1))) break;
+          if (j < n) {
+            // Next scores as soon as the softmax threads have read S(j) (s_free).
+            if (j + 1 < n) {
+              if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc++ & 1))) break;
+              if (!ensure_kv(kv_j + 1)) break;
+              issue_s(kv_j + 1);
+            }
+            if (!wait(bar_p_full + 8 * t, (uint32_t)(pc++ & 1))) break;
             // The first P V of an item overwrites O: the previous item's O must be read.
-            if (j == 0 && !wait(bar_o_free + 8 * t, (uint32_t)(oc[t]++ & 1) ^ 1u)) break;
-            issue_pv(t, kv_j, j > 0);
-            if (j + 1 == wn[t]) mma_commit_warp(bar_o_full + 8 * t);
+            if (j == 0 && !wait(bar_o_free + 8 * t, (uint32_t)(oc++ & 1) ^ 1u)) break;
+            issue_pv(kv_j, j > 0);
+            if (j + 1 == n) mma_commit_warp(bar_o_full + 8 * t);
+            mma_commit_warp(bar_kv_empty + 8 * (int)(kv_j % STAGES));
+          } else {
+            // Not used by this query tile: release it once it has landed.
+            if (!ensure_kv(kv_j)) break;
+            if (lane == 0) mbar_arrive(bar_kv_empty + 8 * (int)(kv_j % STAGES));
+            __syncwarp();
           }
-          if (!ok) break;
-          mma_commit_warp(bar_kv_empty + 8 * (int)(kv_j % STAGES));
         }
+        if (!ok) break;
         kvc += n_kv;
-        if (ok) mma_commit_warp(bar_q_empty + 8 * qb);
+        mma_commit_warp(bar_q_empty + 8 * qb);
       }
       if (!ok) {
         if (lane == 0) {
@@ -320,8 +327,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           report_status(p.status, TTTJ_DEV_TIMEOUT_ATTN);
         }
         if (issued) {
-          mma_commit_warp(bar_drain);
-          mbar_wait(bar_drain, 0, nullptr, limit);
+          mma_commit_warp(bar_drain + 8 * t);
+          mbar_wait(bar_drain + 8 * t, 0, nullptr, limit);
         }
       }
     }

@@ -84,7 +84,8 @@ struct AtcParams {
 constexpr int ATC_BM = 128;         // query rows per tile = TMEM lanes
 constexpr int ATC_BN = 128;         // keys per KV tile
 constexpr int ATC_ITEM_ROWS = 256;  // two query tiles per work item
-constexpr int ATC_THREADS = 320;    // warps 0-3 / 4-7 softmax tile 0 / 1, warp 8 TMA, warp 9 MMA
+// warps 0-3 / 4-7 softmax tile 0 / 1, warp 8 TMA, warps 9 / 10 MMA for tile 0 / 1
+constexpr int ATC_THREADS = 352;
 
 struct TokenPlan {
   int* seq_len;     // [B]

@@ -48,7 +48,10 @@ struct AtcSmem {
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
   static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 2;
   static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
-  static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + 1024;
+  // Epilogue staging per softmax warp: its 32 output rows x HD fp16.
+  static constexpr int EPI_ROW = HD * 2;
+  static constexpr int EPI_BYTES = 8 * 32 * EPI_ROW;
+  static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + EPI_BYTES + 1024;
   static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_P0 = 256, TMEM_P1 = 320,
                             TMEM_O0 = 384, TMEM_O1 = 448;
 };
@@ -120,6 +123,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   // Decoded work item per Q buffer, written by the loader before it arms q_full, read
   // by the MMA and softmax warps after they waited on q_full (one global decode per item).
   AtcItem* info = reinterpret_cast<AtcItem*>(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8 + 16);
+  const uint32_t sEpi = smem_u32(smem + SM::Q_BYTES + SM::KV_BYTES + SM::NBAR * 8 + 16 + SM::INFO_BYTES);
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -487,22 +491,49 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       }
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __half* dst = p.ctx + (size_t)(w.seq0 + qrow) * D + w.h * HD;
+      // The warp's 32 rows go through shared memory so that the stores to ctx cover
+      // whole row segments (16-byte chunk j of row r staged at slot j ^ (r % NCH));
+      // rows past the sequence end are never written (they belong to the next
+      // sequence of the packed layout).
+      constexpr int NCH = SM::EPI_ROW / 16;  // 16-byte chunks per row
+      const uint32_t stage = sEpi + (uint32_t)(warp * 32 * SM::EPI_ROW);
 #pragma unroll
       for (int c = 0; c < HD / 32; ++c) {
         uint32_t o[32];
         tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
         tmem_wait_ld();
-        if (qrow < w.len && w.seq0 + qrow < p.rows_max) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
-          for (int q = 0; q < 4; ++q)
-            d4[q] = make_uint4(pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
-                               pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
-                               pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
-                               pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        for (int q = 0; q < 4; ++q) {
+          const int j = c * 4 + q;  // 8 halves = one 16-byte chunk
+          const uint32_t a = stage + (uint32_t)(lane * SM::EPI_ROW + ((j ^ (lane % NCH)) << 4));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                       "r"(pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv)),
+                       "r"(pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv)),
+                       "r"(pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv)),
+                       "r"(pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv))
+                       : "memory");
         }
       }
+      __syncwarp();
+      {
+        constexpr int RPI = 32 / NCH;  // rows per store instruction
+        const int j = lane % NCH;
+        const int q0row = w.q0 + t * ATC_BM + quad * 32;  // first query row of this warp
+#pragma unroll
+        for (int it = 0; it < 32 / RPI; ++it) {
+          const int rr = it * RPI + lane / NCH;
+          const uint32_t a = stage + (uint32_t)(rr * SM::EPI_ROW + ((j ^ (rr % NCH)) << 4));
+          uint4 v;
+          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                       : "r"(a)
+                       : "memory");
+          const int qr = q0row + rr;
+          if (qr < w.len && w.seq0 + qr < p.rows_max)
+            *reinterpret_cast<uint4*>(p.ctx + (size_t)(w.seq0 + qr) * D + w.h * HD + j * 8) = v;
+        }
+      }
+      __syncwarp();
       tc_fence_before();
       mbar_arrive(bar_o_free + 8 * t);
     }

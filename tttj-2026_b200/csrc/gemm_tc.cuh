@@ -115,6 +115,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // The weights do not depend on the previous kernel: while this CTA waits for it
+  // (programmatic dependent launch starts it early), ask L2 for the B boxes of the
+  // CTA's first tile.
+  if (warp == 0 && lane == 0) {
+    const int n_blk0 = unit % n_tiles;
+    const int b_row0 = n_blk0 * BN + (int)rank * (BN / CTAS);
+    for (int kk = 0; kk < k_iters; ++kk) tma_prefetch_l2_2d(&tmB, kk * GEMM_BK, b_row0);
+  }
   griddep_wait();
   griddep_launch();
   const int rows = p.rows_dev ? min(*p.rows_dev, p.rows_max) : p.rows_max;

@@ -50,6 +50,26 @@ CONFIGS = {
 }
 # Bounded CPU sample per config: (sequences, layers) of the workload per step.
 CPU_SAMPLE = {"C1": (2, 2), "C2": (1, 4), "C3": (4, 6), "C4": (1, 1), "C5": (1, 24)}
+
+# The reference's own 14 cases (optimized_transformer.py:22-42: F = D, causal, 4 layers,
+# 2 for case 14) as workloads R1..R14, all tokens valid and fp16 as in the reference's
+# published timings (benchmarks/benchmark_compile_comparison.py:146-160), with those
+# published H200 forward times (README.md:164-177) for vs_baseline.
+REF_CASES = {
+    1: (64, 128, 128, 4), 2: (1, 128, 128, 4), 3: (4, 128, 128, 4), 4: (16, 128, 128, 4),
+    5: (128, 128, 128, 4), 6: (10000, 128, 128, 4), 7: (64, 128, 32, 4), 8: (64, 128, 1024, 4),
+    9: (64, 128, 128, 1), 10: (64, 128, 128, 2), 11: (64, 128, 128, 16), 12: (64, 32, 128, 4),
+    13: (64, 1024, 128, 4), 14: (32, 100000, 1024, 16),
+}
+PUBLISHED_H200_MS = {
+    1: 0.169280, 2: 0.114272, 3: 0.109408, 4: 0.109664, 5: 0.262880, 6: 12.374400,
+    7: 0.095456, 8: 1.065472, 9: 0.158224, 10: 0.155680, 11: 0.220128, 12: 0.104352,
+    13: 4.443712, 14: 2927.799072,
+}
+for _n, (_b, _s, _d, _h) in REF_CASES.items():
+    CONFIGS[f"R{_n}"] = (_b, _s, _d, _h, _d, 2 if _n == 14 else 4, True, "float16", (_s, _s))
+    # One sequence, one layer per CPU rep; a 100k-token sequence is out of reach.
+    CPU_SAMPLE[f"R{_n}"] = None if _n == 14 else (1, 1)
 METRIC = "forward tokens/sec"
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
@@ -60,7 +80,7 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="C2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="C2", choices=list(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -70,8 +90,14 @@ def parse_args(argv=None):
 
 def workload_desc(name: str) -> str:
     B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
-    mask = "mask=None" if lens is None else f"prefix mask len~U[{lens[0]},{lens[1]}]"
-    return (f"{name}: L{L} D{D} H{H} hd{D // H} F{F} B{B} S{S} "
+    if lens is None:
+        mask = "mask=None"
+    elif lens[0] == lens[1] == S:
+        mask = "all-valid mask"
+    else:
+        mask = f"prefix mask len~U[{lens[0]},{lens[1]}]"
+    case = f" (reference case {name[1:]})" if name.startswith("R") else ""
+    return (f"{name}{case}: L{L} D{D} H{H} hd{D // H} F{F} B{B} S{S} "
             f"{'causal' if causal else 'non-causal'}, {mask}, {dt}")
 
 
@@ -206,6 +232,8 @@ def cpu_oracle_rate(name: str, seed: int, seconds: float, threads: int):
 
     torch.set_num_threads(threads)
     B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    if CPU_SAMPLE[name] is None:
+        return None, "no bounded CPU sample for this workload", None
     n_seq, n_layers = CPU_SAMPLE[name]
     full = tb.TransformerConfig(B, S, D, H, F, L, causal)
     torch.manual_seed(seed)
@@ -240,6 +268,11 @@ def run_reference(args, rank: int, world: int):
     torch.set_num_threads(threads)
     name = args.config
     B, S, D, H, F, L, causal, dt, lens = CONFIGS[name]
+    if CPU_SAMPLE[name] is None:
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"{name}: one CPU forward of a {S}-token sequence exceeds the bench's time bound"}),
+              flush=True)
+        return 0
     n_seq, n_layers = CPU_SAMPLE[name]
 
     import optimized_transformer  # noqa: F401
@@ -438,12 +471,17 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     if world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
         cval, sample, _ = cpu_oracle_rate(name, args.seed, args.cpu_seconds, threads)
-        cpu = {"value": cval, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+        if cval is not None:
+            cpu = {"value": cval, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
 
+    vs_baseline = None
+    if name.startswith("R") and world == 1:
+        # Published H200 forward time of the same case (tokens/s = B*S / time).
+        vs_baseline = value / (tokens / (PUBLISHED_H200_MS[int(name[1:])] * 1e-3))
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": vs_baseline, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": workload_desc(name), "global_batch": world * B, "seq_len": S,
                    "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
                    "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",

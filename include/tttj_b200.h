@@ -76,8 +76,9 @@ const char* tttj_last_error(void);
 /* Library version string. */
 const char* tttj_version(void);
 
-/* Check a configuration against what the kernels support (head_dim 32 or 64,
- * d_model and ffn_dim multiples of 64, ...).  Mirrors case_number_for_model's
+/* Check a configuration against what the kernels support (head_dim a multiple of 8 up
+ * to 256 -- heads narrower than 32 run padded to 32 columns inside the workspace --,
+ * d_model and ffn_dim multiples of 32, ...).  Mirrors case_number_for_model's
  * ValueError contract (optimized_transformer.py:45-66): TTTJ_ERR_INVALID + message. */
 int tttj_validate_config(const tttj_config* cfg);
 
@@ -171,7 +172,8 @@ int tttj_layernorm(const void* in, void* out, int rows, int d, const float* gamm
 
 /* Fused multi-head attention over the packed valid-token layout.
  *   qkv  [qkv_rows, 3*d_model] fp16: valid tokens of sequence 0, then 1, ... in token
- *        order; columns q | k | v with head h at h*head_dim.  qkv_rows (>= the number
+ *        order; columns q | k | v with head h at h*head_dim; head_dim = d_model /
+ *        num_heads must be 32, 64, 128 or 256.  qkv_rows (>= the number
  *        of valid tokens Tv) is the number of rows allocated in qkv and ctx.
  *   ctx  [qkv_rows, d_model] fp16 output (rows of valid tokens are written).
  *   valid_mask [batch, seq_len] bytes or NULL (all valid) -- defines the packing.

@@ -40,5 +40,9 @@ _pkg = _register_package()
 make_optimized_transformer = _pkg.make_optimized_transformer
 TransformerConfig = _pkg.TransformerConfig
 TransformerParameters = _pkg.TransformerParameters
+IMPLEMENTED_CASES = _pkg.IMPLEMENTED_CASES
+IMPLEMENTED_CASE_LAYERS = _pkg.IMPLEMENTED_CASE_LAYERS
+case_number_for_model = _pkg.case_number_for_model
 
-__all__ = ["make_optimized_transformer", "TransformerConfig", "TransformerParameters"]
+__all__ = ["make_optimized_transformer", "TransformerConfig", "TransformerParameters",
+           "IMPLEMENTED_CASES", "IMPLEMENTED_CASE_LAYERS", "case_number_for_model"]

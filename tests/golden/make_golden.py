@@ -38,6 +38,16 @@ CASES = {
     "causal_nomask": (2, 33, 64, 1, 128, 1, True, 31, 32, None),
     # a fully padded sequence next to a valid one
     "empty_sequence": (2, 24, 64, 2, 192, 2, False, 41, 42, [0, 20]),
+    # head widths of the reference's own cases (optimized_transformer.py:22-42),
+    # F = D and causal like them, at small batch and sequence:
+    # case 7 (d_model 32, 4 heads of 8)
+    "case7_hd8": (2, 48, 32, 4, 32, 2, True, 51, 52, [48, 30]),
+    # case 11 (d_model 128, 16 heads of 8)
+    "case11_hd8_h16": (2, 40, 128, 16, 128, 1, True, 81, 82, [40, 9]),
+    # case 9 (one head of 128)
+    "case9_hd128": (2, 140, 128, 1, 128, 2, True, 61, 62, [140, 25]),
+    # case 8's head width 256 (2 heads at d_model 512 keep the fixture small)
+    "case8_hd256": (2, 36, 512, 2, 512, 1, True, 71, 72, [36, 20]),
 }
 
 
@@ -92,11 +102,16 @@ def make_inputs(B, S, D, input_seed, lengths):
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", type=Path, required=True)
+    ap.add_argument("--only", nargs="+", choices=sorted(CASES),
+                    help="regenerate these cases only (the index keeps the others)")
     args = ap.parse_args(argv)
     ref = load_reference(args.reference)
     torch.set_num_threads(8)
-    index = {}
+    index_path = HERE / "index.json"
+    index = json.loads(index_path.read_text()) if args.only and index_path.exists() else {}
     for name, (B, S, D, H, F, L, causal, mseed, iseed, lengths) in CASES.items():
+        if args.only and name not in args.only:
+            continue
         cfg = ref.TransformerConfig(B, S, D, H, F, L, causal)
         torch.manual_seed(mseed)
         model = ref.BaselineTransformer(cfg).eval()
@@ -123,7 +138,7 @@ def main(argv=None) -> int:
             "out_abs_sum": float(out.abs().sum()),
         }
         print(f"{name}: out |sum| = {index[name]['out_abs_sum']:.6f}")
-    (HERE / "index.json").write_text(json.dumps(index, indent=1, sort_keys=True) + "\n")
+    index_path.write_text(json.dumps(index, indent=1, sort_keys=True) + "\n")
     return 0
 
 

@@ -47,9 +47,9 @@ def test_baseline_configs_are_supported(name):
 
 @pytest.mark.parametrize(
     "shape,msg",
-    [((2, 128, 512, 4, 512, 2, True), "head_dim=128"),  # reference case 13-like hd
-     ((2, 128, 32, 4, 32, 4, True), "head_dim=8"),      # reference case 7 (hd 8)
-     ((2, 128, 96, 3, 128, 1, False), "multiples of 64"),
+    [((2, 128, 1024, 2, 1024, 2, True), "head_dim=512"),  # wider than 256
+     ((2, 128, 48, 4, 64, 4, True), "head_dim=12"),        # not a multiple of 8
+     ((2, 128, 80, 2, 128, 1, False), "multiples of 32"),
      ((2, 128, 256, 3, 1024, 1, False), "divisible")],
 )
 def test_unsupported_configs_raise_value_error(shape, msg):

@@ -112,12 +112,12 @@ def _attention_ref(qkv, lengths, H, causal):
     return torch.cat(outs, 0)
 
 
-@pytest.mark.parametrize("hd", [32, 64])
+@pytest.mark.parametrize("hd", [32, 64, 128, 256])
 @pytest.mark.parametrize("causal", [False, True])
 @pytest.mark.parametrize("lengths,S", [([128], 128), ([1, 64, 65, 200, 0, 127], 200),
                                        ([513, 1000, 7], 1000), ([300, 300], 300)])
 def test_attention_matches_torch(hd, causal, lengths, S):
-    H = 4 if hd == 64 else 8
+    H = {32: 8, 64: 4, 128: 2, 256: 1}[hd]
     D = H * hd
     B = len(lengths)
     mask = torch.arange(S, device=DEV)[None, :] < torch.tensor(lengths, device=DEV)[:, None]

@@ -23,6 +23,10 @@ cudaError_t attention_tc_launch(const CUtensorMap& tm, const AtcParams& p, int h
     return causal ? launch_tc<64, true>(tm, p, grid, stream) : launch_tc<64, false>(tm, p, grid, stream);
   if (head_dim == 32)
     return causal ? launch_tc<32, true>(tm, p, grid, stream) : launch_tc<32, false>(tm, p, grid, stream);
+  if (head_dim == 128)
+    return causal ? launch_tc<128, true>(tm, p, grid, stream) : launch_tc<128, false>(tm, p, grid, stream);
+  if (head_dim == 256)
+    return causal ? launch_tc<256, true>(tm, p, grid, stream) : launch_tc<256, false>(tm, p, grid, stream);
   return cudaErrorInvalidValue;
 }
 

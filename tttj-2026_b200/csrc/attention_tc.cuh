@@ -7,8 +7,9 @@
 // probs @ v (:112).  Packing keeps token order inside a sequence, so the key-padding
 // mask is "key < valid length" and the causal mask compares packed positions.
 //
-// Work item = one (sequence, head, 256 query rows) = two 128-row query tiles.  The CTA
-// is persistent over the longest-first work list and runs 11 warps:
+// Work item = one (sequence, head, NT x 128 query rows) = NT 128-row query tiles (NT = 2,
+// or 1 at head_dim 256).  The CTA is persistent over the longest-first work list and runs
+// 11 warps:
 //   warp 8      TMA: Q tiles (double-buffered across items), K/V tiles (STAGES ring)
 //   warps 9/10  issue tcgen05.mma for query tile 0 / 1 (the whole warp runs the loop,
 //               one elected lane issues): S_t = Q_t K_j^T (M=128, N=128, K=hd) into
@@ -24,8 +25,17 @@
 // P V has read the P buffer (pv_done), writes P as packed fp16 and signals the MMA warp
 // (p_full).  At the end of an item it normalises O by the row sum and stores the rows.
 //
-// TMEM (512 columns): S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
-//                     O0 [384,384+hd) O1 [448,448+hd).
+// TMEM (512 columns), head_dim <= 64: S0 [0,128) S1 [128,256) P0 [256,320)
+// P1 [320,384) O0 [384,384+hd) O1 [448,448+hd).
+//
+// head_dim 128 / 256: the O accumulators take 256 columns, so P has no buffer of its
+// own: the softmax writes P_t over the first 64 columns of S_t, and the MMA warp issues
+// the next S_t into that buffer only after P_t V has completed (it waits on pv_done; the
+// tcgen05 ordering rules do not order two MMAs with different accumulators).  Then
+// s_full also tells the softmax that the previous P V is done, so it needs neither
+// s_free nor pv_done.  head_dim 128: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// head_dim 256 (NT = 1): S0 [0,128) O0 [256,512).  Q/K/V tiles of head_dim >= 64 are
+// moved as head_dim/64 boxes of 64 columns (one 128-byte swizzle atom wide each).
 //
 // Every wait is bounded (TTTJ wait limit); on a timeout the role records
 // TTTJ_DEV_TIMEOUT_ATTN in the status word, raises the CTA abort flag and unwinds.
@@ -41,19 +51,29 @@ namespace tttj {
 
 template <int HD>
 struct AtcSmem {
+  static_assert(HD == 32 || HD == 64 || HD == 128 || HD == 256, "head_dim layout");
+  static constexpr int NT = HD == 256 ? 1 : 2;   // query tiles per work item
+  static constexpr bool P_ALIAS = HD >= 128;     // P written over its S buffer
+  static constexpr int QBUF = HD >= 128 ? 1 : 2;  // Q buffers (items in flight)
+  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? 3 : HD == 128 ? 2 : 1;
+  static constexpr int BOX_COLS = HD < 64 ? HD : 64;  // TMA box width (one swizzle atom)
+  static constexpr int NBOX = HD / BOX_COLS;
+  static constexpr int BOX_BYTES = ATC_BM * BOX_COLS * 2;
   static constexpr int Q_TILE = ATC_BM * HD * 2;
   static constexpr int KV_TILE = ATC_BN * HD * 2;
-  static constexpr int STAGES = HD == 64 ? 3 : 4;
-  static constexpr int Q_BYTES = 2 * 2 * Q_TILE;  // 2 buffers x 2 tiles
+  static constexpr int Q_BYTES = QBUF * NT * Q_TILE;
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
   static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 2;
   static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
-  // Epilogue staging per softmax warp: its 32 output rows x HD fp16.
+  // Epilogue staging per softmax warp: its 32 output rows x HD fp16 (head_dim <= 64;
+  // wider heads store straight from registers).
+  static constexpr bool STAGED_EPI = HD <= 64;
   static constexpr int EPI_ROW = HD * 2;
-  static constexpr int EPI_BYTES = 8 * 32 * EPI_ROW;
+  static constexpr int EPI_BYTES = STAGED_EPI ? 8 * 32 * EPI_ROW : 0;
   static constexpr int TOTAL = Q_BYTES + KV_BYTES + NBAR * 8 + 16 + INFO_BYTES + EPI_BYTES + 1024;
-  static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128, TMEM_P0 = 256, TMEM_P1 = 320,
-                            TMEM_O0 = 384, TMEM_O1 = 448;
+  static constexpr uint32_t TMEM_S0 = 0, TMEM_S1 = 128;
+  static constexpr uint32_t TMEM_P0 = P_ALIAS ? TMEM_S0 : 256, TMEM_P1 = P_ALIAS ? TMEM_S1 : 320;
+  static constexpr uint32_t TMEM_O0 = HD <= 64 ? 384 : 256, TMEM_O1 = HD <= 64 ? 448 : 384;
 };
 
 struct AtcItem {
@@ -64,13 +84,13 @@ struct AtcItem {
 };
 static_assert(sizeof(AtcItem) <= 64, "item info slot is 64 bytes");
 
-template <bool CAUSAL>
+template <bool CAUSAL, int NT>
 __device__ __forceinline__ AtcItem atc_decode(const AtcParams& p, int it) {
   AtcItem w;
   const int2 e = p.items[it];
   w.b = e.x;
   w.h = e.y & 0xff;
-  w.q0 = (e.y >> 8) * ATC_ITEM_ROWS;
+  w.q0 = (e.y >> 8) * (NT * ATC_BM);
   w.seq0 = p.seq_off[w.b];
   w.len = p.seq_off[w.b + 1] - w.seq0;
 #pragma unroll
@@ -78,21 +98,29 @@ __device__ __forceinline__ AtcItem atc_decode(const AtcParams& p, int it) {
     const int r0 = w.q0 + t * ATC_BM;
     const int end = CAUSAL ? min(w.len, r0 + ATC_BM) : w.len;
     w.kv_end[t] = end;
-    w.n[t] = (r0 < w.len) ? (end + ATC_BN - 1) / ATC_BN : 0;
+    w.n[t] = (t < NT && r0 < w.len) ? (end + ATC_BN - 1) / ATC_BN : 0;
   }
   w.n_kv = max(w.n[0], w.n[1]);
   return w;
 }
 
+// K-major descriptor of head-dim step kk (16 elements) of a Q or K tile stored as
+// NBOX boxes of [128 rows][BOX_COLS].
 template <int HD>
-__device__ __forceinline__ uint64_t atc_desc_qk(uint32_t addr) {
-  return HD == 64 ? desc_kmajor_sw128(addr) : desc_kmajor_sw64(addr);
+__device__ __forceinline__ uint64_t atc_desc_qk(uint32_t tile, int kk) {
+  if constexpr (HD == 32) {
+    return desc_kmajor_sw64(tile) + (uint64_t)(2 * kk);
+  } else {
+    return desc_kmajor_sw128(tile + (uint32_t)((kk >> 2) * AtcSmem<HD>::BOX_BYTES)) +
+           (uint64_t)(2 * (kk & 3));
+  }
 }
 template <int HD>
 __device__ __forceinline__ uint64_t atc_desc_v(uint32_t addr) {
-  // V tile [128 keys][HD] is the B operand (K = keys, N = HD) stored N-contiguous.
-  return HD == 64 ? desc_mnmajor_sw128(addr, AtcSmem<HD>::KV_TILE, 1024)
-                  : desc_mnmajor_sw64(addr, AtcSmem<HD>::KV_TILE, 512);
+  // V tile [128 keys][HD] is the B operand (K = keys, N = HD) stored N-contiguous; the
+  // 64-column boxes are the N atoms (LBO = box bytes), 8-key groups 1024 B apart.
+  return HD == 32 ? desc_mnmajor_sw64(addr, AtcSmem<HD>::KV_TILE, 512)
+                  : desc_mnmajor_sw128(addr, AtcSmem<HD>::BOX_BYTES, 1024);
 }
 
 template <int HD, bool CAUSAL>
@@ -100,6 +128,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const AtcParams p) {
   using SM = AtcSmem<HD>;
   constexpr int STAGES = SM::STAGES;
+  constexpr int NT = SM::NT;
+  constexpr int QBUF = SM::QBUF;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
@@ -128,7 +158,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const int warp = warp_id();
   const int lane = lane_id();
   const uint64_t limit = p.wait_limit_ns;
-  const int D = p.d_model;
+  const int W = p.qkv_width;  // q | k | v column blocks of the qkv rows; ctx row stride
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQKV);
@@ -136,7 +166,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       mbar_init(bar_q_full + 8 * i, 1);
       // Released by the MMA warp's commit after the item's last Q K^T and by every
       // softmax thread once it copied the item's decoded info out of the slot.
-      mbar_init(bar_q_empty + 8 * i, 2 + 2 * ATC_BM);
+      mbar_init(bar_q_empty + 8 * i, NT + NT * ATC_BM);
       mbar_init(bar_s_full + 8 * i, 1);
       mbar_init(bar_p_full + 8 * i, ATC_BM);
       mbar_init(bar_o_full + 8 * i, 1);
@@ -146,7 +176,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bar_kv_full + 8 * s, 1);
-      mbar_init(bar_kv_empty + 8 * s, 2);  // one arrival per MMA warp
+      mbar_init(bar_kv_empty + 8 * s, NT);  // one arrival per MMA warp
     }
     mbar_init(bar_drain, 1);
     mbar_init(bar_drain + 8, 1);
@@ -180,13 +210,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         const bool stop = it >= n_items;
         AtcItem w;
         if (!stop) {
-          w = atc_decode<CAUSAL>(p, it);
+          w = atc_decode<CAUSAL, NT>(p, it);
         } else {
           w.n_kv = -1;
           w.n[0] = w.n[1] = 0;
         }
-        const int qb = k & 1;
-        if (!mbar_wait(bar_q_empty + 8 * qb, ((k >> 1) & 1) ^ 1u, abort_flag, limit)) {
+        const int qb = k % QBUF;
+        if (!mbar_wait(bar_q_empty + 8 * qb, ((k / QBUF) & 1) ^ 1u, abort_flag, limit)) {
           ok = false;
           break;
         }
@@ -198,8 +228,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         const int nq = w.n[1] > 0 ? 2 : 1;
         mbar_arrive_expect_tx(bar_q_full + 8 * qb, nq * SM::Q_TILE);
         for (int t = 0; t < nq; ++t)
-          tma_load_2d(sQ + (qb * 2 + t) * SM::Q_TILE, &tmQKV, bar_q_full + 8 * qb, w.h * HD,
-                      w.seq0 + w.q0 + t * ATC_BM);
+          for (int x = 0; x < SM::NBOX; ++x)
+            tma_load_2d(sQ + (qb * NT + t) * SM::Q_TILE + x * SM::BOX_BYTES, &tmQKV,
+                        bar_q_full + 8 * qb, w.h * HD + x * SM::BOX_COLS, w.seq0 + w.q0 + t * ATC_BM);
         for (int j = 0; j < w.n_kv; ++j, ++kvc) {
           const int st = (int)(kvc % STAGES);
           if (!mbar_wait(bar_kv_empty + 8 * st, (uint32_t)((kvc / STAGES) & 1) ^ 1u, abort_flag,
@@ -209,9 +240,12 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           }
           const uint32_t dst = sKV + st * 2 * SM::KV_TILE;
           mbar_arrive_expect_tx(bar_kv_full + 8 * st, 2 * SM::KV_TILE);
-          tma_load_2d(dst, &tmQKV, bar_kv_full + 8 * st, D + w.h * HD, w.seq0 + j * ATC_BN);
-          tma_load_2d(dst + SM::KV_TILE, &tmQKV, bar_kv_full + 8 * st, 2 * D + w.h * HD,
-                      w.seq0 + j * ATC_BN);
+          for (int x = 0; x < SM::NBOX; ++x) {
+            tma_load_2d(dst + x * SM::BOX_BYTES, &tmQKV, bar_kv_full + 8 * st,
+                        W + w.h * HD + x * SM::BOX_COLS, w.seq0 + j * ATC_BN);
+            tma_load_2d(dst + SM::KV_TILE + x * SM::BOX_BYTES, &tmQKV, bar_kv_full + 8 * st,
+                        2 * W + w.h * HD + x * SM::BOX_COLS, w.seq0 + j * ATC_BN);
+          }
         }
         if (!ok) break;
       }
@@ -222,11 +256,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         for (long j = kvc > STAGES ? kvc - STAGES : 0; j < kvc; ++j)
           mbar_wait(bar_kv_full + 8 * (int)(j % STAGES), (uint32_t)((j / STAGES) & 1), nullptr,
                     limit);
-        for (int i = k > 2 ? k - 2 : 0; i < k; ++i)
-          mbar_wait(bar_q_full + 8 * (i & 1), (uint32_t)((i >> 1) & 1), nullptr, limit);
+        for (int i = k > QBUF ? k - QBUF : 0; i < k; ++i)
+          mbar_wait(bar_q_full + 8 * (i % QBUF), (uint32_t)((i / QBUF) & 1), nullptr, limit);
       }
     }
-  } else if (warp == 9 || warp == 10) {
+  } else if (warp == 9 || (warp == 10 && NT == 2)) {
     // ------------------------------------------------------------ MMA issuers
     // One issuing warp per query tile, each following only its own tile's events, so
     // neither tile's MMAs wait for the other tile's softmax (a single issuer serving
@@ -249,7 +283,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       bool issued = false;
       long kvc = 0;        // KV tiles of all items so far (global count)
       long kv_waited = -1;  // highest KV tile index whose arrival this warp observed
-      long pc = 0, sfc = 0, oc = 0;  // p_full / s_free / o_free waits
+      long pc = 0, sfc = 0, oc = 0, pvc = 0;  // p_full / s_free / o_free / pv_done waits
       int k = 0;
       auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
         if (!__all_sync(FULL, mbar_wait(bar, parity, abort_flag, limit))) {
@@ -268,20 +302,18 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         return true;
       };
       for (; ok; ++k) {
-        const int qb = k & 1;
-        if (!wait(bar_q_full + 8 * qb, (k >> 1) & 1)) break;
+        const int qb = k % QBUF;
+        if (!wait(bar_q_full + 8 * qb, (k / QBUF) & 1)) break;
         const int n_kv = __shfl_sync(FULL, info[qb].n_kv, 0);
         if (n_kv < 0) break;  // no more items
         const int n = __shfl_sync(FULL, info[qb].n[t], 0);
-        const uint32_t qaddr = sQ + (qb * 2 + t) * SM::Q_TILE;
+        const uint32_t qaddr = sQ + (qb * NT + t) * SM::Q_TILE;
         auto issue_s = [&](long kv_idx) {
           const uint32_t kaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE;
-          const uint64_t qd = atc_desc_qk<HD>(qaddr);
-          const uint64_t kd = atc_desc_qk<HD>(kaddr);
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk)
-            mma_f16_ss_warp(tmem + s_col, qd + (uint64_t)(2 * kk), kd + (uint64_t)(2 * kk), idesc_s,
-                            kk > 0 ? 1u : 0u);
+            mma_f16_ss_warp(tmem + s_col, atc_desc_qk<HD>(qaddr, kk), atc_desc_qk<HD>(kaddr, kk),
+                            idesc_s, kk > 0 ? 1u : 0u);
           mma_commit_warp(bar_s_full + 8 * t);
           issued = true;
         };
@@ -303,7 +335,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           const long kv_j = kvc + j;
           if (j < n) {
             // Next scores as soon as the softmax threads have read S(j) (s_free).
-            if (j + 1 < n) {
+            if (!SM::P_ALIAS && j + 1 < n) {
               if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc++ & 1))) break;
               if (!ensure_kv(kv_j + 1)) break;
               issue_s(kv_j + 1);
@@ -314,6 +346,17 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
             issue_pv(kv_j, j > 0);
             if (j + 1 == n) mma_commit_warp(bar_o_full + 8 * t);
             mma_commit_warp(bar_kv_empty + 8 * (int)(kv_j % STAGES));
+            if (SM::P_ALIAS) {
+              // The next S of this tile (S(j+1), or S(0) of the next item) overwrites
+              // P(j): P V(j) must have completed.  Every P V is waited for here, in
+              // order, so completion pvc of pv_done is unambiguous.
+              if (!wait(bar_pv_done + 8 * t, (uint32_t)(pvc & 1))) break;
+              if (j + 1 < n) {
+                if (!ensure_kv(kv_j + 1)) break;
+                issue_s(kv_j + 1);
+              }
+            }
+            ++pvc;
           } else {
             // Not used by this query tile: release it once it has landed.
             if (!ensure_kv(kv_j)) break;
@@ -336,7 +379,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
       }
     }
-  } else {
+  } else if (warp < 4 * NT) {
     // ------------------------------------------------------------ softmax, warps 0-7
     const int t = warp >> 2;             // query tile of this warpgroup
     const int quad = warp & 3;           // TMEM lane quadrant = rows 32*quad..
@@ -351,8 +394,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     bool ok = true;
     int k = 0;
     for (; ok; ++k) {
-      const int qb = k & 1;
-      if (!mbar_wait(bar_q_full + 8 * qb, (uint32_t)((k >> 1) & 1), abort_flag, limit)) {
+      const int qb = k % QBUF;
+      if (!mbar_wait(bar_q_full + 8 * qb, (uint32_t)((k / QBUF) & 1), abort_flag, limit)) {
         ok = false;
         break;
       }
@@ -381,7 +424,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
         tmem_wait_ld();
         // The scores are in registers: the S buffer may take the next tile's scores.
-        if (j + 1 < n) {
+        if (!SM::P_ALIAS && j + 1 < n) {
           tc_fence_before();
           mbar_arrive(bar_s_free + 8 * t);
         }
@@ -449,7 +492,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         // number pv_before + j - 1 of pv_done.  P V(j) cannot exist yet, and completion
         // j - 2 (or the previous item's last, via o_full) was observed already, so the
         // parity is unambiguous.)  At j == 0 the previous item's o_full covered it.
-        if (j > 0) {
+        // With P written over S (head_dim >= 128), s_full(j) already implies it.
+        if (!SM::P_ALIAS && j > 0) {
           if (!mbar_wait(bar_pv_done + 8 * t, (uint32_t)((pv_before + j - 1) & 1), abort_flag,
                          limit)) {
             ok = false;
@@ -491,46 +535,68 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       }
       tc_fence_after();
       const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      // The warp's 32 rows go through shared memory so that the stores to ctx cover
-      // whole row segments (16-byte chunk j of row r staged at slot j ^ (r % NCH));
-      // rows past the sequence end are never written (they belong to the next
-      // sequence of the packed layout).
-      constexpr int NCH = SM::EPI_ROW / 16;  // 16-byte chunks per row
-      const uint32_t stage = sEpi + (uint32_t)(warp * 32 * SM::EPI_ROW);
+      if constexpr (SM::STAGED_EPI) {
+        // The warp's 32 rows go through shared memory so that the stores to ctx cover
+        // whole row segments (16-byte chunk j of row r staged at slot j ^ (r % NCH));
+        // rows past the sequence end are never written (they belong to the next
+        // sequence of the packed layout).
+        constexpr int NCH = SM::EPI_ROW / 16;  // 16-byte chunks per row
+        const uint32_t stage = sEpi + (uint32_t)(warp * 32 * SM::EPI_ROW);
 #pragma unroll
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
-        tmem_wait_ld();
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
+          tmem_wait_ld();
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int j = c * 4 + q;  // 8 halves = one 16-byte chunk
-          const uint32_t a = stage + (uint32_t)(lane * SM::EPI_ROW + ((j ^ (lane % NCH)) << 4));
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
-                       "r"(pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv)),
-                       "r"(pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv)),
-                       "r"(pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv)),
-                       "r"(pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv))
-                       : "memory");
+          for (int q = 0; q < 4; ++q) {
+            const int j = c * 4 + q;  // 8 halves = one 16-byte chunk
+            const uint32_t a = stage + (uint32_t)(lane * SM::EPI_ROW + ((j ^ (lane % NCH)) << 4));
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a),
+                         "r"(pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv)),
+                         "r"(pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv)),
+                         "r"(pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv)),
+                         "r"(pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv))
+                         : "memory");
+          }
         }
-      }
-      __syncwarp();
-      {
-        constexpr int RPI = 32 / NCH;  // rows per store instruction
-        const int j = lane % NCH;
-        const int q0row = w.q0 + t * ATC_BM + quad * 32;  // first query row of this warp
+        __syncwarp();
+        {
+          constexpr int RPI = 32 / NCH;  // rows per store instruction
+          const int j = lane % NCH;
+          const int q0row = w.q0 + t * ATC_BM + quad * 32;  // first query row of this warp
 #pragma unroll
-        for (int it = 0; it < 32 / RPI; ++it) {
-          const int rr = it * RPI + lane / NCH;
-          const uint32_t a = stage + (uint32_t)(rr * SM::EPI_ROW + ((j ^ (rr % NCH)) << 4));
-          uint4 v;
-          asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                       : "r"(a)
-                       : "memory");
-          const int qr = q0row + rr;
-          if (qr < w.len && w.seq0 + qr < p.rows_max)
-            *reinterpret_cast<uint4*>(p.ctx + (size_t)(w.seq0 + qr) * D + w.h * HD + j * 8) = v;
+          for (int it = 0; it < 32 / RPI; ++it) {
+            const int rr = it * RPI + lane / NCH;
+            const uint32_t a = stage + (uint32_t)(rr * SM::EPI_ROW + ((j ^ (rr % NCH)) << 4));
+            uint4 v;
+            asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                         : "r"(a)
+                         : "memory");
+            const int qr = q0row + rr;
+            if (qr < w.len && w.seq0 + qr < p.rows_max)
+              *reinterpret_cast<uint4*>(p.ctx + (size_t)(w.seq0 + qr) * W + w.h * HD + j * 8) = v;
+          }
+        }
+      } else {
+        // Wide heads: each thread stores its own row, 64 bytes per 32 columns.
+        const int qr = w.q0 + t * ATC_BM + row;
+        const bool store = qr < w.len && w.seq0 + qr < p.rows_max;
+        __half* dst = p.ctx + (size_t)(w.seq0 + qr) * W + w.h * HD;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(o_addr + (uint32_t)(c * 32), o);
+          tmem_wait_ld();
+          if (store) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = make_uint4(
+                  pack_half2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                  pack_half2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                  pack_half2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                  pack_half2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+          }
         }
       }
       __syncwarp();

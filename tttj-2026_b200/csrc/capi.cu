@@ -44,6 +44,20 @@ inline size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 constexpr float kLnEps = 1e-5f;  // nn.LayerNorm default (torch_transformer_benchmark.py:128)
 constexpr unsigned long long kWaitLimitNs = TTTJ_WAIT_LIMIT_NS;
 
+// ---------------------------------------------------------------- head layout
+// The attention kernels handle head_dim 32, 64, 128 and 256.  Narrower heads (and
+// widths between those) are padded: the plan's folded QKV weights put head h's
+// q / k / v columns at h * hp .. h * hp + hd - 1 of a layout head of hp columns, whose
+// other columns are zero rows of the weight (so q, k, v and the attention output are
+// zero there), and the out_proj weight gets matching zero columns.  Scores and
+// outputs are unchanged; the softmax scale stays hd^-0.5.
+int layout_hd(int hd) { return hd <= 32 ? 32 : hd <= 64 ? 64 : hd <= 128 ? 128 : 256; }
+int head_dim_of(const tttj_config& c) { return c.d_model / c.num_heads; }
+int layout_hd(const tttj_config& c) { return layout_hd(head_dim_of(c)); }
+// Columns of each of the q | k | v blocks in the workspace (= d_model unless padded).
+size_t qkv_width(const tttj_config& c) { return (size_t)c.num_heads * layout_hd(c); }
+bool heads_padded(const tttj_config& c) { return layout_hd(c) != head_dim_of(c); }
+
 // ---------------------------------------------------------------- weights layout
 size_t field_bytes(const tttj_config& c, int field) {
   const size_t D = c.d_model, F = c.ffn_dim;
@@ -94,32 +108,35 @@ struct WsLayout {
   size_t total;
 };
 
-// Per-layer fold region: Wqkv' [3D, D] fp16, W1' [F, D] fp16, then fp32 vectors
-// bqkv' [3D], colsum_qkv [3D], b1' [F], colsum_1 [F].
+// Per-layer fold region: Wqkv' [3Q, D] fp16 (Q = qkv_width), W1' [F, D] fp16, then
+// fp32 vectors bqkv' [3Q], colsum_qkv [3Q], b1' [F], colsum_1 [F], and for padded heads
+// the out_proj weight with zero columns Wo' [D, Q] fp16.
 struct FoldLayout {
-  size_t wqkv, w1, bqkv, cqkv, b1, c1, total;
+  size_t wqkv, w1, bqkv, cqkv, b1, c1, wo, total;
 };
 // Statistics partials per row produced by a residual GEMM (N = d_model): two column
-// halves per column tile.  The tile width is the widest dividing d_model (the same
-// rule the residual GEMMs use when they fill the machine; 64 always divides).
-int stats_parts(const tttj_config& c) { return 2 * (c.d_model / 64); }  // upper bound
+// halves per column tile (a half past d_model writes zeros).  Tiles are at least 64
+// columns wide, so 2 * ceil(d_model / 64) bounds the count.
+int stats_parts(const tttj_config& c) { return 2 * ((c.d_model + 63) / 64); }  // upper bound
 
 FoldLayout fold_layout(const tttj_config& c) {
-  const size_t D = c.d_model, F = c.ffn_dim;
+  const size_t D = c.d_model, F = c.ffn_dim, Q = qkv_width(c);
   FoldLayout f{};
   size_t o = 0;
-  f.wqkv = o; o += align_up(3 * D * D * 2);
+  f.wqkv = o; o += align_up(3 * Q * D * 2);
   f.w1 = o; o += align_up(F * D * 2);
-  f.bqkv = o; o += align_up(3 * D * 4);
-  f.cqkv = o; o += align_up(3 * D * 4);
+  f.bqkv = o; o += align_up(3 * Q * 4);
+  f.cqkv = o; o += align_up(3 * Q * 4);
   f.b1 = o; o += align_up(F * 4);
   f.c1 = o; o += align_up(F * 4);
+  f.wo = o; o += heads_padded(c) ? align_up(D * Q * 2) : 0;
   f.total = o;
   return f;
 }
 
+// Work items of 128 query rows bound every item size.
 size_t attn_items_max(size_t B, size_t S, size_t H) {
-  return B * H * ((S + ATC_ITEM_ROWS - 1) / ATC_ITEM_ROWS);
+  return B * H * ((S + ATC_BM - 1) / ATC_BM);
 }
 
 // Token-plan part of the workspace (shared by the forward and tttj_attention).
@@ -140,11 +157,12 @@ size_t plan_layout(size_t B, size_t S, size_t H, WsLayout* w) {
 WsLayout ws_layout(const tttj_config& c) {
   WsLayout w{};
   const size_t T = (size_t)c.batch_size * c.seq_len, D = c.d_model, F = c.ffn_dim;
+  const size_t Q = qkv_width(c);
   size_t o = plan_layout(c.batch_size, c.seq_len, c.num_heads, &w);
   w.resid = o; o += align_up(T * D * 4);
   w.x16 = o; o += align_up(T * D * 2);
-  w.qkv = o; o += align_up(T * 3 * D * 2);
-  w.ctx = o; o += align_up(T * D * 2);
+  w.qkv = o; o += align_up(T * 3 * Q * 2);
+  w.ctx = o; o += align_up(T * Q * 2);
   w.hid = o; o += align_up(T * F * 2);
   w.stats = o; o += align_up((size_t)2 * T * stats_parts(c) * 8);
   w.fold_layer = fold_layout(c).total;
@@ -209,14 +227,16 @@ int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, ui
 }
 
 // TMA map + parameters of the tcgen05 attention over a packed qkv buffer of
-// `qkv_rows` rows: boxes of head_dim columns x 128 rows, swizzle = the row width.
+// `qkv_rows` rows with H heads of `hp` layout columns (hd of them real): boxes of
+// min(hp, 64) columns x 128 rows, swizzle = the box row width.
 int build_attention(CUtensorMap* tm, AtcParams* ap, int* grid, const void* qkv, void* ctx,
-                    int qkv_rows, int B, int S, int D, int H, const TokenPlan& tp, int* status,
-                    int num_sms) {
-  const int hd = D / H;
+                    int qkv_rows, int B, int S, int H, int hd, int hp, const TokenPlan& tp,
+                    int* status, int num_sms) {
+  const int width = H * hp;
+  const uint32_t box_cols = hp < 64 ? (uint32_t)hp : 64u;
   int rc = make_tmap_2d(tm, qkv, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (uint64_t)qkv_rows,
-                        (uint64_t)(3 * D), (uint64_t)(3 * D), (uint32_t)hd, ATC_BM,
-                        hd == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+                        (uint64_t)(3 * width), (uint64_t)(3 * width), box_cols, ATC_BM,
+                        box_cols == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
   if (rc) return rc;
   ap->seq_off = tp.seq_off;
   ap->items = tp.items;
@@ -224,11 +244,12 @@ int build_attention(CUtensorMap* tm, AtcParams* ap, int* grid, const void* qkv, 
   ap->work_counter = tp.counters;  // the forward points layer l at counters[l]
   ap->ctx = static_cast<__half*>(ctx);
   ap->rows_max = qkv_rows;
-  ap->d_model = D;
+  ap->qkv_width = width;
   ap->scale_log2 = (1.0f / sqrtf((float)hd)) * 1.4426950408889634f;
   ap->status = status;
   ap->wait_limit_ns = kWaitLimitNs;
-  const long items = (long)B * H * ((S + ATC_ITEM_ROWS - 1) / ATC_ITEM_ROWS);
+  const int item_rows = atc_item_rows(hp);
+  const long items = (long)B * H * ((S + item_rows - 1) / item_rows);
   *grid = (int)(items < num_sms ? items : num_sms);
   return TTTJ_OK;
 }
@@ -244,7 +265,8 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
                int n, int k, int epi, int* status, int num_sms) {
   if (n <= 0 || k <= 0 || rows < 0) return fail(TTTJ_ERR_INVALID, "linear: bad sizes");
   if (n % 32 != 0) return fail(TTTJ_ERR_INVALID, "linear: n=%d must be a multiple of 32", n);
-  if (k % 64 != 0) return fail(TTTJ_ERR_INVALID, "linear: k=%d must be a multiple of 64", k);
+  // k need not fill the last 64-column block: TMA zero-fills columns past k.
+  if (k % 8 != 0) return fail(TTTJ_ERR_INVALID, "linear: k=%d must be a multiple of 8", k);
   const bool has_res = epi == EPI_BIAS_RESIDUAL || epi == EPI_BIAS_RESIDUAL_F32 ||
                        epi == EPI_RESIDUAL_F32_STATS;
   if (lda % 8 || ldw % 8 || ldo % 8 || (has_res && ldr % 8))
@@ -312,17 +334,20 @@ int check_config(const tttj_config* c) {
     return fail(TTTJ_ERR_INVALID, "d_model (%d) must be divisible by num_heads (%d)", c->d_model,
                 c->num_heads);
   const int hd = c->d_model / c->num_heads;
-  if (hd != 32 && hd != 64)
-    return fail(TTTJ_ERR_INVALID, "no B200 kernel for head_dim=%d (supported: 32, 64)", hd);
-  if (c->d_model % 64 != 0 || c->ffn_dim % 64 != 0)
-    return fail(TTTJ_ERR_INVALID, "d_model (%d) and ffn_dim (%d) must be multiples of 64",
+  if (hd % 8 != 0 || hd > 256)
+    return fail(TTTJ_ERR_INVALID,
+                "no B200 kernel for head_dim=%d (supported: multiples of 8 up to 256)", hd);
+  if (c->d_model % 32 != 0 || c->ffn_dim % 32 != 0)
+    return fail(TTTJ_ERR_INVALID, "d_model (%d) and ffn_dim (%d) must be multiples of 32",
                 c->d_model, c->ffn_dim);
   if (c->d_model > 2048) return fail(TTTJ_ERR_INVALID, "d_model=%d exceeds 2048", c->d_model);
   if (c->num_heads > 255) return fail(TTTJ_ERR_INVALID, "num_heads=%d exceeds 255", c->num_heads);
   if (c->num_layers > PLAN_COUNTERS)
     return fail(TTTJ_ERR_INVALID, "num_layers=%d exceeds %d", c->num_layers, PLAN_COUNTERS);
   const long long T = (long long)c->batch_size * c->seq_len;
-  if (T * (long long)(c->ffn_dim > 3 * c->d_model ? c->ffn_dim : 3 * c->d_model) >= (1ll << 40) ||
+  const long long widest = c->ffn_dim > 3ll * c->num_heads * layout_hd(hd)
+                               ? c->ffn_dim : 3ll * c->num_heads * layout_hd(hd);
+  if (T * widest >= (1ll << 40) ||
       T >= (1ll << 31) - 256)
     return fail(TTTJ_ERR_INVALID, "batch_size*seq_len too large");
   const long long plan_smem = 4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATC_BN - 1) / ATC_BN + 1);
@@ -474,7 +499,9 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   const int* rows_dev = p->tp.seq_off + B;  // number of valid tokens
   // Statistics partials actually produced: two column halves per column tile of the
   // residual GEMMs (N = d_model), whose tile width is fixed by (T, d_model).
-  p->parts = 2 * (D / gemm_choose_bn(T, D, p->num_sms));
+  const int res_bn = gemm_choose_bn(T, D, p->num_sms);
+  p->parts = 2 * ((D + res_bn - 1) / res_bn);
+  const int hd = head_dim_of(*cfg), hp = layout_hd(*cfg), Q = (int)qkv_width(*cfg);
   auto W = [&](int layer, int field) -> const uint8_t* {
     size_t off = 0, bytes = 0;
     weight_offset(*cfg, layer, field, &off, &bytes);
@@ -496,13 +523,17 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     float* cqkv = reinterpret_cast<float*>(fb + fl.cqkv);
     float* b1_f = reinterpret_cast<float*>(fb + fl.b1);
     float* c1 = reinterpret_cast<float*>(fb + fl.c1);
+    __half* wo_pad = heads_padded(*cfg) ? reinterpret_cast<__half*>(fb + fl.wo) : nullptr;
     cudaError_t fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_QKV)),
                                     reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)), L.ln1_w,
-                                    L.ln1_b, 3 * D, D, wqkv_f, bqkv_f, cqkv, 0);
+                                    L.ln1_b, 3 * Q, D, hd, hp, wqkv_f, bqkv_f, cqkv, 0);
     if (fe == cudaSuccess)
       fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_FFN_IN)),
                           reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), L.ln2_w, L.ln2_b, F,
-                          D, w1_f, b1_f, c1, 0);
+                          D, 1, 1, w1_f, b1_f, c1, 0);
+    if (fe == cudaSuccess && wo_pad)
+      fe = pad_head_cols_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_OUT)), D, D, hd, hp,
+                                wo_pad, 0);
     if (fe != cudaSuccess) {
       delete p;
       return cuda_fail(fe, "fold_ln_launch");
@@ -511,16 +542,16 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     // LN1 for qkv(l); out_proj(l) writes LN2 for ffn_in(l).
     float2* st_ln1 = p->stats;
     float2* st_ln2 = p->stats + (size_t)T * p->parts;
-    rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * D, nullptr, 0, T, rows_dev,
-                    3 * D, D, EPI_LN_FOLD, p->status, p->num_sms);
+    rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * Q, nullptr, 0, T, rows_dev,
+                    3 * Q, D, EPI_LN_FOLD, p->status, p->num_sms);
     L.qkv.p.stats_in = st_ln1;
     L.qkv.p.stats_parts = p->parts;
     L.qkv.p.colsum = cqkv;
     L.qkv.p.ln_eps = kLnEps;
     if (!rc)
-      rc = build_gemm(&L.out, p->ctx, D, W(l, TTTJ_W_OUT), D,
-                      reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
-                      T, rows_dev, D, D, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
+      rc = build_gemm(&L.out, p->ctx, Q, wo_pad ? static_cast<const void*>(wo_pad) : W(l, TTTJ_W_OUT),
+                      Q, reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid,
+                      D, T, rows_dev, D, Q, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
     L.out.p.out16 = p->x16;
     L.out.p.ld16 = D;
     L.out.p.stats_out = st_ln2;
@@ -538,7 +569,7 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
                       reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D, p->resid,
                       D, T, rows_dev, D, F, last ? EPI_BIAS_RESIDUAL_F32 : EPI_RESIDUAL_F32_STATS,
                       p->status, p->num_sms);
-    if (!rc && (L.out.bn != 2 * D / p->parts || L.ffn_out.bn != 2 * D / p->parts))
+    if (!rc && (L.out.bn != res_bn || L.ffn_out.bn != res_bn))
       rc = fail(TTTJ_ERR_INVALID, "internal: residual GEMM tile width mismatch");
     if (!last) {
       L.ffn_out.p.out16 = p->x16;
@@ -561,8 +592,8 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
   p->lnf_b = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_B));
 
-  rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S, D,
-                       cfg->num_heads, p->tp, p->status, p->num_sms);
+  rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S,
+                       cfg->num_heads, hd, hp, p->tp, p->status, p->num_sms);
   if (rc) {
     delete p;
     return rc;
@@ -641,7 +672,7 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
   cudaStream_t s = static_cast<cudaStream_t>(stream_ptr);
   const tttj_config& c = p->cfg;
   const int B = c.batch_size, S = c.seq_len, D = c.d_model, T = B * S;
-  const int hd = D / c.num_heads;
+  const int hp = layout_hd(c);
   const int* rows_dev = p->tp.seq_off + B;
 
   // Per-class timing: an event pair around every launch when enabled.
@@ -667,7 +698,7 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
   } while (0)
 
   TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
-                                                  ATC_ITEM_ROWS, ATC_BN, p->tp, s));
+                                                  atc_item_rows(hp), ATC_BN, p->tp, s));
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
                               p->stats, p->parts, s));
@@ -679,7 +710,7 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     AtcParams ap = p->attn;
     ap.work_counter = p->tp.counters + l;
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
-               attention_tc_launch(p->attn_tm, ap, hd, c.causal, p->attn_grid, s));
+               attention_tc_launch(p->attn_tm, ap, hp, c.causal, p->attn_grid, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));
@@ -746,8 +777,8 @@ int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* vali
       qkv_rows <= 0)
     return fail(TTTJ_ERR_INVALID, "attention: bad shape");
   const int hd = d_model / num_heads;
-  if (hd != 32 && hd != 64)
-    return fail(TTTJ_ERR_INVALID, "attention: head_dim=%d unsupported (32, 64)", hd);
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
+    return fail(TTTJ_ERR_INVALID, "attention: head_dim=%d unsupported (32, 64, 128, 256)", hd);
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15)
     return fail(TTTJ_ERR_INVALID, "attention: qkv and ctx must be 16-byte aligned");
   WsLayout w{};
@@ -762,10 +793,10 @@ int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* vali
   CUtensorMap tm;
   AtcParams ap;
   int grid = 0;
-  int rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, d_model,
-                           num_heads, tp, nullptr, sm_count(dev));
+  int rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, num_heads, hd,
+                           hd, tp, nullptr, sm_count(dev));
   if (rc) return rc;
-  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, ATC_ITEM_ROWS,
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, atc_item_rows(hd),
                                ATC_BN, tp, s));
   TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
   return TTTJ_OK;
@@ -839,8 +870,9 @@ extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows,
       qkv_rows <= 0)
     return fail(TTTJ_ERR_INVALID, "attention_noalloc: bad shape");
   const int hd = d_model / num_heads;
-  if (hd != 32 && hd != 64)
-    return fail(TTTJ_ERR_INVALID, "attention_noalloc: head_dim=%d unsupported (32, 64)", hd);
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
+    return fail(TTTJ_ERR_INVALID, "attention_noalloc: head_dim=%d unsupported (32, 64, 128, 256)",
+                hd);
   if ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(ctx)) & 15)
     return fail(TTTJ_ERR_INVALID, "attention_noalloc: qkv and ctx must be 16-byte aligned");
   WsLayout w{};
@@ -860,10 +892,10 @@ extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows,
   CUtensorMap tm;
   AtcParams ap;
   int grid = 0;
-  rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, d_model, num_heads,
+  rc = build_attention(&tm, &ap, &grid, qkv, ctx, qkv_rows, batch, seq_len, num_heads, hd, hd,
                        tp, nullptr, sm_count(dev));
   if (rc) return rc;
-  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, ATC_ITEM_ROWS,
+  TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, atc_item_rows(hd),
                                ATC_BN, tp, s));
   TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
   return TTTJ_OK;

@@ -76,7 +76,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int lane = lane_id();
 
   const int n_tiles = p.n / BN + ((p.n % BN) ? 1 : 0);
-  const int k_iters = p.k / GEMM_BK;
+  const int k_iters = (p.k + GEMM_BK - 1) / GEMM_BK;  // columns past k are zero-filled by TMA
   const uint64_t limit = p.wait_limit_ns;
 
   if (threadIdx.x == 0) {

@@ -65,8 +65,9 @@ int gemm_choose_bn(int rows, int n, int num_sms);
 void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair);
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
-// tcgen05 attention (256-query items, plan with q_block ATC_ITEM_ROWS, kv_block ATC_BN).
-// tmQKV: fp16 [rows, 3D] map, box {head_dim, 128}, swizzle 128 B (hd 64) / 64 B (hd 32).
+// tcgen05 attention for a head-dim layout of 32, 64, 128 or 256 (plan with q_block
+// atc_item_rows(head_dim), kv_block ATC_BN).  tmQKV: fp16 [rows, 3 * qkv_width] map, box
+// {min(head_dim, 64), 128}, swizzle 64 B (head_dim 32) / 128 B.
 cudaError_t attention_tc_launch(const CUtensorMap& tmQKV, const AtcParams& p, int head_dim,
                                 int causal, int grid, cudaStream_t stream);
 
@@ -75,9 +76,15 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
                              int n_parts, cudaStream_t stream);
+// rows_out output rows; with hd < hp the input's rows are heads of hd rows placed at
+// the start of output groups of hp rows, the rest zero (hd == hp: one row each).
 cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,
-                           int rows, int k, __half* w_out, float* b_out, float* colsum,
-                           cudaStream_t stream);
+                           int rows_out, int k, int hd, int hp, __half* w_out, float* b_out,
+                           float* colsum, cudaStream_t stream);
+// w [rows, cols] -> w_out [rows, (cols / hd) * hp]: column groups of hd widened to hp
+// with zero columns.
+cudaError_t pad_head_cols_launch(const __half* w, int rows, int cols, int hd, int hp,
+                                 __half* w_out, cudaStream_t stream);
 // in_dtype: 0 = fp16 rows, 1 = fp32 rows.
 cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, int rows_max, int D,
                            const float* gamma, const float* beta, float eps, __half* out,

@@ -43,7 +43,7 @@ struct GemmParams {
   const int* rows_dev;  // device count of valid rows (nullable: use rows_max)
   int rows_max;         // rows allocated in A / out
   int n;                // output columns (multiple of 32)
-  int k;                // reduction length (multiple of 64)
+  int k;                // reduction length (multiple of 8; the last block is zero-filled)
   const float* bias;    // [n] fp32
   void* out;            // [rows, ldo], fp16 (fp32 for EPI_BIAS_RESIDUAL_F32)
   int ldo;
@@ -68,22 +68,24 @@ constexpr int GEMM_EPI_WARPS = 8;  // two per TMEM lane quadrant, each owning ha
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_STAGE_OUT_BYTES = 32 * 32 * 4;  // per-warp staging: 32 rows x 32 fp32
 
-// tcgen05 attention: work items of 2 query tiles x 128 rows, 128-key KV tiles.
+// tcgen05 attention: work items of 2 query tiles x 128 rows (one tile at head_dim 256),
+// 128-key KV tiles.
 struct AtcParams {
   const int* seq_off;     // [B+1] first packed row of each sequence
   const int2* items;      // work list: {b, (query pair << 8) | h}
   const int* item_count;  // number of valid items
   int* work_counter;      // zeroed before the launch; CTAs take items with atomicAdd
-  __half* ctx;            // [rows_max, D]
+  __half* ctx;            // [rows_max, qkv_width]
   int rows_max;           // rows allocated in qkv / ctx (stores past it are dropped)
-  int d_model;
+  int qkv_width;          // columns of each of the q | k | v blocks = ctx row stride
   float scale_log2;       // hd^-0.5 * log2(e)
   int* status;            // device status word (nullable)
   unsigned long long wait_limit_ns;
 };
 constexpr int ATC_BM = 128;         // query rows per tile = TMEM lanes
 constexpr int ATC_BN = 128;         // keys per KV tile
-constexpr int ATC_ITEM_ROWS = 256;  // two query tiles per work item
+// Query rows per work item for a head-dim layout: two tiles, one at head_dim 256.
+constexpr int atc_item_rows(int layout_hd) { return layout_hd == 256 ? 128 : 256; }
 // warps 0-3 / 4-7 softmax tile 0 / 1, warp 8 TMA, warps 9 / 10 MMA for tile 0 / 1
 constexpr int ATC_THREADS = 352;
 
@@ -92,7 +94,7 @@ struct TokenPlan {
   int* seq_off;     // [B+1]; seq_off[B] = number of valid tokens
   int* packed_src;  // [B*S] packed row -> b*S + s
   int* dst_map;     // [B*S] b*S + s -> packed row, or -1
-  int2* items;      // [B*H*ceil(S/256)] attention work list
+  int2* items;      // [B*H*ceil(S/128)] attention work list (bound for every item size)
   int* item_count;  // [1]
   int* counters;    // [PLAN_COUNTERS] dynamic work counters, zeroed by the plan kernel
 };

@@ -55,12 +55,21 @@ cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, 
 }
 
 cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,
-                           int rows, int k, __half* w_out, float* b_out, float* colsum,
-                           cudaStream_t stream) {
-  const int grid = (rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
+                           int rows_out, int k, int hd, int hp, __half* w_out, float* b_out,
+                           float* colsum, cudaStream_t stream) {
+  const int grid = (rows_out + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
-  fold_ln_kernel<<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(w, b, gamma, beta, rows, k, w_out, b_out,
-                                                          colsum);
+  fold_ln_kernel<<<grid, 32 * ROWS_PER_CTA, 0, stream>>>(w, b, gamma, beta, rows_out, k, hd, hp,
+                                                          w_out, b_out, colsum);
+  return cudaGetLastError();
+}
+
+cudaError_t pad_head_cols_launch(const __half* w, int rows, int cols, int hd, int hp,
+                                 __half* w_out, cudaStream_t stream) {
+  const long total = (long)rows * (cols / hd) * hp;
+  const int grid = (int)((total + 255) / 256);
+  if (grid == 0) return cudaSuccess;
+  pad_head_cols_kernel<<<grid, 256, 0, stream>>>(w, rows, cols, hd, hp, w_out);
   return cudaGetLastError();
 }
 

@@ -241,21 +241,35 @@ __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ 
 
 // One-time LayerNorm fold of a weight matrix W [rows, k] (fp16) consumed by
 // LayerNorm(x) @ W^T + b:  W' = W * gamma (per column k, fp16), colsum[r] = sum_k W'[r, k]
-// (of the fp16 values), b'[r] = b[r] + sum_k W[r, k] * beta[k].  One warp per row.
+// (of the fp16 values), b'[r] = b[r] + sum_k W[r, k] * beta[k].  One warp per output row.
+// Output row r takes input row (r / hp) * hd + r % hp when r % hp < hd and is zero
+// otherwise (heads of hd rows widened to hp; hd == hp is the identity).
 __global__ void __launch_bounds__(256) fold_ln_kernel(const __half* __restrict__ w,
                                                       const float* __restrict__ b,
                                                       const float* __restrict__ gamma,
-                                                      const float* __restrict__ beta, int rows,
-                                                      int k, __half* __restrict__ w_out,
+                                                      const float* __restrict__ beta, int rows_out,
+                                                      int k, int hd, int hp,
+                                                      __half* __restrict__ w_out,
                                                       float* __restrict__ b_out,
                                                       float* __restrict__ colsum) {
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
-  if (row >= rows) return;
+  if (row >= rows_out) return;
   const int lane = lane_id();
+  const int d = row % hp;
+  if (d >= hd) {
+    const float z[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int c = lane * 8; c < k; c += 256) store8(w_out + (size_t)row * k + c, z);
+    if (lane == 0) {
+      colsum[row] = 0.f;
+      b_out[row] = 0.f;
+    }
+    return;
+  }
+  const int src = (row / hp) * hd + d;
   double cs = 0.0, bb = 0.0;
   for (int c = lane * 8; c < k; c += 256) {
     float wv[8], g[8], be[8], wf[8];
-    load8<__half>(w + (size_t)row * k + c, wv);
+    load8<__half>(w + (size_t)src * k + c, wv);
     load8<float>(gamma + c, g);
     load8<float>(beta + c, be);
 #pragma unroll
@@ -272,8 +286,21 @@ __global__ void __launch_bounds__(256) fold_ln_kernel(const __half* __restrict__
   }
   if (lane == 0) {
     colsum[row] = (float)cs;
-    b_out[row] = (float)((double)b[row] + bb);
+    b_out[row] = (float)((double)b[src] + bb);
   }
+}
+
+// w [rows, cols] -> w_out [rows, (cols / hd) * hp]: column c of output row r is
+// w[r, (c / hp) * hd + c % hp] when c % hp < hd, else 0.
+__global__ void __launch_bounds__(256) pad_head_cols_kernel(const __half* __restrict__ w, int rows,
+                                                            int cols, int hd, int hp,
+                                                            __half* __restrict__ w_out) {
+  const int cols_out = (cols / hd) * hp;
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)rows * cols_out) return;
+  const int r = (int)(i / cols_out), c = (int)(i - (long)r * cols_out);
+  const int d = c % hp;
+  w_out[i] = d < hd ? w[(size_t)r * cols + (c / hp) * hd + d] : __float2half_rn(0.f);
 }
 
 template <int VPL, typename TIn>

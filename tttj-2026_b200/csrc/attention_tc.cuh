@@ -275,7 +275,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
     {
       constexpr uint32_t idesc_s = idesc_f16_f32(ATC_BM, ATC_BN);
       constexpr uint32_t idesc_o = idesc_f16_f32(ATC_BM, HD, 0, 1);
-      constexpr uint32_t v_step = HD == 64 ? (2048u >> 4) : (1024u >> 4);  // 16 keys
+      // 16 keys of V: 16 rows of the box (64 B rows at head_dim 32, 128 B otherwise).
+      constexpr uint32_t v_step = HD == 32 ? (1024u >> 4) : (2048u >> 4);
       const uint32_t s_col = t == 0 ? SM::TMEM_S0 : SM::TMEM_S1;
       const uint32_t p_col = t == 0 ? SM::TMEM_P0 : SM::TMEM_P1;
       const uint32_t o_col = t == 0 ? SM::TMEM_O0 : SM::TMEM_O1;

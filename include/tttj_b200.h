@@ -116,6 +116,18 @@ int tttj_plan_destroy(tttj_plan* plan);
 int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
                  void* out, void* stream);
 
+/* Forward path of a plan.  TTTJ_PATH_AUTO (the default) runs every sequence of at most
+ * 128 tokens through one launch of the resident-stack kernel when the shape allows it
+ * (d_model <= 128 or 256, layout head_dim 32/64/128 -- see tttj_plan_path), else the
+ * layer-by-layer kernels; TTTJ_PATH_LAYERWISE always uses the layer-by-layer kernels.
+ * The resident kernel replaces the reference's sequence-resident and fused Triton
+ * megakernels (kernels/sequence_resident.py:125-233, kernels/fused_megakernel.py:1860). */
+#define TTTJ_PATH_AUTO 0
+#define TTTJ_PATH_LAYERWISE 1
+int tttj_plan_set_path(tttj_plan* plan, int path);
+/* 1 if tttj_forward of this plan runs the resident-stack kernel, 0 if layer by layer. */
+int tttj_plan_path(tttj_plan* plan);
+
 /* Synchronise the plan's device and read (then clear) the device status word that
  * bounded device waits write on timeout.  *device_status = 0 when healthy. */
 int tttj_plan_status(tttj_plan* plan, int* device_status);
@@ -134,7 +146,8 @@ int tttj_plan_launch_count(tttj_plan* plan);
 #define TTTJ_KCLASS_GEMM_FFN_IN 5
 #define TTTJ_KCLASS_GEMM_FFN_OUT 6
 #define TTTJ_KCLASS_FINAL_LN 7
-#define TTTJ_KCLASS_COUNT 8
+#define TTTJ_KCLASS_RESIDENT 8 /* the whole stack in one launch (resident path) */
+#define TTTJ_KCLASS_COUNT 9
 
 /* With timing enabled, every later tttj_forward records a CUDA event pair around
  * each launch on the forward's stream; tttj_plan_kernel_times returns, per class,
@@ -155,7 +168,7 @@ const char* tttj_kernel_class_name(int cls);
  *   a [rows, k] fp16 (row stride lda), w [n, k] fp16 (row stride ldw), bias [n] fp32,
  *   out [rows, n] fp16 (ldo); residual [rows, n] fp16 (ldr) for TTTJ_EPI_BIAS_RESIDUAL
  *   (out may equal residual).  rows_dev (nullable) holds a device row count <= rows.
- *   n % 32 == 0, k % 64 == 0, strides multiples of 8 elements. */
+ *   n % 32 == 0, k % 8 == 0, strides multiples of 8 elements. */
 #define TTTJ_EPI_BIAS 0
 #define TTTJ_EPI_BIAS_GELU 1
 #define TTTJ_EPI_BIAS_RESIDUAL 2

@@ -72,9 +72,13 @@ _SIGNATURES = {
     "tttj_plan_enable_timing": (_c.c_int, [_vp, _c.c_int]),
     "tttj_plan_kernel_times": (_c.c_int, [_vp, _c.POINTER(_c.c_double), _c.POINTER(_c.c_long)]),
     "tttj_kernel_class_name": (_c.c_char_p, [_c.c_int]),
+    "tttj_plan_set_path": (_c.c_int, [_vp, _c.c_int]),
+    "tttj_plan_path": (_c.c_int, [_vp]),
 }
 
-KCLASS_COUNT = 8
+KCLASS_COUNT = 9
+PATH_AUTO = 0
+PATH_LAYERWISE = 1
 
 
 class TttjConfig(ctypes.Structure):

@@ -218,6 +218,26 @@ int make_tmap_2d(CUtensorMap* m, const void* base, CUtensorMapDataType dtype, ui
   return TTTJ_OK;
 }
 
+// Per-layer 2-D matrices [rows, cols] (row stride `ld` elements) laid out `layer_bytes`
+// apart, as one 3-D tensor {cols, rows, layers} moved in boxes of box_cols x box_rows.
+int make_tmap_3d(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint64_t layers, uint64_t layer_bytes, uint32_t box_cols, uint32_t box_rows,
+                 CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16 || layer_bytes % 16)
+    return fail(TTTJ_ERR_INVALID, "TMA operand must be 16-byte aligned with 16-byte strides");
+  cuuint64_t dims[3] = {cols, rows, layers};
+  cuuint64_t strides[2] = {ld * 2, layer_bytes};
+  cuuint32_t box[3] = {box_cols, box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(TTTJ_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return TTTJ_OK;
+}
+
 // GEMM operand: fp16 [rows, cols], boxes of 64 columns (128 B, one swizzle atom) x
 // box_rows rows, 128-byte swizzle (the canonical K-major UMMA layout).
 int make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
@@ -355,6 +375,23 @@ int check_config(const tttj_config* c) {
   return TTTJ_OK;
 }
 
+// Shapes the resident-stack kernel (resident.cuh) takes: sequences of <= 128 tokens,
+// the residual (d_model fp32 columns) plus the largest step accumulator inside TMEM's
+// 512 columns, residual MMA groups of d_model <= 128 or two of 128, and the shared
+// memory layout within the 227 KB per CTA.
+bool resident_fits(const tttj_config& c) {
+  const int D = c.d_model, hp = layout_hd(c), F = c.ffn_dim;
+  if (c.seq_len > RES_ROWS) return false;
+  if (!(D <= 128 || D == 256) || D % 32) return false;
+  if (hp != 32 && hp != 64 && hp != 128) return false;
+  const int fc = F < 128 ? F : 128;
+  int acc = 3 * hp;
+  if (128 + hp > acc) acc = 128 + hp;
+  if (fc > acc) acc = fc;
+  if (D + acc > 512) return false;
+  return res_layout(D, F, hp).total <= 232448;
+}
+
 struct LayerGemms {
   GemmLaunch qkv, out, ffn_in, ffn_out;
   const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
@@ -380,6 +417,10 @@ struct tttj_plan {
   CUtensorMap attn_tm;
   AtcParams attn;
   int attn_grid;
+  // Resident-stack path (sequences of <= 128 tokens), built when the shape fits.
+  bool res_ok = false;
+  int path = TTTJ_PATH_AUTO;
+  ResLaunch res;
   // Optional per-kernel-class timing (tttj_plan_enable_timing).
   bool timing = false;
   std::vector<cudaEvent_t> ev_start, ev_stop;  // one pair per launch of one forward
@@ -403,7 +444,11 @@ struct DeviceGuard {
 };
 }  // namespace
 
-int launches_per_forward(const tttj_config& c) { return 5 * c.num_layers + 3; }
+int layerwise_launches(const tttj_config& c) { return 5 * c.num_layers + 3; }
+bool use_resident(const tttj_plan* p) { return p->res_ok && p->path == TTTJ_PATH_AUTO; }
+int launches_per_forward(const tttj_plan* p) {
+  return use_resident(p) ? 1 : layerwise_launches(p->cfg);
+}
 
 // Fold the events of the previous timed forward into the per-class totals.
 int collect_timing(tttj_plan* p) {
@@ -426,6 +471,66 @@ void destroy_events(tttj_plan* p) {
   p->ev_stop.clear();
   p->ev_class.clear();
   p->ev_used = 0;
+}
+
+// TMA maps and parameters of the resident-stack kernel: the plan's folded QKV / ffn_in
+// weights and (for padded heads) padded out_proj weight in the workspace, the caller's
+// out_proj / ffn_out weights, all as 3-D maps over the layers.
+int build_resident(tttj_plan* p, const FoldLayout& fl) {
+  const tttj_config& c = p->cfg;
+  const int D = c.d_model, F = c.ffn_dim, hp = layout_hd(c), Q = (int)qkv_width(c), L = c.num_layers;
+  const ResLayout ly = res_layout(D, F, hp);
+  const uint8_t* fold = p->ws + p->lay.fold;
+  const size_t fstride = p->lay.fold_layer, lstride = layer_stride(c);
+  auto W = [&](int field) -> const uint8_t* {
+    size_t off = 0, bytes = 0;
+    weight_offset(c, 0, field, &off, &bytes);
+    return p->weights + off;
+  };
+  ResLaunch& r = p->res;
+  std::memset(&r, 0, sizeof(r));
+  int rc = make_tmap_3d(&r.tmWqkv, fold + fl.wqkv, (uint64_t)3 * Q, D, D, L, fstride, 64, hp,
+                        CU_TENSOR_MAP_SWIZZLE_128B);
+  const uint32_t woc = hp < 64 ? hp : 64;
+  const CUtensorMapSwizzle wosw = hp < 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if (!rc) {
+    if (heads_padded(c))
+      rc = make_tmap_3d(&r.tmWo, fold + fl.wo, D, Q, Q, L, fstride, woc, ly.NB, wosw);
+    else
+      rc = make_tmap_3d(&r.tmWo, W(TTTJ_W_OUT), D, D, D, L, lstride, woc, ly.NB, wosw);
+  }
+  if (!rc)
+    rc = make_tmap_3d(&r.tmW1, fold + fl.w1, F, D, D, L, fstride, 64, ly.FC, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc)
+    rc = make_tmap_3d(&r.tmW2, W(TTTJ_W_FFN_OUT), D, F, F, L, lstride, 64, ly.NB,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  ResParams& q = r.p;
+  q.B = c.batch_size;
+  q.S = c.seq_len;
+  q.D = D;
+  q.H = c.num_heads;
+  q.F = F;
+  q.L = L;
+  q.causal = c.causal ? 1 : 0;
+  q.hp = hp;
+  q.Q = Q;
+  q.scale_log2 = (1.0f / sqrtf((float)head_dim_of(c))) * 1.4426950408889634f;
+  q.eps = kLnEps;
+  q.bqkv = reinterpret_cast<const float*>(fold + fl.bqkv);
+  q.cqkv = reinterpret_cast<const float*>(fold + fl.cqkv);
+  q.b1 = reinterpret_cast<const float*>(fold + fl.b1);
+  q.c1 = reinterpret_cast<const float*>(fold + fl.c1);
+  q.fold_stride = fstride;
+  q.bo = reinterpret_cast<const float*>(W(TTTJ_B_OUT));
+  q.b2 = reinterpret_cast<const float*>(W(TTTJ_B_FFN_OUT));
+  q.layer_stride = lstride;
+  q.lnf_w = p->lnf_w;
+  q.lnf_b = p->lnf_b;
+  q.status = p->status;
+  q.wait_limit_ns = kWaitLimitNs;
+  p->res_ok = true;
+  return TTTJ_OK;
 }
 
 extern "C" {
@@ -598,9 +703,26 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     delete p;
     return rc;
   }
+  if (resident_fits(*cfg)) {
+    rc = build_resident(p, fl);
+    if (rc) {
+      delete p;
+      return rc;
+    }
+  }
   *out_plan = p;
   return TTTJ_OK;
 }
+
+int tttj_plan_set_path(tttj_plan* p, int path) {
+  if (!p) return fail(TTTJ_ERR_INVALID, "set_path: null plan");
+  if (path != TTTJ_PATH_AUTO && path != TTTJ_PATH_LAYERWISE)
+    return fail(TTTJ_ERR_INVALID, "set_path: unknown path %d", path);
+  p->path = path;
+  return TTTJ_OK;
+}
+
+int tttj_plan_path(tttj_plan* p) { return p && use_resident(p) ? 1 : 0; }
 
 int tttj_plan_destroy(tttj_plan* plan) {
   if (plan) {
@@ -612,14 +734,14 @@ int tttj_plan_destroy(tttj_plan* plan) {
 }
 
 int tttj_plan_launch_count(tttj_plan* plan) {
-  return plan ? launches_per_forward(plan->cfg) : 0;
+  return plan ? launches_per_forward(plan) : 0;
 }
 
 int tttj_plan_enable_timing(tttj_plan* p, int enable) {
   if (!p) return fail(TTTJ_ERR_INVALID, "timing: null plan");
   DeviceGuard guard(p->device);
   if (enable && !p->timing) {
-    const int n = launches_per_forward(p->cfg);
+    const int n = layerwise_launches(p->cfg);  // the larger of the two paths
     p->ev_start.resize(n);
     p->ev_stop.resize(n);
     p->ev_class.assign(n, 0);
@@ -657,7 +779,7 @@ int tttj_plan_kernel_times(tttj_plan* p, double* total_ms, long* launches) {
 const char* tttj_kernel_class_name(int cls) {
   static const char* names[TTTJ_KCLASS_COUNT] = {
       "plan_tokens", "layernorm", "gemm_qkv", "attention", "gemm_out_proj",
-      "gemm_ffn_in_gelu", "gemm_ffn_out", "final_layernorm_scatter"};
+      "gemm_ffn_in_gelu", "gemm_ffn_out", "final_layernorm_scatter", "resident_stack"};
   return (cls >= 0 && cls < TTTJ_KCLASS_COUNT) ? names[cls] : "";
 }
 
@@ -697,6 +819,17 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     TTTJ_CUDA(tock());             \
   } while (0)
 
+  if (use_resident(p)) {
+    // The whole stack in one launch: one CTA per sequence reads x and the mask directly.
+    ResLaunch r = p->res;
+    r.p.x = x;
+    r.p.mask = valid_mask;
+    r.p.out = out;
+    r.p.x_f32 = x_dtype == TTTJ_DTYPE_F32 ? 1 : 0;
+    TTTJ_TIMED(TTTJ_KCLASS_RESIDENT, resident_launch(r, s));
+    p->ev_used = slot;
+    return TTTJ_OK;
+  }
   TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
                                                   atc_item_rows(hp), ATC_BN, p->tp, s));
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,

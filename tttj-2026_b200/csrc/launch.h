@@ -71,6 +71,17 @@ cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 cudaError_t attention_tc_launch(const CUtensorMap& tmQKV, const AtcParams& p, int head_dim,
                                 int causal, int grid, cudaStream_t stream);
 
+// K3 resident stack (resident.cuh): weights as 3-D TMA maps over the layers
+// ({columns, rows, layer}, one box per MMA unit).
+struct ResLaunch {
+  CUtensorMap tmWqkv;  // folded Wqkv [3Q, D] per layer, box {64, hp}
+  CUtensorMap tmWo;    // out_proj [D, Q] per layer, box {min(hp, 64), min(D, 128)}
+  CUtensorMap tmW1;    // folded W1 [F, D] per layer, box {64, min(F, 128)}
+  CUtensorMap tmW2;    // W2 [D, F] per layer, box {64, min(D, 128)}
+  ResParams p;
+};
+cudaError_t resident_launch(const ResLaunch& r, cudaStream_t stream);
+
 cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
                                int kv_block, const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,

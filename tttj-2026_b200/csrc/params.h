@@ -19,6 +19,7 @@ enum TttjDeviceStatus : int {
   TTTJ_DEV_TIMEOUT_EPILOGUE = 0x103,
   TTTJ_DEV_TIMEOUT_SELFTEST = 0x1ff,
   TTTJ_DEV_TIMEOUT_ATTN = 0x201,
+  TTTJ_DEV_TIMEOUT_RESIDENT = 0x301,
 };
 
 
@@ -98,6 +99,72 @@ struct TokenPlan {
   int* item_count;  // [1]
   int* counters;    // [PLAN_COUNTERS] dynamic work counters, zeroed by the plan kernel
 };
+
+// K3 resident stack: one CTA runs every layer of one sequence of <= 128 tokens.
+constexpr int RES_ROWS = 128;            // rows of a sequence = TMEM lanes
+constexpr int RES_STAGE_BYTES = 16384;   // one weight box: <= 128 rows x 64 fp16
+constexpr int RES_STAGES = 4;
+constexpr int RES_WORKERS = 256;         // warps 2-9: two per TMEM lane quadrant
+constexpr int RES_THREADS = 64 + RES_WORKERS;
+constexpr int RES_MISC_BYTES = 4096;     // barriers, row statistics, row maps
+
+struct ResParams {
+  const void* x;          // [B, S, D] fp16 or fp32 input
+  const uint8_t* mask;    // [B, S] valid_token_mask bytes, or null (all valid)
+  void* out;              // [B, S, D] output, same dtype as x
+  int x_f32;              // 1: x and out are fp32
+  int B, S, D, H, F, L, causal;
+  int hp;                 // layout head dim (32, 64, 128)
+  int Q;                  // H * hp: width of each of the q | k | v weight blocks
+  float scale_log2;       // hd^-0.5 * log2(e)
+  float eps;
+  // Per-layer fp32 vectors: layer l at base + l * stride bytes.
+  const float* bqkv;      // LayerNorm-folded [3Q]
+  const float* cqkv;      // column sums of the folded Wqkv [3Q]
+  const float* b1;        // folded [F]
+  const float* c1;        // [F]
+  size_t fold_stride;
+  const float* bo;        // [D]
+  const float* b2;        // [D]
+  size_t layer_stride;
+  const float* lnf_w;     // [D]
+  const float* lnf_b;     // [D]
+  int* status;
+  unsigned long long wait_limit_ns;
+};
+
+// Shared-memory layout of the resident kernel for (D, F, hp); the same on host and
+// device.  All regions start on 1024-byte boundaries (128-byte swizzle atoms).
+struct ResLayout {
+  int Dp;     // D rounded up to 64 (columns of the fp16 residual copy)
+  int FC;     // FFN columns per chunk (min(F, 128))
+  int FCp;    // FC rounded up to 64
+  int NB;     // output columns per residual MMA group (min(D, 128))
+  int NH;     // residual column groups (D / NB)
+  int KC;     // 64-column K chunks of D
+  int NF;     // FFN chunks
+  int tile;   // bytes of one [128 x hp] operand tile
+  int xa, qkvh, ring, misc, total;
+};
+
+__host__ __device__ inline ResLayout res_layout(int D, int F, int hp) {
+  ResLayout y;
+  y.Dp = (D + 63) / 64 * 64;
+  y.FC = F < 128 ? F : 128;
+  y.FCp = (y.FC + 63) / 64 * 64;
+  y.NB = D < 128 ? D : 128;
+  y.NH = D / y.NB;
+  y.KC = y.Dp / 64;
+  y.NF = (F + y.FC - 1) / y.FC;
+  y.tile = RES_ROWS * hp * 2;
+  const int qkv = 3 * y.tile, hbuf = RES_ROWS * y.FCp * 2;
+  y.xa = 0;
+  y.qkvh = y.xa + RES_ROWS * y.Dp * 2;
+  y.ring = y.qkvh + (qkv > hbuf ? qkv : hbuf);
+  y.misc = y.ring + RES_STAGES * RES_STAGE_BYTES;
+  y.total = y.misc + RES_MISC_BYTES + 1024;  // + alignment slack
+  return y;
+}
 
 constexpr int PLAN_COUNTERS = 256;  // one per attention launch of a forward (layers)
 

@@ -1,0 +1,32 @@
+// Instantiations and launcher of the K3 resident-stack kernel (resident.cuh).
+#include "launch.h"
+#include "resident.cuh"
+
+namespace tttj {
+
+namespace {
+template <int HP>
+cudaError_t launch_res(const ResLaunch& r, cudaStream_t stream) {
+  auto kern = resident_stack_kernel<HP>;
+  // At least half the SM's shared memory: one CTA per SM, so a CTA never waits for
+  // another to release the 512 TMEM columns it allocates.
+  int smem = res_layout(r.p.D, r.p.F, HP).total;
+  if (smem < 116 * 1024) smem = 116 * 1024;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(r.p.B), dim3(RES_THREADS), (size_t)smem, stream, r.tmWqkv, r.tmWo,
+                    r.tmW1, r.tmW2, r.p);
+}
+}  // namespace
+
+cudaError_t resident_launch(const ResLaunch& r, cudaStream_t stream) {
+  if (r.p.B <= 0) return cudaSuccess;
+  switch (r.p.hp) {
+    case 32: return launch_res<32>(r, stream);
+    case 64: return launch_res<64>(r, stream);
+    case 128: return launch_res<128>(r, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace tttj

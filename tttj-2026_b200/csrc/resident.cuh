@@ -1,0 +1,650 @@
+// K3: the whole transformer stack for short sequences in one launch.
+//
+// For sequences of at most 128 tokens (the reference's resident cases,
+// kernels/sequence_resident.py:125-233 and kernels/fused_megakernel.py:1163-1858, and
+// BASELINE config C1) the layer-by-layer path spends most of its time starting and
+// draining 5 kernels per layer.  Here one CTA owns one sequence for the whole forward:
+// BaselineTransformerBlock x L, final LayerNorm and masking
+// (benchmarks/torch_transformer_benchmark.py:134-172), with no intermediate tensor in
+// global memory and no launch in between.
+//
+// State of a CTA (one sequence, rows r < len valid, the rest kept at zero):
+//   TMEM [0, D)        fp32 residual stream x, row r = TMEM lane r.  out_proj and
+//                      ffn_out accumulate straight into it (tcgen05.mma with the
+//                      accumulate flag); their biases are added by the next LayerNorm pass.
+//   TMEM [D, 512)      accumulators of the current step: q|k|v of one head, then S (P
+//                      written over its first 64 columns) and O, then one FFN chunk.
+//   smem xa            fp16 copy of x, the A operand of the LayerNorm-folded QKV and
+//                      ffn_in GEMMs (the same folded weights and epilogue as the
+//                      layer-by-layer path: out = rstd (acc - mean colsum) + b').
+//   smem q/k/v tiles   one head at a time; the head's attention output reuses the q tile
+//                      and is multiplied into the residual right away (out_proj per head,
+//                      K = hp), so no [S, D] context buffer is needed.
+//   smem h             one FFN chunk of GELU(ffn_in) (<= 128 columns), multiplied into
+//                      the residual by ffn_out before the next chunk.
+//   smem ring          weight boxes streamed by TMA from L2 (all CTAs read the same
+//                      weights), RES_STAGES x 16 KB.
+//
+// Roles: warp 0 TMA producer (weight boxes in the fixed order of the schedule below),
+// warp 1 TMEM owner and MMA issuer (whole warp, elected lane issues), warps 2-9
+// workers: LayerNorm passes, epilogues, softmax (two warps per TMEM lane quadrant, each
+// one half of the 32-column chunks).  Workers and the MMA warp alternate strictly: the
+// workers finish a step's inputs and arrive on `ready`, the MMA warp issues the step and
+// commits to `done`, the workers wait for `done`.  Steps per layer:
+//   QKV(h=0) | S(h) | PV(h) | out_proj(h) + QKV(h+1) ... | ffn_in(0) | ffn_out(c) + ffn_in(c+1) ...
+// Every wait is bounded; on a timeout the role records TTTJ_DEV_TIMEOUT_RESIDENT, raises
+// the CTA abort flag and unwinds.
+//
+// Attention of a sequence of <= 128 tokens is one 128 x 128 score tile per head, so the
+// softmax is exact in one pass (no running max): causal triu(1) and key-padding masks
+// (:99-108), fp32 softmax (:111), P V (:112).
+#pragma once
+#include "common.cuh"
+#include "params.h"
+
+namespace tttj {
+
+// 16-byte chunk store into a K-major 128-byte-swizzled operand made of 64-column boxes of
+// [128 rows][128 B]: row r, columns col .. col + 7 (col a multiple of 8).
+__device__ __forceinline__ void res_store_sw128(uint32_t base, int r, int col, uint4 v) {
+  const uint32_t a = base + (uint32_t)((col >> 6) * (RES_ROWS * 128) + r * 128 +
+                                       ((((col >> 3) & 7) ^ (r & 7)) << 4));
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+// The same for a 64-byte-swizzled [128 rows][64 B] operand (32 columns).
+__device__ __forceinline__ void res_store_sw64(uint32_t base, int r, int col, uint4 v) {
+  const uint32_t a = base + (uint32_t)(r * 64 + ((((col >> 3) & 3) ^ ((r >> 1) & 3)) << 4));
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z),
+               "r"(v.w)
+               : "memory");
+}
+
+template <int HP>
+__device__ __forceinline__ void res_store_tile(uint32_t tile, int r, int col, uint4 v) {
+  if constexpr (HP == 32)
+    res_store_sw64(tile, r, col, v);
+  else
+    res_store_sw128(tile, r, col, v);
+}
+
+// K-major descriptor of K step ks (16 elements) of a [128 x HP] q / k / context tile.
+template <int HP>
+__device__ __forceinline__ uint64_t res_desc_tile(uint32_t tile, int ks) {
+  if constexpr (HP == 32)
+    return desc_kmajor_sw64(tile) + (uint64_t)(2 * ks);
+  else
+    return desc_kmajor_sw128(tile + (uint32_t)((ks >> 2) * (RES_ROWS * 128))) +
+           (uint64_t)(2 * (ks & 3));
+}
+
+__device__ __forceinline__ void res_tmem_st_f32(uint32_t taddr, const float (&v)[32]) {
+  uint32_t u[32];
+#pragma unroll
+  for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(v[e]);
+  tmem_st_32x32b_x32(taddr, u);
+}
+
+__device__ __forceinline__ uint4 res_pack8(const float* v) {
+  return make_uint4(pack_half2(v[0], v[1]), pack_half2(v[2], v[3]), pack_half2(v[4], v[5]),
+                    pack_half2(v[6], v[7]));
+}
+
+template <int HP>
+__global__ void __launch_bounds__(RES_THREADS, 1)
+    resident_stack_kernel(const __grid_constant__ CUtensorMap tmWqkv,
+                          const __grid_constant__ CUtensorMap tmWo,
+                          const __grid_constant__ CUtensorMap tmW1,
+                          const __grid_constant__ CUtensorMap tmW2, const ResParams p) {
+  constexpr unsigned FULL = 0xffffffffu;
+  constexpr int WOC = HP < 64 ? HP : 64;        // columns of one out_proj weight box
+  constexpr int KW = HP / WOC;                  // out_proj boxes per head and column group
+  const ResLayout ly = res_layout(p.D, p.F, HP);
+  const int D = p.D, F = p.F, Q = p.Q, H = p.H;
+  const int A0 = D;  // first TMEM column after the residual
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t pad = (1024u - (raw & 1023u)) & 1023u;
+  uint8_t* smem = smem_raw + pad;
+  const uint32_t base = raw + pad;
+  const uint32_t sXA = base + ly.xa;
+  const uint32_t sQ = base + ly.qkvh, sK = sQ + ly.tile, sV = sK + ly.tile, sH = sQ;
+  const uint32_t sRing = base + ly.ring;
+  const uint32_t bar0 = base + ly.misc;
+  const uint32_t bar_full = bar0;                          // [RES_STAGES]
+  const uint32_t bar_empty = bar_full + 8 * RES_STAGES;    // [RES_STAGES]
+  const uint32_t bar_ready = bar_empty + 8 * RES_STAGES;   // workers -> MMA warp
+  const uint32_t bar_done = bar_ready + 8;                 // MMA warp -> workers
+  const uint32_t bar_wsync = bar_done + 8;                 // workers among themselves
+  const uint32_t bar_drain = bar_wsync + 8;
+  uint8_t* misc = smem + ly.misc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 128);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 132);
+  int* len_slot = reinterpret_cast<int*>(misc + 136);
+  float2* stats = reinterpret_cast<float2*>(misc + 256);       // [2][128]
+  float* invl = reinterpret_cast<float*>(misc + 256 + 2048);   // [128]
+  int* pos = reinterpret_cast<int*>(misc + 256 + 2048 + 512);  // [128]
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const uint64_t limit = p.wait_limit_ns;
+  const int b = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmWqkv);
+    tma_prefetch_desc(&tmWo);
+    tma_prefetch_desc(&tmW1);
+    tma_prefetch_desc(&tmW2);
+    for (int s = 0; s < RES_STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_ready, RES_WORKERS);
+    mbar_init(bar_done, 1);
+    mbar_init(bar_wsync, RES_WORKERS);
+    mbar_init(bar_drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Inputs and weights may come from the previous kernel of the stream.
+  griddep_wait();
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      long u = 0;
+      bool ok = true;
+      auto load = [&](const CUtensorMap* m, int c0, int c1, int c2, uint32_t bytes) {
+        if (!ok) return;
+        const int st = (int)(u % RES_STAGES);
+        if (!mbar_wait(bar_empty + 8 * st, (uint32_t)((u / RES_STAGES) & 1) ^ 1u, abort_flag,
+                       limit)) {
+          ok = false;
+          return;
+        }
+        mbar_arrive_expect_tx(bar_full + 8 * st, bytes);
+        tma_load_3d(sRing + st * RES_STAGE_BYTES, m, bar_full + 8 * st, c0, c1, c2);
+        ++u;
+      };
+      for (int l = 0; l < p.L && ok; ++l) {
+        for (int h = 0; h < H && ok; ++h) {
+          for (int kc = 0; kc < ly.KC; ++kc)
+            for (int part = 0; part < 3; ++part)
+              load(&tmWqkv, kc * 64, part * Q + h * HP, l, HP * 128);
+          for (int nh = 0; nh < ly.NH; ++nh)
+            for (int kk = 0; kk < KW; ++kk)
+              load(&tmWo, h * HP + kk * 64, nh * ly.NB, l, ly.NB * WOC * 2);
+        }
+        for (int c = 0; c < ly.NF && ok; ++c) {
+          for (int kc = 0; kc < ly.KC; ++kc) load(&tmW1, kc * 64, c * ly.FC, l, ly.FC * 128);
+          for (int nh = 0; nh < ly.NH; ++nh)
+            for (int kk = 0; kk < ly.FCp / 64; ++kk)
+              load(&tmW2, c * ly.FC + kk * 64, nh * ly.NB, l, ly.NB * 128);
+        }
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
+        for (long j = u > RES_STAGES ? u - RES_STAGES : 0; j < u; ++j)
+          mbar_wait(bar_full + 8 * (int)(j % RES_STAGES), (uint32_t)((j / RES_STAGES) & 1),
+                    nullptr, limit);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    long u = 0, step = 0;
+    bool ok = true, issued = false;
+    auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+      if (!ok) return false;
+      if (!__all_sync(FULL, mbar_wait(bar, parity, abort_flag, limit))) {
+        ok = false;
+        return false;
+      }
+      tc_fence_after();
+      return true;
+    };
+    auto ready = [&]() -> bool { return wait(bar_ready, (uint32_t)(step & 1)); };
+    auto done = [&]() {
+      if (!ok) return;
+      mma_commit_warp(bar_done);
+      ++step;
+    };
+    // Consume the next weight box: issue(box address), then release its stage.
+    auto unit = [&](auto&& issue) {
+      const int st = (int)(u % RES_STAGES);
+      if (!wait(bar_full + 8 * st, (uint32_t)((u / RES_STAGES) & 1))) return;
+      issue(sRing + st * RES_STAGE_BYTES);
+      mma_commit_warp(bar_empty + 8 * st);
+      issued = true;
+      ++u;
+    };
+    const uint32_t id_qkv = idesc_f16_f32(RES_ROWS, HP);
+    const uint32_t id_res = idesc_f16_f32(RES_ROWS, ly.NB);
+    const uint32_t id_s = idesc_f16_f32(RES_ROWS, 128);
+    const uint32_t id_pv = idesc_f16_f32(RES_ROWS, HP, 0, 1);
+    const uint32_t id_ffn = idesc_f16_f32(RES_ROWS, ly.FC);
+    auto qkv = [&]() {
+      for (int kc = 0; kc < ly.KC; ++kc)
+        for (int part = 0; part < 3; ++part)
+          unit([&](uint32_t w) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f16_ss_warp(tmem + (uint32_t)(A0 + part * HP),
+                              desc_kmajor_sw128(sXA + (uint32_t)(kc * RES_ROWS * 128)) + (uint64_t)(2 * k),
+                              desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_qkv,
+                              (kc > 0 || k > 0) ? 1u : 0u);
+          });
+    };
+    auto out_proj = [&]() {  // A = this head's attention output (in the q tile)
+      for (int nh = 0; nh < ly.NH; ++nh)
+        for (int kk = 0; kk < KW; ++kk)
+          unit([&](uint32_t w) {
+#pragma unroll
+            for (int k = 0; k < WOC / 16; ++k) {
+              const uint64_t bd = HP == 32 ? desc_kmajor_sw64(w) + (uint64_t)(2 * k)
+                                           : desc_kmajor_sw128(w) + (uint64_t)(2 * k);
+              mma_f16_ss_warp(tmem + (uint32_t)(nh * ly.NB), res_desc_tile<HP>(sQ, kk * (WOC / 16) + k),
+                              bd, id_res, 1u);
+            }
+          });
+    };
+    auto scores = [&]() {
+#pragma unroll
+      for (int ks = 0; ks < HP / 16; ++ks)
+        mma_f16_ss_warp(tmem + (uint32_t)A0, res_desc_tile<HP>(sQ, ks), res_desc_tile<HP>(sK, ks),
+                        id_s, ks > 0 ? 1u : 0u);
+      issued = true;
+    };
+    auto pv = [&]() {
+      const uint64_t vd = HP == 32 ? desc_mnmajor_sw64(sV, ly.tile, 512)
+                                   : desc_mnmajor_sw128(sV, RES_ROWS * 128, 1024);
+      constexpr uint32_t vstep = HP == 32 ? (1024u >> 4) : (2048u >> 4);  // 16 keys
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_f16_ts_warp(tmem + (uint32_t)(A0 + 128), tmem + (uint32_t)(A0 + kk * 8),
+                        vd + (uint64_t)(kk * vstep), id_pv, kk > 0 ? 1u : 0u);
+      issued = true;
+    };
+    auto ffn_in = [&]() {
+      for (int kc = 0; kc < ly.KC; ++kc)
+        unit([&](uint32_t w) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16_ss_warp(tmem + (uint32_t)A0,
+                            desc_kmajor_sw128(sXA + (uint32_t)(kc * RES_ROWS * 128)) + (uint64_t)(2 * k),
+                            desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_ffn,
+                            (kc > 0 || k > 0) ? 1u : 0u);
+        });
+    };
+    auto ffn_out = [&]() {
+      for (int nh = 0; nh < ly.NH; ++nh)
+        for (int kk = 0; kk < ly.FCp / 64; ++kk)
+          unit([&](uint32_t w) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_f16_ss_warp(tmem + (uint32_t)(nh * ly.NB),
+                              desc_kmajor_sw128(sH + (uint32_t)(kk * RES_ROWS * 128)) + (uint64_t)(2 * k),
+                              desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_res, 1u);
+          });
+    };
+    for (int l = 0; l < p.L && ok; ++l) {
+      if (ready()) qkv();
+      done();
+      for (int h = 0; h < H && ok; ++h) {
+        if (ready()) scores();
+        done();
+        if (ready()) pv();
+        done();
+        if (ready()) {
+          out_proj();
+          if (h + 1 < H) qkv();
+        }
+        done();
+      }
+      if (ready()) ffn_in();
+      done();
+      for (int c = 0; c < ly.NF && ok; ++c) {
+        if (ready()) {
+          ffn_out();
+          if (c + 1 < ly.NF) ffn_in();
+        }
+        done();
+      }
+    }
+    if (!ok) {
+      if (lane == 0) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
+      }
+      if (issued) {
+        mma_commit_warp(bar_drain);
+        mbar_wait(bar_drain, 0, nullptr, limit);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ workers, warps 2-9
+    const int wt = threadIdx.x - 64;          // worker thread 0..255
+    const int quad = warp & 3;                // TMEM lane quadrant
+    const int half = (warp - 2) >> 2;         // which 32-column chunks: c % 2 == half
+    const int r = quad * 32 + lane;           // row = token of the sequence
+    const uint32_t tr = tmem + ((uint32_t)(quad * 32) << 16);
+    const int nchunk = D / 32;
+    const float invD = 1.0f / (float)D;
+    long step = 0, ws = 0;
+    bool ok = true;
+
+    auto wsync = [&]() -> bool {
+      if (!ok) return false;
+      mbar_arrive(bar_wsync);
+      if (!mbar_wait(bar_wsync, (uint32_t)(ws & 1), abort_flag, limit)) ok = false;
+      ++ws;
+      return ok;
+    };
+    // Hand the finished inputs of the next MMA step over and wait for its results.
+    auto step_sync = [&]() -> bool {
+      if (!ok) return false;
+      tmem_wait_st();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar_ready);
+      if (!mbar_wait(bar_done, (uint32_t)(step & 1), abort_flag, limit)) ok = false;
+      ++step;
+      tc_fence_after();
+      return ok;
+    };
+
+    // Zero the operand buffers once: columns past D / F in the last 64-column box
+    // meet zero-filled weight columns and must hold finite values.
+    {
+      const uint32_t n16 = (uint32_t)(ly.ring - ly.xa) / 16;
+      for (uint32_t i = (uint32_t)wt; i < n16; i += RES_WORKERS)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(sXA + i * 16), "r"(0u)
+                     : "memory");
+    }
+    // Valid tokens of this sequence, in order (any mask, not only prefixes).
+    if (warp == 2) {
+      int running = 0;
+      for (int s0 = 0; s0 < p.S; s0 += 32) {
+        const int s = s0 + lane;
+        const bool v = s < p.S && (p.mask == nullptr || p.mask[(size_t)b * p.S + s] != 0);
+        const unsigned bal = __ballot_sync(FULL, v);
+        if (v) pos[running + __popc(bal & ((1u << lane) - 1u))] = s;
+        running += __popc(bal);
+      }
+      if (lane == 0) *len_slot = running;
+    }
+    wsync();
+    const int len = *len_slot;
+    const bool row_valid = r < len;
+    const bool warp_has_pad = quad * 32 + 31 >= len;  // warp-uniform
+
+    // Residual <- x (fp32), padded rows zero.
+    if (ok) {
+      const int src = row_valid ? pos[r] : 0;
+      for (int c = half; c < nchunk; c += 2) {
+        float v[32];
+        if (row_valid) {
+          if (p.x_f32) {
+            const float4* xs = reinterpret_cast<const float4*>(
+                static_cast<const float*>(p.x) + ((size_t)b * p.S + src) * D + c * 32);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 t = xs[q];
+              v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
+            }
+          } else {
+            const uint4* xs = reinterpret_cast<const uint4*>(
+                static_cast<const __half*>(p.x) + ((size_t)b * p.S + src) * D + c * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const uint4 t = xs[q];
+              const float2 a0 = unpack_half2(t.x), a1 = unpack_half2(t.y);
+              const float2 a2 = unpack_half2(t.z), a3 = unpack_half2(t.w);
+              v[8 * q] = a0.x; v[8 * q + 1] = a0.y; v[8 * q + 2] = a1.x; v[8 * q + 3] = a1.y;
+              v[8 * q + 4] = a2.x; v[8 * q + 5] = a2.y; v[8 * q + 6] = a3.x; v[8 * q + 7] = a3.y;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] = 0.f;
+        }
+        res_tmem_st_f32(tr + (uint32_t)(c * 32), v);
+      }
+      tmem_wait_st();
+    }
+
+    // LayerNorm statistics pass over the residual: adds a pending bias (the previous
+    // residual GEMM's), keeps padded rows at zero (masked_fill after every block,
+    // :143-144), writes the fp16 copy into xa when asked, and returns mean / rstd of
+    // the row (both halves' partial sums exchanged through shared memory).
+    auto ln_pass = [&](const float* pbias, bool write_xa, float& mean, float& rstd) -> bool {
+      float s = 0.f, q = 0.f;
+      const bool store_back = pbias != nullptr || warp_has_pad;
+      for (int c = half; c < nchunk; c += 2) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tr + (uint32_t)(c * 32), u);
+        float bb[32];
+        if (pbias) {
+          const float4* b4 = reinterpret_cast<const float4*>(pbias + c * 32);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 t = __ldg(b4 + k);
+            bb[4 * k] = t.x; bb[4 * k + 1] = t.y; bb[4 * k + 2] = t.z; bb[4 * k + 3] = t.w;
+          }
+        }
+        tmem_wait_ld();
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          float t = __uint_as_float(u[e]);
+          if (pbias) t += bb[e];
+          v[e] = row_valid ? t : 0.f;
+          s += v[e];
+          q = fmaf(v[e], v[e], q);
+        }
+        if (store_back) res_tmem_st_f32(tr + (uint32_t)(c * 32), v);
+        if (write_xa) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) res_store_sw128(sXA, r, c * 32 + 8 * j, res_pack8(v + 8 * j));
+        }
+      }
+      tmem_wait_st();
+      stats[half * RES_ROWS + r] = make_float2(s, q);
+      if (!wsync()) return false;
+      const float2 a = stats[r], c2 = stats[RES_ROWS + r];
+      mean = (a.x + c2.x) * invD;
+      const float var = fmaxf((a.y + c2.y) * invD - mean * mean, 0.f);
+      rstd = rsqrtf(var + p.eps);
+      return true;
+    };
+
+    auto layer_vec = [&](const float* v, size_t stride, int l) {
+      return reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(v) + (size_t)l * stride);
+    };
+
+    float mean = 0.f, rstd = 0.f;
+    for (int l = 0; l < p.L && ok; ++l) {
+      const float* bq = layer_vec(p.bqkv, p.fold_stride, l);
+      const float* cq = layer_vec(p.cqkv, p.fold_stride, l);
+      // LN1 statistics (the previous block's ffn_out bias is still pending in TMEM).
+      if (!ln_pass(l > 0 ? layer_vec(p.b2, p.layer_stride, l - 1) : nullptr, true, mean, rstd)) break;
+      if (!step_sync()) break;  // -> QKV(0) done
+      for (int h = 0; h < H && ok; ++h) {
+        // q | k | v of head h: folded LayerNorm epilogue, fp16 into the operand tiles.
+        for (int i = half; i < 3 * HP / 32; i += 2) {
+          const int part = i / (HP / 32), cc = i % (HP / 32);
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + i * 32), u);
+          const int n0 = part * Q + h * HP + cc * 32;
+          float cs[32], bb[32];
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(cq + n0) + k);
+            const float4 w = __ldg(reinterpret_cast<const float4*>(bq + n0) + k);
+            cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
+            bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
+          }
+          tmem_wait_ld();
+          float v[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e)
+            v[e] = fmaf(rstd, fmaf(-mean, cs[e], __uint_as_float(u[e])), bb[e]);
+          const uint32_t tile = part == 0 ? sQ : part == 1 ? sK : sV;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) res_store_tile<HP>(tile, r, cc * 32 + 8 * j, res_pack8(v + 8 * j));
+        }
+        if (!step_sync()) break;  // -> S = q k^T done
+        // Softmax of the row (one warp per quadrant), P written over the scores.
+        if (half == 0) {
+          uint32_t sv[128];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t chunk[32];
+            tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + c * 32), chunk);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = chunk[e];
+          }
+          tmem_wait_ld();
+          const int lim = p.causal ? min(len - 1, r) : len - 1;  // keys c > lim masked
+          float mx = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c <= lim) mx = fmaxf(mx, __uint_as_float(sv[c]));
+          const float base_v = mx == -INFINITY ? 0.f : mx * p.scale_log2;
+          float lsum = 0.f;
+          uint32_t pk[64];
+#pragma unroll
+          for (int c = 0; c < 64; ++c) {
+            const float p0 = (2 * c <= lim) ? ex2_approx(fmaf(__uint_as_float(sv[2 * c]), p.scale_log2, -base_v)) : 0.f;
+            const float p1 = (2 * c + 1 <= lim) ? ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), p.scale_log2, -base_v)) : 0.f;
+            lsum += p0 + p1;
+            pk[c] = pack_half2(p0, p1);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t chunk[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
+            tmem_st_32x32b_x16(tr + (uint32_t)(A0 + q * 16), chunk);
+          }
+          invl[r] = lsum > 0.f ? 1.f / lsum : 0.f;
+        }
+        if (!step_sync()) break;  // -> O = P v done
+        if (!wsync()) break;      // 1 / row sum visible to both halves
+        {
+          const float inv = invl[r];
+          for (int i = half; i < HP / 32; i += 2) {
+            uint32_t u[32];
+            tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + 128 + i * 32), u);
+            tmem_wait_ld();
+            float v[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]) * inv;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) res_store_tile<HP>(sQ, r, i * 32 + 8 * j, res_pack8(v + 8 * j));
+          }
+        }
+        if (!step_sync()) break;  // -> out_proj(h) (+ QKV(h+1)) done
+      }
+      if (!ok) break;
+      // LN2 statistics (out_proj bias pending), fp16 copy for ffn_in.
+      if (!ln_pass(layer_vec(p.bo, p.layer_stride, l), true, mean, rstd)) break;
+      if (!step_sync()) break;  // -> ffn_in(0) done
+      const float* b1 = layer_vec(p.b1, p.fold_stride, l);
+      const float* c1 = layer_vec(p.c1, p.fold_stride, l);
+      for (int c = 0; c < ly.NF && ok; ++c) {
+        for (int i = half; i < ly.FC / 32; i += 2) {
+          const int n0 = c * ly.FC + i * 32;
+          uint32_t u[32];
+          tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + i * 32), u);
+          float v[32];
+          if (n0 < F) {  // F is a multiple of 32: a 32-column group is all in or all out
+            float cs[32], bb[32];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(c1 + n0) + k);
+              const float4 w = __ldg(reinterpret_cast<const float4*>(b1 + n0) + k);
+              cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
+              bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 g = gelu_erf2(fmaf(rstd, fmaf(-mean, cs[e], __uint_as_float(u[e])), bb[e]),
+                                         fmaf(rstd, fmaf(-mean, cs[e + 1], __uint_as_float(u[e + 1])), bb[e + 1]));
+              v[e] = g.x;
+              v[e + 1] = g.y;
+            }
+          } else {
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) v[e] = 0.f;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) res_store_sw128(sH, r, i * 32 + 8 * j, res_pack8(v + 8 * j));
+        }
+        if (!step_sync()) break;  // -> ffn_out(c) (+ ffn_in(c+1)) done
+      }
+    }
+
+    // Final LayerNorm of the valid rows into out; masked positions are written as zeros.
+    if (ok && ln_pass(layer_vec(p.b2, p.layer_stride, p.L - 1), false, mean, rstd)) {
+      // tcgen05.ld is warp-wide: every lane loads, only valid rows store.
+      const int dst = row_valid ? pos[r] : 0;
+      for (int c = half; c < nchunk; c += 2) {
+        uint32_t u[32];
+        tmem_ld_32x32b_x32(tr + (uint32_t)(c * 32), u);
+        tmem_wait_ld();
+        if (!row_valid) continue;
+        float v[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int col = c * 32 + e;
+          v[e] = fmaf((__uint_as_float(u[e]) - mean) * rstd, __ldg(p.lnf_w + col), __ldg(p.lnf_b + col));
+        }
+        if (p.x_f32) {
+          float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + ((size_t)b * p.S + dst) * D + c * 32);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) o[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        } else {
+          uint4* o = reinterpret_cast<uint4*>(static_cast<__half*>(p.out) + ((size_t)b * p.S + dst) * D + c * 32);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) o[q] = res_pack8(v + 8 * q);
+        }
+      }
+      if (len < p.S) {
+        const int esz = p.x_f32 ? 4 : 2;
+        const int per_row = D * esz / 16;  // 16-byte chunks per output row
+        for (int s = 0; s < p.S; ++s) {
+          if (p.mask != nullptr && p.mask[(size_t)b * p.S + s] == 0) {
+            uint4* o = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.out) + ((size_t)b * p.S + s) * D * esz);
+            for (int i = wt; i < per_row; i += RES_WORKERS) o[i] = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+      }
+    }
+    if (!ok) {
+      *abort_flag = 1;
+      report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace tttj

@@ -146,14 +146,28 @@ class B200Transformer(nn.Module):
         self.parameter_model = parameter_model
         self.register_buffer("packed_weights", pack_weights(parameter_model, device), persistent=False)
         self._plans: dict[tuple[int, int], _Plan] = {}
+        self._path = _lib.PATH_AUTO
 
     def plan_for(self, batch: int, seq_len: int) -> _Plan:
         key = (batch, seq_len)
         plan = self._plans.get(key)
         if plan is None:
             plan = _Plan(self.config, batch, seq_len, self.packed_weights, self.device)
+            _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, self._path), "set_path")
             self._plans[key] = plan
         return plan
+
+    def set_layerwise(self, layerwise: bool) -> None:
+        """Force the layer-by-layer kernels (True) or let each shape pick (False, the
+        default: sequences of <= 128 tokens run the whole stack in one resident launch
+        when the shape fits)."""
+        self._path = _lib.PATH_LAYERWISE if layerwise else _lib.PATH_AUTO
+        for plan in self._plans.values():
+            _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, self._path), "set_path")
+
+    def uses_resident(self, batch: int, seq_len: int) -> bool:
+        """Whether a forward of shape [batch, seq_len] runs the resident-stack kernel."""
+        return bool(_lib.lib().tttj_plan_path(self.plan_for(batch, seq_len).handle))
 
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         if x.dim() != 3 or x.shape[-1] != self.config.d_model:

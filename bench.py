@@ -83,6 +83,9 @@ def parse_args(argv=None):
     ap.add_argument("--config", default="C2", choices=list(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--path", default="auto", choices=["auto", "layerwise", "resident"],
+                    help="auto: the library picks (the resident whole-stack kernel for short "
+                         "sequences of small layers); layerwise / resident: force one path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
     return ap.parse_args(argv)
@@ -144,6 +147,8 @@ def useful_work(cfg, mask, out_bytes: int = 2):
         "plan_tokens": ("hbm", float(B * S)),
     }
     flops = (2.0 * Tv * (4 * D * D + 2 * D * F) + 4.0 * hd * H * pairs) * cfg.num_layers
+    # The resident path runs the whole stack (every layer) in one launch.
+    per_launch["resident_stack"] = ("tensor", flops)
     return Tv, pairs, per_launch, flops
 
 
@@ -326,6 +331,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     B, S = CONFIGS[name][0], CONFIGS[name][1]
     cfg, model, x, mask = make_case(name, args.seed, rank, dev)
     opt = tb.make_optimized_transformer(model)
+    opt.set_path(args.path)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -484,6 +490,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         "scaling": "weak", "vs_baseline": vs_baseline, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": workload_desc(name), "global_batch": world * B, "seq_len": S,
                    "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
+                   "path": ("resident stack (1 launch per forward)" if opt.uses_resident(B, S)
+                            else f"layer by layer ({launches} launches per forward)"),
                    "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",
                    "inputs": f"x~N(0,1), input seed {args.seed + 1} (+1000*rank)"},
         "p50_ms": statistics.median(step_ms),

@@ -116,14 +116,19 @@ int tttj_plan_destroy(tttj_plan* plan);
 int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
                  void* out, void* stream);
 
-/* Forward path of a plan.  TTTJ_PATH_AUTO (the default) runs every sequence of at most
- * 128 tokens through one launch of the resident-stack kernel when the shape allows it
- * (d_model <= 128 or 256, layout head_dim 32/64/128 -- see tttj_plan_path), else the
- * layer-by-layer kernels; TTTJ_PATH_LAYERWISE always uses the layer-by-layer kernels.
+/* Forward path of a plan.  The resident-stack kernel runs the whole forward of
+ * sequences of at most 128 tokens in one launch (one CTA per sequence); it fits
+ * d_model <= 128 or 256 with layout head_dim 32/64/128 and enough TMEM / shared memory.
+ * TTTJ_PATH_AUTO (the default) takes it for the shapes where it measured faster than
+ * the layer-by-layer kernels (small layers: few heads, little weight per layer), else
+ * the layer-by-layer kernels; TTTJ_PATH_LAYERWISE always takes the layer-by-layer
+ * kernels; TTTJ_PATH_RESIDENT takes the resident kernel whenever it fits (set_path
+ * returns TTTJ_ERR_INVALID when it does not).  tttj_plan_path reports the choice.
  * The resident kernel replaces the reference's sequence-resident and fused Triton
  * megakernels (kernels/sequence_resident.py:125-233, kernels/fused_megakernel.py:1860). */
 #define TTTJ_PATH_AUTO 0
 #define TTTJ_PATH_LAYERWISE 1
+#define TTTJ_PATH_RESIDENT 2
 int tttj_plan_set_path(tttj_plan* plan, int path);
 /* 1 if tttj_forward of this plan runs the resident-stack kernel, 0 if layer by layer. */
 int tttj_plan_path(tttj_plan* plan);

@@ -65,15 +65,16 @@ def test_resident_matches_oracle_and_layerwise(name):
     model = tb.make_parameter_model(cfg, 3, dtype, DEV)
     x, mask = _inputs(name, cfg, dtype)
     opt = tb.make_optimized_transformer(model)
+    opt.set_path("resident")
     assert opt.uses_resident(B, S), name
     assert opt.launches_per_forward(B, S) == 1
     with torch.inference_mode():
         res = opt(x, mask)
         res2 = opt(x, mask)
-        opt.set_layerwise(True)
+        opt.set_path("layerwise")
         assert not opt.uses_resident(B, S)
         lw = opt(x, mask)
-        opt.set_layerwise(False)
+        opt.set_path("auto")
         ref = forward_fp32(state_dict_fp32(model, DEV), cfg, x.float(), mask)
     torch.cuda.synchronize()
     assert res.dtype == x.dtype and res.shape == x.shape
@@ -92,3 +93,20 @@ def test_long_sequences_keep_the_layerwise_path():
     opt = tb.make_optimized_transformer(model)
     assert not opt.uses_resident(2, 129)
     assert opt.launches_per_forward(2, 129) == 5 * 1 + 3
+    with pytest.raises(ValueError, match="does not fit"):
+        opt.set_path("resident")
+    assert not opt.uses_resident(2, 129)  # the failed switch changed nothing
+
+
+def test_auto_path_choice():
+    """Auto takes the resident kernel for the reference's small cases and keeps the
+    layer-by-layer kernels where those measured faster (C1, 16-head case 11)."""
+    def auto(B, S, D, H, F, L, causal):
+        cfg = tb.TransformerConfig(B, S, D, H, F, L, causal)
+        opt = tb.make_optimized_transformer(tb.make_parameter_model(cfg, 0, torch.float16, DEV))
+        return opt.uses_resident(B, S)
+
+    assert auto(64, 128, 128, 4, 128, 4, True)        # case 1
+    assert auto(64, 128, 128, 1, 128, 4, True)        # case 9
+    assert not auto(64, 128, 128, 16, 128, 4, True)   # case 11
+    assert not auto(2, 128, 256, 4, 1024, 2, False)   # C1

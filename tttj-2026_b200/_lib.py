@@ -79,6 +79,8 @@ _SIGNATURES = {
 KCLASS_COUNT = 9
 PATH_AUTO = 0
 PATH_LAYERWISE = 1
+PATH_RESIDENT = 2
+PATHS = {"auto": PATH_AUTO, "layerwise": PATH_LAYERWISE, "resident": PATH_RESIDENT}
 
 
 class TttjConfig(ctypes.Structure):

@@ -389,7 +389,20 @@ bool resident_fits(const tttj_config& c) {
   if (128 + hp > acc) acc = 128 + hp;
   if (fc > acc) acc = fc;
   if (D + acc > 512) return false;
-  return res_layout(D, F, hp).total <= 232448;
+  return res_layout(D, F, hp, c.num_heads * hp).stages >= 3;
+}
+
+// Whether TTTJ_PATH_AUTO takes the resident kernel for a shape it fits.  One CTA works
+// through 3H + 3 + ceil(F / 128) worker <-> MMA hand-offs per layer (about 2 us each)
+// and streams every layer's weights through its own ring (about 60 GB/s); measured on
+// B200 against the layer-by-layer kernels, the resident kernel is faster up to about
+// 24 hand-offs and 512 KB of weights per layer (the reference's cases 1-7, 9, 10, 12)
+// and slower beyond (case 11: 16 heads; C1: 1.6 MB of weights per layer).
+bool resident_preferred(const tttj_config& c) {
+  const long D = c.d_model, F = c.ffn_dim, Q = (long)qkv_width(c);
+  const long steps = 3l * c.num_heads + 3 + (F + 127) / 128;
+  const long weight_bytes = 2 * (3 * Q * D + D * Q + 2 * D * F);
+  return steps <= 24 && weight_bytes <= 512 * 1024;
 }
 
 struct LayerGemms {
@@ -418,7 +431,8 @@ struct tttj_plan {
   AtcParams attn;
   int attn_grid;
   // Resident-stack path (sequences of <= 128 tokens), built when the shape fits.
-  bool res_ok = false;
+  bool res_ok = false;       // the resident kernel fits this shape (launch built)
+  bool res_auto = false;     // ... and TTTJ_PATH_AUTO prefers it
   int path = TTTJ_PATH_AUTO;
   ResLaunch res;
   // Optional per-kernel-class timing (tttj_plan_enable_timing).
@@ -445,7 +459,9 @@ struct DeviceGuard {
 }  // namespace
 
 int layerwise_launches(const tttj_config& c) { return 5 * c.num_layers + 3; }
-bool use_resident(const tttj_plan* p) { return p->res_ok && p->path == TTTJ_PATH_AUTO; }
+bool use_resident(const tttj_plan* p) {
+  return p->path == TTTJ_PATH_RESIDENT || (p->path == TTTJ_PATH_AUTO && p->res_auto);
+}
 int launches_per_forward(const tttj_plan* p) {
   return use_resident(p) ? 1 : layerwise_launches(p->cfg);
 }
@@ -479,7 +495,7 @@ void destroy_events(tttj_plan* p) {
 int build_resident(tttj_plan* p, const FoldLayout& fl) {
   const tttj_config& c = p->cfg;
   const int D = c.d_model, F = c.ffn_dim, hp = layout_hd(c), Q = (int)qkv_width(c), L = c.num_layers;
-  const ResLayout ly = res_layout(D, F, hp);
+  const ResLayout ly = res_layout(D, F, hp, Q);
   const uint8_t* fold = p->ws + p->lay.fold;
   const size_t fstride = p->lay.fold_layer, lstride = layer_stride(c);
   auto W = [&](int field) -> const uint8_t* {
@@ -530,6 +546,7 @@ int build_resident(tttj_plan* p, const FoldLayout& fl) {
   q.status = p->status;
   q.wait_limit_ns = kWaitLimitNs;
   p->res_ok = true;
+  p->res_auto = resident_preferred(c);
   return TTTJ_OK;
 }
 
@@ -716,8 +733,12 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
 
 int tttj_plan_set_path(tttj_plan* p, int path) {
   if (!p) return fail(TTTJ_ERR_INVALID, "set_path: null plan");
-  if (path != TTTJ_PATH_AUTO && path != TTTJ_PATH_LAYERWISE)
+  if (path != TTTJ_PATH_AUTO && path != TTTJ_PATH_LAYERWISE && path != TTTJ_PATH_RESIDENT)
     return fail(TTTJ_ERR_INVALID, "set_path: unknown path %d", path);
+  if (path == TTTJ_PATH_RESIDENT && !p->res_ok)
+    return fail(TTTJ_ERR_INVALID,
+                "set_path: the resident kernel does not fit this shape (seq_len <= 128, "
+                "d_model <= 128 or 256, layout head_dim 32/64/128, TMEM and shared memory)");
   p->path = path;
   return TTTJ_OK;
 }

@@ -178,6 +178,13 @@ __device__ __forceinline__ void bulk_wait_read_all() {
 __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
+// Untiled bulk copy global -> shared (no multicast), completing on `bar` (tx bytes).
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+               : "memory");
+}
 // Hint: bring `bytes` (a multiple of 16, 16-byte aligned address) of global memory into
 // L2.  No completion tracking; a later ordinary load of the range finds it in L2.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gptr, uint32_t bytes) {

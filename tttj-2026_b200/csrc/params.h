@@ -102,11 +102,12 @@ struct TokenPlan {
 
 // K3 resident stack: one CTA runs every layer of one sequence of <= 128 tokens.
 constexpr int RES_ROWS = 128;            // rows of a sequence = TMEM lanes
-constexpr int RES_STAGE_BYTES = 16384;   // one weight box: <= 128 rows x 64 fp16
-constexpr int RES_STAGES = 4;
+constexpr int RES_STAGE_BYTES = 16384;   // one weight box: <= 128 rows x 64 fp16 (minimum stage)
+constexpr int RES_MAX_STAGES = 12;
 constexpr int RES_WORKERS = 256;         // warps 2-9: two per TMEM lane quadrant
 constexpr int RES_THREADS = 64 + RES_WORKERS;
-constexpr int RES_MISC_BYTES = 4096;     // barriers, row statistics, row maps
+constexpr int RES_MISC_BYTES = 6144;     // barriers, row statistics, row maps
+constexpr int RES_SMEM_LIMIT = 232448;   // 227 KB per CTA
 
 struct ResParams {
   const void* x;          // [B, S, D] fp16 or fp32 input
@@ -118,7 +119,8 @@ struct ResParams {
   int Q;                  // H * hp: width of each of the q | k | v weight blocks
   float scale_log2;       // hd^-0.5 * log2(e)
   float eps;
-  // Per-layer fp32 vectors: layer l at base + l * stride bytes.
+  // Per-layer fp32 vectors: layer l at base + l * stride bytes.  Each layer's are
+  // copied into shared memory (one block, see ResLayout) before the layer starts.
   const float* bqkv;      // LayerNorm-folded [3Q]
   const float* cqkv;      // column sums of the folded Wqkv [3Q]
   const float* b1;        // folded [F]
@@ -133,8 +135,8 @@ struct ResParams {
   unsigned long long wait_limit_ns;
 };
 
-// Shared-memory layout of the resident kernel for (D, F, hp); the same on host and
-// device.  All regions start on 1024-byte boundaries (128-byte swizzle atoms).
+// Shared-memory layout of the resident kernel for (D, F, hp, Q); the same on host and
+// device.  Regions start on 1024-byte boundaries (128-byte swizzle atoms).
 struct ResLayout {
   int Dp;     // D rounded up to 64 (columns of the fp16 residual copy)
   int FC;     // FFN columns per chunk (min(F, 128))
@@ -144,10 +146,18 @@ struct ResLayout {
   int KC;     // 64-column K chunks of D
   int NF;     // FFN chunks
   int tile;   // bytes of one [128 x hp] operand tile
-  int xa, qkvh, ring, misc, total;
+  // One layer's vectors, in floats: bqkv [3Q] cqkv [3Q] bo [D] b1 [F] c1 [F] b2 [D].
+  int v_bq, v_cq, v_bo, v_b1, v_c1, v_b2, v_floats;
+  int vec_bytes;  // one layer's block (two are kept: layer l in buffer l & 1)
+  // hp <= 64: a head's q, k and v weight boxes of one K chunk share a stage (stacked
+  // rows), so one MMA group with N = 3 hp computes all three.
+  int qkv_merged;
+  int stage_bytes;
+  int stages;     // weight ring stages that fit
+  int xa, qkvh, vec, ring, misc, total;
 };
 
-__host__ __device__ inline ResLayout res_layout(int D, int F, int hp) {
+__host__ __device__ inline ResLayout res_layout(int D, int F, int hp, int Q) {
   ResLayout y;
   y.Dp = (D + 63) / 64 * 64;
   y.FC = F < 128 ? F : 128;
@@ -157,11 +167,26 @@ __host__ __device__ inline ResLayout res_layout(int D, int F, int hp) {
   y.KC = y.Dp / 64;
   y.NF = (F + y.FC - 1) / y.FC;
   y.tile = RES_ROWS * hp * 2;
+  y.v_bq = 0;
+  y.v_cq = 3 * Q;
+  y.v_bo = 6 * Q;
+  y.v_b1 = 6 * Q + D;
+  y.v_c1 = 6 * Q + D + F;
+  y.v_b2 = 6 * Q + D + 2 * F;
+  y.v_floats = 6 * Q + 2 * D + 2 * F;
+  y.vec_bytes = y.v_floats * 4;
   const int qkv = 3 * y.tile, hbuf = RES_ROWS * y.FCp * 2;
   y.xa = 0;
   y.qkvh = y.xa + RES_ROWS * y.Dp * 2;
-  y.ring = y.qkvh + (qkv > hbuf ? qkv : hbuf);
-  y.misc = y.ring + RES_STAGES * RES_STAGE_BYTES;
+  y.vec = y.qkvh + (qkv > hbuf ? qkv : hbuf);
+  y.ring = y.vec + (2 * y.vec_bytes + 1023) / 1024 * 1024;
+  y.qkv_merged = hp <= 64;
+  y.stage_bytes = RES_STAGE_BYTES;
+  if (y.qkv_merged && 3 * hp * 128 > y.stage_bytes) y.stage_bytes = 3 * hp * 128;
+  const int room = RES_SMEM_LIMIT - 1024 - RES_MISC_BYTES - y.ring;
+  y.stages = room / y.stage_bytes;
+  if (y.stages > RES_MAX_STAGES) y.stages = RES_MAX_STAGES;
+  y.misc = y.ring + y.stages * y.stage_bytes;
   y.total = y.misc + RES_MISC_BYTES + 1024;  // + alignment slack
   return y;
 }

@@ -10,7 +10,7 @@ cudaError_t launch_res(const ResLaunch& r, cudaStream_t stream) {
   auto kern = resident_stack_kernel<HP>;
   // At least half the SM's shared memory: one CTA per SM, so a CTA never waits for
   // another to release the 512 TMEM columns it allocates.
-  int smem = res_layout(r.p.D, r.p.F, HP).total;
+  int smem = res_layout(r.p.D, r.p.F, HP, r.p.Q).total;
   if (smem < 116 * 1024) smem = 116 * 1024;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;

@@ -22,8 +22,10 @@
 //                      K = hp), so no [S, D] context buffer is needed.
 //   smem h             one FFN chunk of GELU(ffn_in) (<= 128 columns), multiplied into
 //                      the residual by ffn_out before the next chunk.
+//   smem vectors       each layer's biases and column sums, copied in by the producer
+//                      (two layers' worth: layer l in buffer l & 1).
 //   smem ring          weight boxes streamed by TMA from L2 (all CTAs read the same
-//                      weights), RES_STAGES x 16 KB.
+//                      weights), as many 16 KB stages as shared memory holds.
 //
 // Roles: warp 0 TMA producer (weight boxes in the fixed order of the schedule below),
 // warp 1 TMEM owner and MMA issuer (whole warp, elected lane issues), warps 2-9
@@ -100,7 +102,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   constexpr unsigned FULL = 0xffffffffu;
   constexpr int WOC = HP < 64 ? HP : 64;        // columns of one out_proj weight box
   constexpr int KW = HP / WOC;                  // out_proj boxes per head and column group
-  const ResLayout ly = res_layout(p.D, p.F, HP);
+  const ResLayout ly = res_layout(p.D, p.F, HP, p.Q);
+  const int NST = ly.stages;
   const int D = p.D, F = p.F, Q = p.Q, H = p.H;
   const int A0 = D;  // first TMEM column after the residual
 
@@ -112,20 +115,25 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   const uint32_t sXA = base + ly.xa;
   const uint32_t sQ = base + ly.qkvh, sK = sQ + ly.tile, sV = sK + ly.tile, sH = sQ;
   const uint32_t sRing = base + ly.ring;
+  const uint32_t sVec = base + ly.vec;
+  const float* vec_smem = reinterpret_cast<const float*>(smem + ly.vec);
   const uint32_t bar0 = base + ly.misc;
-  const uint32_t bar_full = bar0;                          // [RES_STAGES]
-  const uint32_t bar_empty = bar_full + 8 * RES_STAGES;    // [RES_STAGES]
-  const uint32_t bar_ready = bar_empty + 8 * RES_STAGES;   // workers -> MMA warp
-  const uint32_t bar_done = bar_ready + 8;                 // MMA warp -> workers
-  const uint32_t bar_wsync = bar_done + 8;                 // workers among themselves
+  const uint32_t bar_full = bar0;                              // [RES_MAX_STAGES]
+  const uint32_t bar_empty = bar_full + 8 * RES_MAX_STAGES;    // [RES_MAX_STAGES]
+  const uint32_t bar_ready = bar_empty + 8 * RES_MAX_STAGES;   // workers -> MMA warp
+  const uint32_t bar_done = bar_ready + 8;                     // MMA warp -> workers
+  const uint32_t bar_wsync = bar_done + 8;                     // workers among themselves
   const uint32_t bar_drain = bar_wsync + 8;
+  const uint32_t bar_vfull = bar_drain + 8;                    // [2] layer vectors landed
+  const uint32_t bar_vempty = bar_vfull + 16;                  // [2] layer vectors released
   uint8_t* misc = smem + ly.misc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 128);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 132);
-  int* len_slot = reinterpret_cast<int*>(misc + 136);
-  float2* stats = reinterpret_cast<float2*>(misc + 256);       // [2][128]
-  float* invl = reinterpret_cast<float*>(misc + 256 + 2048);   // [128]
-  int* pos = reinterpret_cast<int*>(misc + 256 + 2048 + 512);  // [128]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(misc + 256);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(misc + 260);
+  int* len_slot = reinterpret_cast<int*>(misc + 264);
+  float2* stats = reinterpret_cast<float2*>(misc + 512);    // [2][128] LayerNorm partials
+  float* rowmax = reinterpret_cast<float*>(misc + 2560);    // [2][128] softmax partial max
+  float* rowsum = reinterpret_cast<float*>(misc + 3584);    // [2][128] softmax partial sum
+  int* pos = reinterpret_cast<int*>(misc + 4608);           // [128] token of each row
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -137,7 +145,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     tma_prefetch_desc(&tmWo);
     tma_prefetch_desc(&tmW1);
     tma_prefetch_desc(&tmW2);
-    for (int s = 0; s < RES_STAGES; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(bar_full + 8 * s, 1);
       mbar_init(bar_empty + 8 * s, 1);
     }
@@ -145,6 +153,10 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     mbar_init(bar_done, 1);
     mbar_init(bar_wsync, RES_WORKERS);
     mbar_init(bar_drain, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar_vfull + 8 * i, 1);
+      mbar_init(bar_vempty + 8 * i, RES_WORKERS);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -162,25 +174,58 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      long u = 0;
+      // Ring position kept incrementally (the depth is a run-time value: no division).
+      int st = 0, issued_n = 0;
+      uint32_t ph = 0;
       bool ok = true;
-      auto load = [&](const CUtensorMap* m, int c0, int c1, int c2, uint32_t bytes) {
+      // One ring stage: `nbox` boxes of the same map, rows c1 + i * row_step, stacked.
+      auto load = [&](const CUtensorMap* m, int c0, int c1, int c2, uint32_t bytes, int nbox = 1,
+                      int row_step = 0) {
         if (!ok) return;
-        const int st = (int)(u % RES_STAGES);
-        if (!mbar_wait(bar_empty + 8 * st, (uint32_t)((u / RES_STAGES) & 1) ^ 1u, abort_flag,
-                       limit)) {
+        if (!mbar_wait(bar_empty + 8 * st, ph ^ 1u, abort_flag, limit)) {
           ok = false;
           return;
         }
-        mbar_arrive_expect_tx(bar_full + 8 * st, bytes);
-        tma_load_3d(sRing + st * RES_STAGE_BYTES, m, bar_full + 8 * st, c0, c1, c2);
-        ++u;
+        mbar_arrive_expect_tx(bar_full + 8 * st, bytes * (uint32_t)nbox);
+        for (int i = 0; i < nbox; ++i)
+          tma_load_3d(sRing + st * ly.stage_bytes + i * bytes, m, bar_full + 8 * st, c0,
+                      c1 + i * row_step, c2);
+        ++issued_n;
+        if (++st == NST) {
+          st = 0;
+          ph ^= 1u;
+        }
+      };
+      int vloads = 0;  // layer-vector copies issued
+      auto layer_ptr = [&](const float* v, size_t stride, int l) {
+        return reinterpret_cast<const uint8_t*>(v) + (size_t)l * stride;
       };
       for (int l = 0; l < p.L && ok; ++l) {
+        // This layer's vectors into buffer l & 1 once the workers released layer l - 2's.
+        const int vb = l & 1;
+        if (l >= 2 && !mbar_wait(bar_vempty + 8 * vb, (uint32_t)(((l >> 1) - 1) & 1), abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dv = sVec + (uint32_t)(vb * ly.vec_bytes);
+        const uint32_t vbar = bar_vfull + 8 * vb;
+        mbar_arrive_expect_tx(vbar, (uint32_t)ly.vec_bytes);
+        bulk_load(dv + 4 * ly.v_bq, layer_ptr(p.bqkv, p.fold_stride, l), 12 * Q, vbar);
+        bulk_load(dv + 4 * ly.v_cq, layer_ptr(p.cqkv, p.fold_stride, l), 12 * Q, vbar);
+        bulk_load(dv + 4 * ly.v_bo, layer_ptr(p.bo, p.layer_stride, l), 4 * D, vbar);
+        bulk_load(dv + 4 * ly.v_b1, layer_ptr(p.b1, p.fold_stride, l), 4 * F, vbar);
+        bulk_load(dv + 4 * ly.v_c1, layer_ptr(p.c1, p.fold_stride, l), 4 * F, vbar);
+        bulk_load(dv + 4 * ly.v_b2, layer_ptr(p.b2, p.layer_stride, l), 4 * D, vbar);
+        ++vloads;
         for (int h = 0; h < H && ok; ++h) {
-          for (int kc = 0; kc < ly.KC; ++kc)
-            for (int part = 0; part < 3; ++part)
-              load(&tmWqkv, kc * 64, part * Q + h * HP, l, HP * 128);
+          for (int kc = 0; kc < ly.KC; ++kc) {
+            if (ly.qkv_merged) {
+              load(&tmWqkv, kc * 64, h * HP, l, HP * 128, 3, Q);
+            } else {
+              for (int part = 0; part < 3; ++part)
+                load(&tmWqkv, kc * 64, part * Q + h * HP, l, HP * 128);
+            }
+          }
           for (int nh = 0; nh < ly.NH; ++nh)
             for (int kk = 0; kk < KW; ++kk)
               load(&tmWo, h * HP + kk * 64, nh * ly.NB, l, ly.NB * WOC * 2);
@@ -195,25 +240,36 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       if (!ok) {
         *abort_flag = 1;
         report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
-        for (long j = u > RES_STAGES ? u - RES_STAGES : 0; j < u; ++j)
-          mbar_wait(bar_full + 8 * (int)(j % RES_STAGES), (uint32_t)((j / RES_STAGES) & 1),
-                    nullptr, limit);
+        // Let the boxes in flight (the last min(issued, NST)) land before the CTA exits.
+        for (int j = 0; j < NST && j < issued_n; ++j) {
+          if (--st < 0) {
+            st = NST - 1;
+            ph ^= 1u;
+          }
+          mbar_wait(bar_full + 8 * st, ph, nullptr, limit);
+        }
+        for (int j = vloads > 2 ? vloads - 2 : 0; j < vloads; ++j)
+          mbar_wait(bar_vfull + 8 * (j & 1), (uint32_t)((j >> 1) & 1), nullptr, limit);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    long u = 0, step = 0;
+    long step = 0;
+    int st_c = 0;  // ring position of the next box to consume
+    uint32_t ph_c = 0;
     bool ok = true, issued = false;
-    auto wait = [&](uint32_t bar, uint32_t parity) -> bool {
+    // `tc_sync`: the barrier publishes worker writes to TMEM / shared memory, which the
+    // following MMAs must see (tcgen05 fence); a weight box landed by TMA needs none.
+    auto wait = [&](uint32_t bar, uint32_t parity, bool tc_sync = false) -> bool {
       if (!ok) return false;
       if (!__all_sync(FULL, mbar_wait(bar, parity, abort_flag, limit))) {
         ok = false;
         return false;
       }
-      tc_fence_after();
+      if (tc_sync) tc_fence_after();
       return true;
     };
-    auto ready = [&]() -> bool { return wait(bar_ready, (uint32_t)(step & 1)); };
+    auto ready = [&]() -> bool { return wait(bar_ready, (uint32_t)(step & 1), true); };
     auto done = [&]() {
       if (!ok) return;
       mma_commit_warp(bar_done);
@@ -221,29 +277,44 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     };
     // Consume the next weight box: issue(box address), then release its stage.
     auto unit = [&](auto&& issue) {
-      const int st = (int)(u % RES_STAGES);
-      if (!wait(bar_full + 8 * st, (uint32_t)((u / RES_STAGES) & 1))) return;
-      issue(sRing + st * RES_STAGE_BYTES);
-      mma_commit_warp(bar_empty + 8 * st);
+      if (!wait(bar_full + 8 * st_c, ph_c)) return;
+      issue(sRing + st_c * ly.stage_bytes);
+      mma_commit_warp(bar_empty + 8 * st_c);
       issued = true;
-      ++u;
+      if (++st_c == NST) {
+        st_c = 0;
+        ph_c ^= 1u;
+      }
     };
     const uint32_t id_qkv = idesc_f16_f32(RES_ROWS, HP);
     const uint32_t id_res = idesc_f16_f32(RES_ROWS, ly.NB);
     const uint32_t id_s = idesc_f16_f32(RES_ROWS, 128);
     const uint32_t id_pv = idesc_f16_f32(RES_ROWS, HP, 0, 1);
     const uint32_t id_ffn = idesc_f16_f32(RES_ROWS, ly.FC);
+    const uint32_t id_qkv3 = idesc_f16_f32(RES_ROWS, 3 * HP);
     auto qkv = [&]() {
-      for (int kc = 0; kc < ly.KC; ++kc)
-        for (int part = 0; part < 3; ++part)
+      for (int kc = 0; kc < ly.KC; ++kc) {
+        const uint64_t ad = desc_kmajor_sw128(sXA + (uint32_t)(kc * RES_ROWS * 128));
+        if (ly.qkv_merged) {
+          // q | k | v weight rows stacked in the stage: one N = 3 hp group.
           unit([&](uint32_t w) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma_f16_ss_warp(tmem + (uint32_t)(A0 + part * HP),
-                              desc_kmajor_sw128(sXA + (uint32_t)(kc * RES_ROWS * 128)) + (uint64_t)(2 * k),
-                              desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_qkv,
+              mma_f16_ss_warp(tmem + (uint32_t)A0, ad + (uint64_t)(2 * k),
+                              desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_qkv3,
                               (kc > 0 || k > 0) ? 1u : 0u);
           });
+        } else {
+          for (int part = 0; part < 3; ++part)
+            unit([&](uint32_t w) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma_f16_ss_warp(tmem + (uint32_t)(A0 + part * HP), ad + (uint64_t)(2 * k),
+                                desc_kmajor_sw128(w) + (uint64_t)(2 * k), id_qkv,
+                                (kc > 0 || k > 0) ? 1u : 0u);
+            });
+        }
+      }
     };
     auto out_proj = [&]() {  // A = this head's attention output (in the q tile)
       for (int nh = 0; nh < ly.NH; ++nh)
@@ -345,8 +416,10 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
 
     auto wsync = [&]() -> bool {
       if (!ok) return false;
+      tc_fence_before();
       mbar_arrive(bar_wsync);
       if (!mbar_wait(bar_wsync, (uint32_t)(ws & 1), abort_flag, limit)) ok = false;
+      tc_fence_after();
       ++ws;
       return ok;
     };
@@ -364,9 +437,10 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     };
 
     // Zero the operand buffers once: columns past D / F in the last 64-column box
-    // meet zero-filled weight columns and must hold finite values.
+    // meet zero-filled weight columns and must hold finite values.  (Only up to the
+    // vector buffers, which the producer is already filling.)
     {
-      const uint32_t n16 = (uint32_t)(ly.ring - ly.xa) / 16;
+      const uint32_t n16 = (uint32_t)(ly.vec - ly.xa) / 16;
       for (uint32_t i = (uint32_t)wt; i < n16; i += RES_WORKERS)
         asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(sXA + i * 16), "r"(0u)
                      : "memory");
@@ -438,7 +512,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           const float4* b4 = reinterpret_cast<const float4*>(pbias + c * 32);
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const float4 t = __ldg(b4 + k);
+            const float4 t = b4[k];
             bb[4 * k] = t.x; bb[4 * k + 1] = t.y; bb[4 * k + 2] = t.z; bb[4 * k + 3] = t.w;
           }
         }
@@ -468,16 +542,22 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       return true;
     };
 
-    auto layer_vec = [&](const float* v, size_t stride, int l) {
-      return reinterpret_cast<const float*>(reinterpret_cast<const uint8_t*>(v) + (size_t)l * stride);
-    };
+    // Layer l's vectors in shared memory (buffer l & 1).
+    auto layer_vec = [&](int l) { return vec_smem + (size_t)(l & 1) * ly.v_floats; };
 
     float mean = 0.f, rstd = 0.f;
     for (int l = 0; l < p.L && ok; ++l) {
-      const float* bq = layer_vec(p.bqkv, p.fold_stride, l);
-      const float* cq = layer_vec(p.cqkv, p.fold_stride, l);
+      if (!mbar_wait(bar_vfull + 8 * (l & 1), (uint32_t)((l >> 1) & 1), abort_flag, limit)) {
+        ok = false;
+        break;
+      }
+      const float* V = layer_vec(l);
+      const float* bq = V + ly.v_bq;
+      const float* cq = V + ly.v_cq;
       // LN1 statistics (the previous block's ffn_out bias is still pending in TMEM).
-      if (!ln_pass(l > 0 ? layer_vec(p.b2, p.layer_stride, l - 1) : nullptr, true, mean, rstd)) break;
+      if (!ln_pass(l > 0 ? layer_vec(l - 1) + ly.v_b2 : nullptr, true, mean, rstd)) break;
+      // Layer l - 1's vectors are no longer needed: the producer may reuse the buffer.
+      if (l > 0) mbar_arrive(bar_vempty + 8 * ((l - 1) & 1));
       if (!step_sync()) break;  // -> QKV(0) done
       for (int h = 0; h < H && ok; ++h) {
         // q | k | v of head h: folded LayerNorm epilogue, fp16 into the operand tiles.
@@ -489,8 +569,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           float cs[32], bb[32];
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
-            const float4 t = __ldg(reinterpret_cast<const float4*>(cq + n0) + k);
-            const float4 w = __ldg(reinterpret_cast<const float4*>(bq + n0) + k);
+            const float4 t = reinterpret_cast<const float4*>(cq + n0)[k];
+            const float4 w = reinterpret_cast<const float4*>(bq + n0)[k];
             cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
             bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
           }
@@ -504,45 +584,88 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           for (int j = 0; j < 4; ++j) res_store_tile<HP>(tile, r, cc * 32 + 8 * j, res_pack8(v + 8 * j));
         }
         if (!step_sync()) break;  // -> S = q k^T done
-        // Softmax of the row (one warp per quadrant), P written over the scores.
-        if (half == 0) {
-          uint32_t sv[128];
+        // Softmax of the row, split over both halves: half `half` takes keys
+        // 64 half .. 64 half + 63 (S chunks 2 half, 2 half + 1) and writes their P over
+        // TMEM columns 32 half .. 32 half + 31; the two partial maxima and sums meet in
+        // shared memory.  A 32-key chunk that every row of the warp masks (causal, or
+        // past the sequence end) is neither read nor exponentiated: its P is zero.
+        {
+          const int lim = p.causal ? min(len - 1, r) : len - 1;  // keys k > lim masked
+          const int wlim = p.causal ? min(len - 1, quad * 32 + 31) : len - 1;  // warp max
+          const float sc = p.scale_log2;
+          uint32_t sv[64];
+          bool act[2];
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t chunk[32];
-            tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + c * 32), chunk);
+          for (int cc = 0; cc < 2; ++cc) {
+            const int k0 = (2 * half + cc) * 32;
+            act[cc] = k0 <= wlim;  // warp-uniform
+            if (act[cc]) {
+              uint32_t chunk[32];
+              tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + k0), chunk);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = chunk[e];
+              for (int e = 0; e < 32; ++e) sv[cc * 32 + e] = chunk[e];
+            }
           }
           tmem_wait_ld();
-          const int lim = p.causal ? min(len - 1, r) : len - 1;  // keys c > lim masked
-          float mx = -INFINITY;
+          float pm[8];
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (c <= lim) mx = fmaxf(mx, __uint_as_float(sv[c]));
-          const float base_v = mx == -INFINITY ? 0.f : mx * p.scale_log2;
-          float lsum = 0.f;
-          uint32_t pk[64];
+          for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
 #pragma unroll
-          for (int c = 0; c < 64; ++c) {
-            const float p0 = (2 * c <= lim) ? ex2_approx(fmaf(__uint_as_float(sv[2 * c]), p.scale_log2, -base_v)) : 0.f;
-            const float p1 = (2 * c + 1 <= lim) ? ex2_approx(fmaf(__uint_as_float(sv[2 * c + 1]), p.scale_log2, -base_v)) : 0.f;
-            lsum += p0 + p1;
-            pk[c] = pack_half2(p0, p1);
+          for (int cc = 0; cc < 2; ++cc) {
+            if (!act[cc]) continue;
+            const int k0 = (2 * half + cc) * 32;
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (k0 + e <= lim) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(sv[cc * 32 + e]));
+          }
+          const float mh = fmaxf(fmax3f(pm[0], pm[1], pm[2]), fmaxf(fmax3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+          rowmax[half * RES_ROWS + r] = mh;
+          if (!wsync()) break;
+          const float mx = fmaxf(rowmax[r], rowmax[RES_ROWS + r]);
+          const float base_v = mx == -INFINITY ? 0.f : mx * sc;
+          const float2 sc2 = make_float2(sc, sc), nb2 = make_float2(-base_v, -base_v);
+          unsigned long long ps2[2] = {0ull, 0ull};
+          uint32_t pk[32];
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int k0 = (2 * half + cc) * 32;
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              float p0 = 0.f, p1 = 0.f;
+              if (act[cc]) {
+                const float2 x = ffma2(make_float2(__uint_as_float(sv[cc * 32 + 2 * c]),
+                                                   __uint_as_float(sv[cc * 32 + 2 * c + 1])), sc2, nb2);
+                // One pair in four on the FMA pipe: the exponentials (MUFU) bound this loop.
+                if ((c & 3) == 3) {
+                  const float2 e2 = exp2_fma2(x);
+                  p0 = e2.x;
+                  p1 = e2.y;
+                } else {
+                  p0 = ex2_approx(x.x);
+                  p1 = ex2_approx(x.y);
+                }
+                if (k0 + 2 * c > lim) p0 = 0.f;
+                if (k0 + 2 * c + 1 > lim) p1 = 0.f;
+              }
+              ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
+              pk[cc * 16 + c] = pack_half2(p0, p1);
+            }
           }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 2; ++q) {
             uint32_t chunk[16];
 #pragma unroll
             for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
-            tmem_st_32x32b_x16(tr + (uint32_t)(A0 + q * 16), chunk);
+            tmem_st_32x32b_x16(tr + (uint32_t)(A0 + half * 32 + q * 16), chunk);
           }
-          invl[r] = lsum > 0.f ? 1.f / lsum : 0.f;
+          const float2 rs = upk2(add2p(ps2[0], ps2[1]));
+          rowsum[half * RES_ROWS + r] = rs.x + rs.y;
         }
         if (!step_sync()) break;  // -> O = P v done
-        if (!wsync()) break;      // 1 / row sum visible to both halves
+        if (!wsync()) break;      // both halves' row sums visible
         {
-          const float inv = invl[r];
+          const float lsum = rowsum[r] + rowsum[RES_ROWS + r];
+          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
           for (int i = half; i < HP / 32; i += 2) {
             uint32_t u[32];
             tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + 128 + i * 32), u);
@@ -558,10 +681,10 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       }
       if (!ok) break;
       // LN2 statistics (out_proj bias pending), fp16 copy for ffn_in.
-      if (!ln_pass(layer_vec(p.bo, p.layer_stride, l), true, mean, rstd)) break;
+      if (!ln_pass(V + ly.v_bo, true, mean, rstd)) break;
       if (!step_sync()) break;  // -> ffn_in(0) done
-      const float* b1 = layer_vec(p.b1, p.fold_stride, l);
-      const float* c1 = layer_vec(p.c1, p.fold_stride, l);
+      const float* b1 = V + ly.v_b1;
+      const float* c1 = V + ly.v_c1;
       for (int c = 0; c < ly.NF && ok; ++c) {
         for (int i = half; i < ly.FC / 32; i += 2) {
           const int n0 = c * ly.FC + i * 32;
@@ -572,8 +695,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
             float cs[32], bb[32];
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(c1 + n0) + k);
-              const float4 w = __ldg(reinterpret_cast<const float4*>(b1 + n0) + k);
+              const float4 t = reinterpret_cast<const float4*>(c1 + n0)[k];
+              const float4 w = reinterpret_cast<const float4*>(b1 + n0)[k];
               cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
               bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
             }
@@ -598,7 +721,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     }
 
     // Final LayerNorm of the valid rows into out; masked positions are written as zeros.
-    if (ok && ln_pass(layer_vec(p.b2, p.layer_stride, p.L - 1), false, mean, rstd)) {
+    if (ok && ln_pass(layer_vec(p.L - 1) + ly.v_b2, false, mean, rstd)) {
       // tcgen05.ld is warp-wide: every lane loads, only valid rows store.
       const int dst = row_valid ? pos[r] : 0;
       for (int c = half; c < nchunk; c += 2) {

@@ -157,13 +157,24 @@ class B200Transformer(nn.Module):
             self._plans[key] = plan
         return plan
 
-    def set_layerwise(self, layerwise: bool) -> None:
-        """Force the layer-by-layer kernels (True) or let each shape pick (False, the
-        default: sequences of <= 128 tokens run the whole stack in one resident launch
-        when the shape fits)."""
-        self._path = _lib.PATH_LAYERWISE if layerwise else _lib.PATH_AUTO
-        for plan in self._plans.values():
-            _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, self._path), "set_path")
+    def set_path(self, path: str) -> None:
+        """Forward path for every shape: "auto" (default: the resident whole-stack
+        kernel for short sequences of small layers, where it is faster, else layer by
+        layer), "layerwise", or "resident" (whenever it fits; shapes it does not fit
+        raise ValueError when their plan is built or used)."""
+        if path not in _lib.PATHS:
+            raise ValueError(f"path must be one of {sorted(_lib.PATHS)}, got {path!r}")
+        new = _lib.PATHS[path]
+        done = []
+        try:
+            for plan in self._plans.values():
+                _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, new), "set_path")
+                done.append(plan)
+        except Exception:
+            for plan in done:  # all or nothing
+                _lib.lib().tttj_plan_set_path(plan.handle, self._path)
+            raise
+        self._path = new
 
     def uses_resident(self, batch: int, seq_len: int) -> bool:
         """Whether a forward of shape [batch, seq_len] runs the resident-stack kernel."""

@@ -507,24 +507,20 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       for (int c = half; c < nchunk; c += 2) {
         uint32_t u[32];
         tmem_ld_32x32b_x32(tr + (uint32_t)(c * 32), u);
-        float bb[32];
-        if (pbias) {
-          const float4* b4 = reinterpret_cast<const float4*>(pbias + c * 32);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float4 t = b4[k];
-            bb[4 * k] = t.x; bb[4 * k + 1] = t.y; bb[4 * k + 2] = t.z; bb[4 * k + 3] = t.w;
-          }
-        }
         tmem_wait_ld();
         float v[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          float t = __uint_as_float(u[e]);
-          if (pbias) t += bb[e];
-          v[e] = row_valid ? t : 0.f;
-          s += v[e];
-          q = fmaf(v[e], v[e], q);
+        for (int k = 0; k < 8; ++k) {
+          const float4 bb = pbias ? reinterpret_cast<const float4*>(pbias + c * 32)[k]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+          const float t4[4] = {__uint_as_float(u[4 * k]) + bb.x, __uint_as_float(u[4 * k + 1]) + bb.y,
+                               __uint_as_float(u[4 * k + 2]) + bb.z, __uint_as_float(u[4 * k + 3]) + bb.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            v[4 * k + e] = row_valid ? t4[e] : 0.f;
+            s += v[4 * k + e];
+            q = fmaf(v[4 * k + e], v[4 * k + e], q);
+          }
         }
         if (store_back) res_tmem_st_f32(tr + (uint32_t)(c * 32), v);
         if (write_xa) {
@@ -566,22 +562,23 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           uint32_t u[32];
           tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + i * 32), u);
           const int n0 = part * Q + h * HP + cc * 32;
-          float cs[32], bb[32];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const float4 t = reinterpret_cast<const float4*>(cq + n0)[k];
-            const float4 w = reinterpret_cast<const float4*>(bq + n0)[k];
-            cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
-            bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
-          }
           tmem_wait_ld();
-          float v[32];
-#pragma unroll
-          for (int e = 0; e < 32; ++e)
-            v[e] = fmaf(rstd, fmaf(-mean, cs[e], __uint_as_float(u[e])), bb[e]);
           const uint32_t tile = part == 0 ? sQ : part == 1 ? sK : sV;
+          // 8 columns at a time, the vectors read from shared memory as needed (few
+          // live registers: no spills).
 #pragma unroll
-          for (int j = 0; j < 4; ++j) res_store_tile<HP>(tile, r, cc * 32 + 8 * j, res_pack8(v + 8 * j));
+          for (int j = 0; j < 4; ++j) {
+            const float4* c4 = reinterpret_cast<const float4*>(cq + n0 + 8 * j);
+            const float4* b4 = reinterpret_cast<const float4*>(bq + n0 + 8 * j);
+            const float4 c0 = c4[0], c1v = c4[1], b0 = b4[0], b1v = b4[1];
+            const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1v.x, c1v.y, c1v.z, c1v.w};
+            const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1v.x, b1v.y, b1v.z, b1v.w};
+            float v[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              v[e] = fmaf(rstd, fmaf(-mean, cs[e], __uint_as_float(u[8 * j + e])), bb[e]);
+            res_store_tile<HP>(tile, r, cc * 32 + 8 * j, res_pack8(v));
+          }
         }
         if (!step_sync()) break;  // -> S = q k^T done
         // Softmax of the row, split over both halves: half `half` takes keys
@@ -692,21 +689,19 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + i * 32), u);
           float v[32];
           if (n0 < F) {  // F is a multiple of 32: a 32-column group is all in or all out
-            float cs[32], bb[32];
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float4 t = reinterpret_cast<const float4*>(c1 + n0)[k];
-              const float4 w = reinterpret_cast<const float4*>(b1 + n0)[k];
-              cs[4 * k] = t.x; cs[4 * k + 1] = t.y; cs[4 * k + 2] = t.z; cs[4 * k + 3] = t.w;
-              bb[4 * k] = w.x; bb[4 * k + 1] = w.y; bb[4 * k + 2] = w.z; bb[4 * k + 3] = w.w;
-            }
             tmem_wait_ld();
 #pragma unroll
-            for (int e = 0; e < 32; e += 2) {
-              const float2 g = gelu_erf2(fmaf(rstd, fmaf(-mean, cs[e], __uint_as_float(u[e])), bb[e]),
-                                         fmaf(rstd, fmaf(-mean, cs[e + 1], __uint_as_float(u[e + 1])), bb[e + 1]));
-              v[e] = g.x;
-              v[e + 1] = g.y;
+            for (int j = 0; j < 8; ++j) {  // 4 columns at a time, vectors from shared memory
+              const float4 cs = reinterpret_cast<const float4*>(c1 + n0)[j];
+              const float4 bb = reinterpret_cast<const float4*>(b1 + n0)[j];
+              const float2 g0 = gelu_erf2(fmaf(rstd, fmaf(-mean, cs.x, __uint_as_float(u[4 * j])), bb.x),
+                                          fmaf(rstd, fmaf(-mean, cs.y, __uint_as_float(u[4 * j + 1])), bb.y));
+              const float2 g1 = gelu_erf2(fmaf(rstd, fmaf(-mean, cs.z, __uint_as_float(u[4 * j + 2])), bb.z),
+                                          fmaf(rstd, fmaf(-mean, cs.w, __uint_as_float(u[4 * j + 3])), bb.w));
+              v[4 * j] = g0.x;
+              v[4 * j + 1] = g0.y;
+              v[4 * j + 2] = g1.x;
+              v[4 * j + 3] = g1.y;
             }
           } else {
             tmem_wait_ld();

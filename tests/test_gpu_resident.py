@@ -33,6 +33,8 @@ SHAPES = {
     "case12_s32": (64, 32, 128, 4, 128, 4, True, torch.float16, "prefix"),
     "holes_f192": (6, 100, 128, 2, 192, 2, False, torch.float16, "holes"),
     "empty_seq": (3, 64, 64, 2, 160, 2, True, torch.float16, "empty"),
+    # odd head count: one head per attention step (even counts of 32-wide heads pair up)
+    "odd_heads_d96": (4, 100, 96, 3, 96, 2, True, torch.float16, "prefix"),
 }
 
 

@@ -379,17 +379,27 @@ int check_config(const tttj_config* c) {
 // the residual (d_model fp32 columns) plus the largest step accumulator inside TMEM's
 // 512 columns, residual MMA groups of d_model <= 128 or two of 128, and the shared
 // memory layout within the 227 KB per CTA.
+// TMEM columns a resident step needs after the residual, for `gh` heads per step.
+int resident_acc_cols(int hp, int gh, int F) {
+  const int fc = F < 128 ? F : 128;
+  int acc = 3 * gh * hp;                                  // q | k | v
+  if (gh * (128 + hp) > acc) acc = gh * (128 + hp);       // S (P over it) and O
+  return fc > acc ? fc : acc;                             // one FFN chunk
+}
+// Heads per attention step: pairs for hp 32 with an even head count when TMEM allows.
+int resident_gh(const tttj_config& c) {
+  const int hp = layout_hd(c);
+  return (hp == 32 && c.num_heads % 2 == 0 &&
+          c.d_model + resident_acc_cols(hp, 2, c.ffn_dim) <= 512) ? 2 : 1;
+}
 bool resident_fits(const tttj_config& c) {
   const int D = c.d_model, hp = layout_hd(c), F = c.ffn_dim;
   if (c.seq_len > RES_ROWS) return false;
   if (!(D <= 128 || D == 256) || D % 32) return false;
   if (hp != 32 && hp != 64 && hp != 128) return false;
-  const int fc = F < 128 ? F : 128;
-  int acc = 3 * hp;
-  if (128 + hp > acc) acc = 128 + hp;
-  if (fc > acc) acc = fc;
-  if (D + acc > 512) return false;
-  return res_layout(D, F, hp, c.num_heads * hp).stages >= 3;
+  const int gh = resident_gh(c);
+  if (D + resident_acc_cols(hp, gh, F) > 512) return false;
+  return res_layout(D, F, hp, c.num_heads * hp, gh).stages >= 3;
 }
 
 // Whether TTTJ_PATH_AUTO takes the resident kernel for a shape it fits.  One CTA works
@@ -400,7 +410,7 @@ bool resident_fits(const tttj_config& c) {
 // and slower beyond (case 11: 16 heads; C1: 1.6 MB of weights per layer).
 bool resident_preferred(const tttj_config& c) {
   const long D = c.d_model, F = c.ffn_dim, Q = (long)qkv_width(c);
-  const long steps = 3l * c.num_heads + 3 + (F + 127) / 128;
+  const long steps = 3l * c.num_heads / resident_gh(c) + 3 + (F + 127) / 128;
   const long weight_bytes = 2 * (3 * Q * D + D * Q + 2 * D * F);
   return steps <= 24 && weight_bytes <= 512 * 1024;
 }
@@ -495,7 +505,8 @@ void destroy_events(tttj_plan* p) {
 int build_resident(tttj_plan* p, const FoldLayout& fl) {
   const tttj_config& c = p->cfg;
   const int D = c.d_model, F = c.ffn_dim, hp = layout_hd(c), Q = (int)qkv_width(c), L = c.num_layers;
-  const ResLayout ly = res_layout(D, F, hp, Q);
+  const int gh = resident_gh(c);
+  const ResLayout ly = res_layout(D, F, hp, Q, gh);
   const uint8_t* fold = p->ws + p->lay.fold;
   const size_t fstride = p->lay.fold_layer, lstride = layer_stride(c);
   auto W = [&](int field) -> const uint8_t* {
@@ -505,8 +516,9 @@ int build_resident(tttj_plan* p, const FoldLayout& fl) {
   };
   ResLaunch& r = p->res;
   std::memset(&r, 0, sizeof(r));
-  int rc = make_tmap_3d(&r.tmWqkv, fold + fl.wqkv, (uint64_t)3 * Q, D, D, L, fstride, 64, hp,
-                        CU_TENSOR_MAP_SWIZZLE_128B);
+  // Wqkv boxes: the q (k, v) rows of the gh heads of one attention step.
+  int rc = make_tmap_3d(&r.tmWqkv, fold + fl.wqkv, (uint64_t)3 * Q, D, D, L, fstride, 64,
+                        (uint32_t)(ly.qkv_merged ? gh * hp : hp), CU_TENSOR_MAP_SWIZZLE_128B);
   const uint32_t woc = hp < 64 ? hp : 64;
   const CUtensorMapSwizzle wosw = hp < 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   if (!rc) {
@@ -530,6 +542,7 @@ int build_resident(tttj_plan* p, const FoldLayout& fl) {
   q.L = L;
   q.causal = c.causal ? 1 : 0;
   q.hp = hp;
+  q.gh = gh;
   q.Q = Q;
   q.scale_log2 = (1.0f / sqrtf((float)head_dim_of(c))) * 1.4426950408889634f;
   q.eps = kLnEps;

@@ -116,6 +116,7 @@ struct ResParams {
   int x_f32;              // 1: x and out are fp32
   int B, S, D, H, F, L, causal;
   int hp;                 // layout head dim (32, 64, 128)
+  int gh;                 // heads per attention step (2: head pairs, hp 32, even H)
   int Q;                  // H * hp: width of each of the q | k | v weight blocks
   float scale_log2;       // hd^-0.5 * log2(e)
   float eps;
@@ -146,6 +147,7 @@ struct ResLayout {
   int KC;     // 64-column K chunks of D
   int NF;     // FFN chunks
   int tile;   // bytes of one [128 x hp] operand tile
+  int gh;     // heads per attention step: 2 ("head pairs", hp 32 only) or 1
   // One layer's vectors, in floats: bqkv [3Q] cqkv [3Q] bo [D] b1 [F] c1 [F] b2 [D].
   int v_bq, v_cq, v_bo, v_b1, v_c1, v_b2, v_floats;
   int vec_bytes;  // one layer's block (two are kept: layer l in buffer l & 1)
@@ -157,7 +159,7 @@ struct ResLayout {
   int xa, qkvh, vec, ring, misc, total;
 };
 
-__host__ __device__ inline ResLayout res_layout(int D, int F, int hp, int Q) {
+__host__ __device__ inline ResLayout res_layout(int D, int F, int hp, int Q, int gh) {
   ResLayout y;
   y.Dp = (D + 63) / 64 * 64;
   y.FC = F < 128 ? F : 128;
@@ -167,6 +169,7 @@ __host__ __device__ inline ResLayout res_layout(int D, int F, int hp, int Q) {
   y.KC = y.Dp / 64;
   y.NF = (F + y.FC - 1) / y.FC;
   y.tile = RES_ROWS * hp * 2;
+  y.gh = gh;
   y.v_bq = 0;
   y.v_cq = 3 * Q;
   y.v_bo = 6 * Q;
@@ -175,14 +178,14 @@ __host__ __device__ inline ResLayout res_layout(int D, int F, int hp, int Q) {
   y.v_b2 = 6 * Q + D + 2 * F;
   y.v_floats = 6 * Q + 2 * D + 2 * F;
   y.vec_bytes = y.v_floats * 4;
-  const int qkv = 3 * y.tile, hbuf = RES_ROWS * y.FCp * 2;
+  const int qkv = 3 * gh * y.tile, hbuf = RES_ROWS * y.FCp * 2;
   y.xa = 0;
   y.qkvh = y.xa + RES_ROWS * y.Dp * 2;
   y.vec = y.qkvh + (qkv > hbuf ? qkv : hbuf);
   y.ring = y.vec + (2 * y.vec_bytes + 1023) / 1024 * 1024;
   y.qkv_merged = hp <= 64;
   y.stage_bytes = RES_STAGE_BYTES;
-  if (y.qkv_merged && 3 * hp * 128 > y.stage_bytes) y.stage_bytes = 3 * hp * 128;
+  if (y.qkv_merged && 3 * gh * hp * 128 > y.stage_bytes) y.stage_bytes = 3 * gh * hp * 128;
   const int room = RES_SMEM_LIMIT - 1024 - RES_MISC_BYTES - y.ring;
   y.stages = room / y.stage_bytes;
   if (y.stages > RES_MAX_STAGES) y.stages = RES_MAX_STAGES;

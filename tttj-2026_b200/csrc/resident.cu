@@ -5,12 +5,12 @@
 namespace tttj {
 
 namespace {
-template <int HP>
+template <int HP, bool PAIR>
 cudaError_t launch_res(const ResLaunch& r, cudaStream_t stream) {
-  auto kern = resident_stack_kernel<HP>;
+  auto kern = resident_stack_kernel<HP, PAIR>;
   // At least half the SM's shared memory: one CTA per SM, so a CTA never waits for
   // another to release the 512 TMEM columns it allocates.
-  int smem = res_layout(r.p.D, r.p.F, HP, r.p.Q).total;
+  int smem = res_layout(r.p.D, r.p.F, HP, r.p.Q, PAIR ? 2 : 1).total;
   if (smem < 116 * 1024) smem = 116 * 1024;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
@@ -22,9 +22,9 @@ cudaError_t launch_res(const ResLaunch& r, cudaStream_t stream) {
 cudaError_t resident_launch(const ResLaunch& r, cudaStream_t stream) {
   if (r.p.B <= 0) return cudaSuccess;
   switch (r.p.hp) {
-    case 32: return launch_res<32>(r, stream);
-    case 64: return launch_res<64>(r, stream);
-    case 128: return launch_res<128>(r, stream);
+    case 32: return r.p.gh == 2 ? launch_res<32, true>(r, stream) : launch_res<32, false>(r, stream);
+    case 64: return launch_res<64, false>(r, stream);
+    case 128: return launch_res<128, false>(r, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -93,7 +93,10 @@ __device__ __forceinline__ uint4 res_pack8(const float* v) {
                     pack_half2(v[6], v[7]));
 }
 
-template <int HP>
+// PAIR (hp 32, even H): attention works on two heads per step; worker half j takes head
+// j of the pair (a full 128-key row per thread), so the three attention steps and
+// their hand-offs are shared by two heads.
+template <int HP, bool PAIR>
 __global__ void __launch_bounds__(RES_THREADS, 1)
     resident_stack_kernel(const __grid_constant__ CUtensorMap tmWqkv,
                           const __grid_constant__ CUtensorMap tmWo,
@@ -102,7 +105,9 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   constexpr unsigned FULL = 0xffffffffu;
   constexpr int WOC = HP < 64 ? HP : 64;        // columns of one out_proj weight box
   constexpr int KW = HP / WOC;                  // out_proj boxes per head and column group
-  const ResLayout ly = res_layout(p.D, p.F, HP, p.Q);
+  constexpr int GH = PAIR ? 2 : 1;              // heads per attention step
+  static_assert(!PAIR || HP == 32, "head pairs are built for hp 32");
+  const ResLayout ly = res_layout(p.D, p.F, HP, p.Q, GH);
   const int NST = ly.stages;
   const int D = p.D, F = p.F, Q = p.Q, H = p.H;
   const int A0 = D;  // first TMEM column after the residual
@@ -113,7 +118,9 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   uint8_t* smem = smem_raw + pad;
   const uint32_t base = raw + pad;
   const uint32_t sXA = base + ly.xa;
-  const uint32_t sQ = base + ly.qkvh, sK = sQ + ly.tile, sV = sK + ly.tile, sH = sQ;
+  // q / k / v tiles of the heads of one step: tile (part, j) of head j of the group.
+  const uint32_t sQKV = base + ly.qkvh, sH = sQKV;
+  auto tile_of = [&](int part, int j) { return sQKV + (uint32_t)((part * GH + j) * ly.tile); };
   const uint32_t sRing = base + ly.ring;
   const uint32_t sVec = base + ly.vec;
   const float* vec_smem = reinterpret_cast<const float*>(smem + ly.vec);
@@ -217,18 +224,19 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
         bulk_load(dv + 4 * ly.v_c1, layer_ptr(p.c1, p.fold_stride, l), 4 * F, vbar);
         bulk_load(dv + 4 * ly.v_b2, layer_ptr(p.b2, p.layer_stride, l), 4 * D, vbar);
         ++vloads;
-        for (int h = 0; h < H && ok; ++h) {
+        for (int h0 = 0; h0 < H && ok; h0 += GH) {
           for (int kc = 0; kc < ly.KC; ++kc) {
-            if (ly.qkv_merged) {
-              load(&tmWqkv, kc * 64, h * HP, l, HP * 128, 3, Q);
+            if (ly.qkv_merged) {  // boxes of GH * hp rows: q, k, v of the step's heads
+              load(&tmWqkv, kc * 64, h0 * HP, l, GH * HP * 128, 3, Q);
             } else {
               for (int part = 0; part < 3; ++part)
-                load(&tmWqkv, kc * 64, part * Q + h * HP, l, HP * 128);
+                load(&tmWqkv, kc * 64, part * Q + h0 * HP, l, HP * 128);
             }
           }
-          for (int nh = 0; nh < ly.NH; ++nh)
-            for (int kk = 0; kk < KW; ++kk)
-              load(&tmWo, h * HP + kk * 64, nh * ly.NB, l, ly.NB * WOC * 2);
+          for (int j = 0; j < GH; ++j)
+            for (int nh = 0; nh < ly.NH; ++nh)
+              for (int kk = 0; kk < KW; ++kk)
+                load(&tmWo, (h0 + j) * HP + kk * 64, nh * ly.NB, l, ly.NB * WOC * 2);
         }
         for (int c = 0; c < ly.NF && ok; ++c) {
           for (int kc = 0; kc < ly.KC; ++kc) load(&tmW1, kc * 64, c * ly.FC, l, ly.FC * 128);
@@ -291,12 +299,12 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     const uint32_t id_s = idesc_f16_f32(RES_ROWS, 128);
     const uint32_t id_pv = idesc_f16_f32(RES_ROWS, HP, 0, 1);
     const uint32_t id_ffn = idesc_f16_f32(RES_ROWS, ly.FC);
-    const uint32_t id_qkv3 = idesc_f16_f32(RES_ROWS, 3 * HP);
+    const uint32_t id_qkv3 = idesc_f16_f32(RES_ROWS, 3 * GH * HP);
     auto qkv = [&]() {
       for (int kc = 0; kc < ly.KC; ++kc) {
         const uint64_t ad = desc_kmajor_sw128(sXA + (uint32_t)(kc * RES_ROWS * 128));
         if (ly.qkv_merged) {
-          // q | k | v weight rows stacked in the stage: one N = 3 hp group.
+          // q | k | v weight rows stacked in the stage: one N = 3 GH hp group.
           unit([&](uint32_t w) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -316,34 +324,44 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
         }
       }
     };
-    auto out_proj = [&]() {  // A = this head's attention output (in the q tile)
-      for (int nh = 0; nh < ly.NH; ++nh)
-        for (int kk = 0; kk < KW; ++kk)
-          unit([&](uint32_t w) {
+    auto out_proj = [&]() {  // A = each head's attention output (in its q tile)
+      for (int j = 0; j < GH; ++j)
+        for (int nh = 0; nh < ly.NH; ++nh)
+          for (int kk = 0; kk < KW; ++kk)
+            unit([&](uint32_t w) {
 #pragma unroll
-            for (int k = 0; k < WOC / 16; ++k) {
-              const uint64_t bd = HP == 32 ? desc_kmajor_sw64(w) + (uint64_t)(2 * k)
-                                           : desc_kmajor_sw128(w) + (uint64_t)(2 * k);
-              mma_f16_ss_warp(tmem + (uint32_t)(nh * ly.NB), res_desc_tile<HP>(sQ, kk * (WOC / 16) + k),
-                              bd, id_res, 1u);
-            }
-          });
+              for (int k = 0; k < WOC / 16; ++k) {
+                const uint64_t bd = HP == 32 ? desc_kmajor_sw64(w) + (uint64_t)(2 * k)
+                                             : desc_kmajor_sw128(w) + (uint64_t)(2 * k);
+                mma_f16_ss_warp(tmem + (uint32_t)(nh * ly.NB),
+                                res_desc_tile<HP>(tile_of(0, j), kk * (WOC / 16) + k), bd, id_res, 1u);
+              }
+            });
     };
+    // Head j of the step: S_j in TMEM [A0 + 128 j, +128) (P_j over its first 64
+    // columns), O_j in [A0 + 128 GH + hp j, +hp).
     auto scores = [&]() {
 #pragma unroll
-      for (int ks = 0; ks < HP / 16; ++ks)
-        mma_f16_ss_warp(tmem + (uint32_t)A0, res_desc_tile<HP>(sQ, ks), res_desc_tile<HP>(sK, ks),
-                        id_s, ks > 0 ? 1u : 0u);
+      for (int j = 0; j < GH; ++j)
+#pragma unroll
+        for (int ks = 0; ks < HP / 16; ++ks)
+          mma_f16_ss_warp(tmem + (uint32_t)(A0 + 128 * j), res_desc_tile<HP>(tile_of(0, j), ks),
+                          res_desc_tile<HP>(tile_of(1, j), ks), id_s, ks > 0 ? 1u : 0u);
       issued = true;
     };
     auto pv = [&]() {
-      const uint64_t vd = HP == 32 ? desc_mnmajor_sw64(sV, ly.tile, 512)
-                                   : desc_mnmajor_sw128(sV, RES_ROWS * 128, 1024);
       constexpr uint32_t vstep = HP == 32 ? (1024u >> 4) : (2048u >> 4);  // 16 keys
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_f16_ts_warp(tmem + (uint32_t)(A0 + 128), tmem + (uint32_t)(A0 + kk * 8),
-                        vd + (uint64_t)(kk * vstep), id_pv, kk > 0 ? 1u : 0u);
+      for (int j = 0; j < GH; ++j) {
+        const uint32_t sVj = tile_of(2, j);
+        const uint64_t vd = HP == 32 ? desc_mnmajor_sw64(sVj, ly.tile, 512)
+                                     : desc_mnmajor_sw128(sVj, RES_ROWS * 128, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_f16_ts_warp(tmem + (uint32_t)(A0 + 128 * GH + HP * j),
+                          tmem + (uint32_t)(A0 + 128 * j + kk * 8), vd + (uint64_t)(kk * vstep),
+                          id_pv, kk > 0 ? 1u : 0u);
+      }
       issued = true;
     };
     auto ffn_in = [&]() {
@@ -371,14 +389,14 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     for (int l = 0; l < p.L && ok; ++l) {
       if (ready()) qkv();
       done();
-      for (int h = 0; h < H && ok; ++h) {
+      for (int h0 = 0; h0 < H && ok; h0 += GH) {
         if (ready()) scores();
         done();
         if (ready()) pv();
         done();
         if (ready()) {
           out_proj();
-          if (h + 1 < H) qkv();
+          if (h0 + GH < H) qkv();
         }
         done();
       }
@@ -555,15 +573,18 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       // Layer l - 1's vectors are no longer needed: the producer may reuse the buffer.
       if (l > 0) mbar_arrive(bar_vempty + 8 * ((l - 1) & 1));
       if (!step_sync()) break;  // -> QKV(0) done
-      for (int h = 0; h < H && ok; ++h) {
-        // q | k | v of head h: folded LayerNorm epilogue, fp16 into the operand tiles.
-        for (int i = half; i < 3 * HP / 32; i += 2) {
-          const int part = i / (HP / 32), cc = i % (HP / 32);
+      float pair_lsum = 0.f;  // PAIR: row sum of this thread's head
+      for (int h0 = 0; h0 < H && ok; h0 += GH) {
+        // q | k | v of the step's heads: folded LayerNorm epilogue, fp16 into the
+        // operand tiles.  Accumulator columns: [part][head j][hp] (32-column chunks).
+        for (int i = half; i < 3 * GH * HP / 32; i += 2) {
+          const int part = i / (GH * HP / 32), rem = i % (GH * HP / 32);
+          const int jh = rem / (HP / 32), cc = rem % (HP / 32);
           uint32_t u[32];
           tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + i * 32), u);
-          const int n0 = part * Q + h * HP + cc * 32;
+          const int n0 = part * Q + (h0 + jh) * HP + cc * 32;
           tmem_wait_ld();
-          const uint32_t tile = part == 0 ? sQ : part == 1 ? sK : sV;
+          const uint32_t tile = tile_of(part, jh);
           // 8 columns at a time, the vectors read from shared memory as needed (few
           // live registers: no spills).
 #pragma unroll
@@ -581,59 +602,46 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           }
         }
         if (!step_sync()) break;  // -> S = q k^T done
-        // Softmax of the row, split over both halves: half `half` takes keys
-        // 64 half .. 64 half + 63 (S chunks 2 half, 2 half + 1) and writes their P over
-        // TMEM columns 32 half .. 32 half + 31; the two partial maxima and sums meet in
-        // shared memory.  A 32-key chunk that every row of the warp masks (causal, or
-        // past the sequence end) is neither read nor exponentiated: its P is zero.
-        {
-          const int lim = p.causal ? min(len - 1, r) : len - 1;  // keys k > lim masked
-          const int wlim = p.causal ? min(len - 1, quad * 32 + 31) : len - 1;  // warp max
+        if constexpr (PAIR) {
+          // Head j = half of the pair: this thread owns a whole 128-key row of S_j.
+          // Pass 1: row max; pass 2: exponentials, P (16 packed columns per 32-key
+          // chunk) over the scores -- chunk c's P lands on columns already re-read.
+          // Key chunks every row of the warp masks are skipped (P zero).
+          const uint32_t sb = tr + (uint32_t)(A0 + 128 * half);
+          const int lim = p.causal ? min(len - 1, r) : len - 1;
+          const int wlim = p.causal ? min(len - 1, quad * 32 + 31) : len - 1;
           const float sc = p.scale_log2;
-          uint32_t sv[64];
-          bool act[2];
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int k0 = (2 * half + cc) * 32;
-            act[cc] = k0 <= wlim;  // warp-uniform
-            if (act[cc]) {
-              uint32_t chunk[32];
-              tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + k0), chunk);
-#pragma unroll
-              for (int e = 0; e < 32; ++e) sv[cc * 32 + e] = chunk[e];
-            }
-          }
-          tmem_wait_ld();
           float pm[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            if (!act[cc]) continue;
-            const int k0 = (2 * half + cc) * 32;
+          for (int c = 0; c < 4; ++c) {
+            if (32 * c > wlim) continue;  // warp-uniform
+            uint32_t u[32];
+            tmem_ld_32x32b_x32(sb + (uint32_t)(32 * c), u);
+            tmem_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e)
-              if (k0 + e <= lim) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(sv[cc * 32 + e]));
+              if (32 * c + e <= lim) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(u[e]));
           }
-          const float mh = fmaxf(fmax3f(pm[0], pm[1], pm[2]), fmaxf(fmax3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])));
-          rowmax[half * RES_ROWS + r] = mh;
-          if (!wsync()) break;
-          const float mx = fmaxf(rowmax[r], rowmax[RES_ROWS + r]);
+          const float mx = fmaxf(fmaxf(fmax3f(pm[0], pm[1], pm[2]), fmax3f(pm[3], pm[4], pm[5])),
+                                 fmaxf(pm[6], pm[7]));
           const float base_v = mx == -INFINITY ? 0.f : mx * sc;
           const float2 sc2 = make_float2(sc, sc), nb2 = make_float2(-base_v, -base_v);
           unsigned long long ps2[2] = {0ull, 0ull};
-          uint32_t pk[32];
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) {
-            const int k0 = (2 * half + cc) * 32;
+          for (int c = 0; c < 4; ++c) {
+            uint32_t pk[16];
+            if (32 * c <= wlim) {
+              uint32_t u[32];
+              tmem_ld_32x32b_x32(sb + (uint32_t)(32 * c), u);
+              tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              float p0 = 0.f, p1 = 0.f;
-              if (act[cc]) {
-                const float2 x = ffma2(make_float2(__uint_as_float(sv[cc * 32 + 2 * c]),
-                                                   __uint_as_float(sv[cc * 32 + 2 * c + 1])), sc2, nb2);
-                // One pair in four on the FMA pipe: the exponentials (MUFU) bound this loop.
-                if ((c & 3) == 3) {
+              for (int k = 0; k < 16; ++k) {
+                const float2 x = ffma2(make_float2(__uint_as_float(u[2 * k]), __uint_as_float(u[2 * k + 1])),
+                                       sc2, nb2);
+                float p0, p1;
+                if ((k & 3) == 3) {  // one pair in four on the FMA pipe
                   const float2 e2 = exp2_fma2(x);
                   p0 = e2.x;
                   p1 = e2.y;
@@ -641,40 +649,127 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
                   p0 = ex2_approx(x.x);
                   p1 = ex2_approx(x.y);
                 }
-                if (k0 + 2 * c > lim) p0 = 0.f;
-                if (k0 + 2 * c + 1 > lim) p1 = 0.f;
+                if (32 * c + 2 * k > lim) p0 = 0.f;
+                if (32 * c + 2 * k + 1 > lim) p1 = 0.f;
+                ps2[k & 1] = add2p(ps2[k & 1], pk2(p0, p1));
+                pk[k] = pack_half2(p0, p1);
               }
-              ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
-              pk[cc * 16 + c] = pack_half2(p0, p1);
+            } else {
+#pragma unroll
+              for (int k = 0; k < 16; ++k) pk[k] = 0u;
             }
-          }
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            uint32_t chunk[16];
-#pragma unroll
-            for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
-            tmem_st_32x32b_x16(tr + (uint32_t)(A0 + half * 32 + q * 16), chunk);
+            tmem_st_32x32b_x16(sb + (uint32_t)(16 * c), pk);
           }
           const float2 rs = upk2(add2p(ps2[0], ps2[1]));
-          rowsum[half * RES_ROWS + r] = rs.x + rs.y;
-        }
-        if (!step_sync()) break;  // -> O = P v done
-        if (!wsync()) break;      // both halves' row sums visible
-        {
-          const float lsum = rowsum[r] + rowsum[RES_ROWS + r];
-          const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-          for (int i = half; i < HP / 32; i += 2) {
+          pair_lsum = rs.x + rs.y;
+          if (!step_sync()) break;  // -> O = P v done
+          {
+            const float inv = pair_lsum > 0.f ? 1.f / pair_lsum : 0.f;
             uint32_t u[32];
-            tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + 128 + i * 32), u);
+            tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + 128 * GH + HP * half), u);
             tmem_wait_ld();
             float v[32];
 #pragma unroll
             for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]) * inv;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) res_store_tile<HP>(sQ, r, i * 32 + 8 * j, res_pack8(v + 8 * j));
+            for (int j = 0; j < 4; ++j) res_store_tile<HP>(tile_of(0, half), r, 8 * j, res_pack8(v + 8 * j));
+          }
+        } else {
+          // Softmax of the row, split over both halves: half `half` takes keys
+          // 64 half .. 64 half + 63 (S chunks 2 half, 2 half + 1) and writes their P over
+          // TMEM columns 32 half .. 32 half + 31; the two partial maxima and sums meet in
+          // shared memory.  A 32-key chunk that every row of the warp masks (causal, or
+          // past the sequence end) is neither read nor exponentiated: its P is zero.
+          {
+            const int lim = p.causal ? min(len - 1, r) : len - 1;  // keys k > lim masked
+            const int wlim = p.causal ? min(len - 1, quad * 32 + 31) : len - 1;  // warp max
+            const float sc = p.scale_log2;
+            uint32_t sv[64];
+            bool act[2];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int k0 = (2 * half + cc) * 32;
+              act[cc] = k0 <= wlim;  // warp-uniform
+              if (act[cc]) {
+                uint32_t chunk[32];
+                tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + k0), chunk);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) sv[cc * 32 + e] = chunk[e];
+              }
+            }
+            tmem_wait_ld();
+            float pm[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) pm[i] = -INFINITY;
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              if (!act[cc]) continue;
+              const int k0 = (2 * half + cc) * 32;
+#pragma unroll
+              for (int e = 0; e < 32; ++e)
+                if (k0 + e <= lim) pm[e & 7] = fmaxf(pm[e & 7], __uint_as_float(sv[cc * 32 + e]));
+            }
+            const float mh = fmaxf(fmax3f(pm[0], pm[1], pm[2]), fmaxf(fmax3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+            rowmax[half * RES_ROWS + r] = mh;
+            if (!wsync()) break;
+            const float mx = fmaxf(rowmax[r], rowmax[RES_ROWS + r]);
+            const float base_v = mx == -INFINITY ? 0.f : mx * sc;
+            const float2 sc2 = make_float2(sc, sc), nb2 = make_float2(-base_v, -base_v);
+            unsigned long long ps2[2] = {0ull, 0ull};
+            uint32_t pk[32];
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) {
+              const int k0 = (2 * half + cc) * 32;
+#pragma unroll
+              for (int c = 0; c < 16; ++c) {
+                float p0 = 0.f, p1 = 0.f;
+                if (act[cc]) {
+                  const float2 x = ffma2(make_float2(__uint_as_float(sv[cc * 32 + 2 * c]),
+                                                     __uint_as_float(sv[cc * 32 + 2 * c + 1])), sc2, nb2);
+                  // One pair in four on the FMA pipe: the exponentials (MUFU) bound this loop.
+                  if ((c & 3) == 3) {
+                    const float2 e2 = exp2_fma2(x);
+                    p0 = e2.x;
+                    p1 = e2.y;
+                  } else {
+                    p0 = ex2_approx(x.x);
+                    p1 = ex2_approx(x.y);
+                  }
+                  if (k0 + 2 * c > lim) p0 = 0.f;
+                  if (k0 + 2 * c + 1 > lim) p1 = 0.f;
+                }
+                ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
+                pk[cc * 16 + c] = pack_half2(p0, p1);
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 2; ++q) {
+              uint32_t chunk[16];
+#pragma unroll
+              for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
+              tmem_st_32x32b_x16(tr + (uint32_t)(A0 + half * 32 + q * 16), chunk);
+            }
+            const float2 rs = upk2(add2p(ps2[0], ps2[1]));
+            rowsum[half * RES_ROWS + r] = rs.x + rs.y;
+          }
+          if (!step_sync()) break;  // -> O = P v done
+          if (!wsync()) break;      // both halves' row sums visible
+          {
+            const float lsum = rowsum[r] + rowsum[RES_ROWS + r];
+            const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+            for (int i = half; i < HP / 32; i += 2) {
+              uint32_t u[32];
+              tmem_ld_32x32b_x32(tr + (uint32_t)(A0 + 128 + i * 32), u);
+              tmem_wait_ld();
+              float v[32];
+#pragma unroll
+              for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(u[e]) * inv;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) res_store_tile<HP>(tile_of(0, 0), r, i * 32 + 8 * j, res_pack8(v + 8 * j));
+            }
           }
         }
-        if (!step_sync()) break;  // -> out_proj(h) (+ QKV(h+1)) done
+        if (!step_sync()) break;  // -> out_proj (+ the next step's QKV) done
       }
       if (!ok) break;
       // LN2 statistics (out_proj bias pending), fp16 copy for ffn_in.

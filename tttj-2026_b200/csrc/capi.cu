@@ -403,16 +403,17 @@ bool resident_fits(const tttj_config& c) {
 }
 
 // Whether TTTJ_PATH_AUTO takes the resident kernel for a shape it fits.  One CTA works
-// through 3H + 3 + ceil(F / 128) worker <-> MMA hand-offs per layer (about 2 us each)
-// and streams every layer's weights through its own ring (about 60 GB/s); measured on
-// B200 against the layer-by-layer kernels, the resident kernel is faster up to about
-// 24 hand-offs and 512 KB of weights per layer (the reference's cases 1-7, 9, 10, 12)
-// and slower beyond (case 11: 16 heads; C1: 1.6 MB of weights per layer).
+// through 3H / gh + 3 + ceil(F / 128) worker <-> MMA hand-offs per layer (about 1.5 us
+// each) and streams every layer's weights through its own ring (about 60 GB/s);
+// measured on B200 against the layer-by-layer kernels, the resident kernel is faster up
+// to about 32 hand-offs and 768 KB of weights per layer (the reference's cases 1-7 and
+// 9-12; case 11 with 16 heads: 0.202 vs 0.224 ms) and slower beyond (C1, 1.6 MB of
+// weights per layer: 0.156 vs 0.076 ms).
 bool resident_preferred(const tttj_config& c) {
   const long D = c.d_model, F = c.ffn_dim, Q = (long)qkv_width(c);
   const long steps = 3l * c.num_heads / resident_gh(c) + 3 + (F + 127) / 128;
   const long weight_bytes = 2 * (3 * Q * D + D * Q + 2 * D * F);
-  return steps <= 24 && weight_bytes <= 512 * 1024;
+  return steps <= 32 && weight_bytes <= 768 * 1024;
 }
 
 struct LayerGemms {

@@ -133,6 +133,24 @@ int tttj_plan_set_path(tttj_plan* plan, int path);
 /* 1 if tttj_forward of this plan runs the resident-stack kernel, 0 if layer by layer. */
 int tttj_plan_path(tttj_plan* plan);
 
+/* Per-stage capture for numerics bisection: the same forward as tttj_forward (always
+ * layer by layer), which also writes, for batch index `sequence` at block `layer`, the
+ * stages of the reference's capture_debug dump (kernels/sequence_resident.py:28-46,
+ * kernels/csrc/sequence_resident.cu:355-450, there fixed to sequence 0, layer 0) into
+ * `debug` (device, fp32, tttj_debug_floats(cfg) values), in this order:
+ *   layernorm [S, D]           LN1 output
+ *   qkv.q, qkv.k, qkv.v [S, D] projections (LayerNorm-folded GEMM, fp16 values)
+ *   scores [H, S, S]           q k^T hd^-0.5, -inf at masked keys
+ *   softmax [H, S, S]          probabilities (recomputed in fp32 from q, k)
+ *   pv [S, D]                  attention output before out_proj
+ *   output_projection [S, D]   attention branch added to the residual
+ *   ffn [S, D]                 FFN branch added to the residual
+ * then 2 [S, D] scratch blocks.  Positions are the sequence's token positions; padded
+ * positions are zeros (rows of padded queries too). */
+size_t tttj_debug_floats(const tttj_config* cfg);
+int tttj_forward_debug(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
+                       void* out, int layer, int sequence, float* debug, void* stream);
+
 /* Synchronise the plan's device and read (then clear) the device status word that
  * bounded device waits write on timeout.  *device_status = 0 when healthy. */
 int tttj_plan_status(tttj_plan* plan, int* device_status);

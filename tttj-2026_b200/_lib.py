@@ -73,6 +73,10 @@ _SIGNATURES = {
     "tttj_plan_kernel_times": (_c.c_int, [_vp, _c.POINTER(_c.c_double), _c.POINTER(_c.c_long)]),
     "tttj_kernel_class_name": (_c.c_char_p, [_c.c_int]),
     "tttj_plan_set_path": (_c.c_int, [_vp, _c.c_int]),
+    "tttj_debug_floats": (_c.c_size_t, [_c.c_void_p]),
+    "tttj_forward_debug": (
+        _c.c_int, [_vp, _vp, _c.c_int, _vp, _vp, _c.c_int, _c.c_int, _vp, _vp]
+    ),
     "tttj_plan_path": (_c.c_int, [_vp]),
 }
 

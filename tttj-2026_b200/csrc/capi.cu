@@ -818,8 +818,48 @@ const char* tttj_kernel_class_name(int cls) {
   return (cls >= 0 && cls < TTTJ_KCLASS_COUNT) ? names[cls] : "";
 }
 
-int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask, void* out,
-                 void* stream_ptr) {
+}  // extern "C"
+
+namespace {
+// Stage capture of one sequence at one layer (tttj_forward_debug).  Buffer layout in
+// floats: layernorm [S, D], q, k, v [S, D], scores [H, S, S], softmax [H, S, S],
+// pv [S, D], output_projection [S, D], ffn [S, D], then two [S, D] scratch rows.
+struct DebugCapture {
+  int layer, sequence;
+  float* buf;
+};
+size_t debug_floats(const tttj_config& c) {
+  const size_t S = c.seq_len, D = c.d_model, H = c.num_heads;
+  return 9 * S * D + 2 * H * S * S;
+}
+}  // namespace
+
+static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
+                        void* out, void* stream_ptr, const DebugCapture* dbg);
+
+extern "C" int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
+                            void* out, void* stream_ptr) {
+  return forward_impl(p, x, x_dtype, valid_mask, out, stream_ptr, nullptr);
+}
+
+extern "C" size_t tttj_debug_floats(const tttj_config* cfg) {
+  if (check_config(cfg)) return 0;
+  return debug_floats(*cfg);
+}
+
+extern "C" int tttj_forward_debug(tttj_plan* p, const void* x, int x_dtype,
+                                  const uint8_t* valid_mask, void* out, int layer, int sequence,
+                                  float* debug, void* stream) {
+  if (!p || !debug) return fail(TTTJ_ERR_INVALID, "forward_debug: null argument");
+  if (layer < 0 || layer >= p->cfg.num_layers || sequence < 0 || sequence >= p->cfg.batch_size)
+    return fail(TTTJ_ERR_INVALID, "forward_debug: layer %d / sequence %d out of range", layer,
+                sequence);
+  DebugCapture d{layer, sequence, debug};
+  return forward_impl(p, x, x_dtype, valid_mask, out, stream, &d);
+}
+
+static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
+                        void* out, void* stream_ptr, const DebugCapture* dbg) {
   if (!p || !x || !out) return fail(TTTJ_ERR_INVALID, "forward: null argument");
   if (x_dtype != TTTJ_DTYPE_F16 && x_dtype != TTTJ_DTYPE_F32)
     return fail(TTTJ_ERR_INVALID, "forward: x must be fp16 or fp32");
@@ -854,7 +894,7 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
     TTTJ_CUDA(tock());             \
   } while (0)
 
-  if (use_resident(p)) {
+  if (use_resident(p) && dbg == nullptr) {  // a capture always runs layer by layer
     // The whole stack in one launch: one CTA per sequence reads x and the mask directly.
     ResLaunch r = p->res;
     r.p.x = x;
@@ -870,18 +910,47 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
                               p->stats, p->parts, s));
+  // Capture buffers (floats) of tttj_forward_debug, filled at its layer.
+  const size_t SD = (size_t)S * D, HSS = (size_t)c.num_heads * S * S;
+  float* dg = dbg ? dbg->buf : nullptr;
+  float *d_ln = dg, *d_q = dg + SD, *d_k = dg + 2 * SD, *d_v = dg + 3 * SD, *d_sc = dg + 4 * SD,
+        *d_pr = d_sc + HSS, *d_pv = d_pr + HSS, *d_op = d_pv + SD, *d_ffn = d_op + SD,
+        *d_x0 = d_ffn + SD, *d_x1 = d_x0 + SD;
+  const int hd = head_dim_of(c), Qw = (int)qkv_width(c), bq = dbg ? dbg->sequence : 0;
+  const int* dmap = p->tp.dst_map;
   for (int l = 0; l < c.num_layers; ++l) {
     // Every LayerNorm is folded into the GEMM that consumes it; the statistics come
     // from the gather (layer 0) or the preceding residual epilogue.
     const LayerGemms& L = p->layers[l];
+    const bool cap = dbg && dbg->layer == l;
+    if (cap) {  // block input x and its LN1 output
+      TTTJ_CUDA(debug_gather_launch(p->resid, 0, D, 0, D, 1, 1, dmap, bq, S, d_x0, s));
+      TTTJ_CUDA(debug_ln_launch(d_x0, L.ln1_w, L.ln1_b, kLnEps, S, D, dmap, bq, d_ln, s));
+    }
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_QKV, gemm_launch(L.qkv, s));
+    if (cap) {
+      TTTJ_CUDA(debug_gather_launch(p->qkv, 1, 3 * Qw, 0, D, hd, hp, dmap, bq, S, d_q, s));
+      TTTJ_CUDA(debug_gather_launch(p->qkv, 1, 3 * Qw, Qw, D, hd, hp, dmap, bq, S, d_k, s));
+      TTTJ_CUDA(debug_gather_launch(p->qkv, 1, 3 * Qw, 2 * Qw, D, hd, hp, dmap, bq, S, d_v, s));
+      TTTJ_CUDA(debug_scores_launch(d_q, d_k, dmap, bq, S, c.num_heads, hd, c.causal,
+                                    1.0f / sqrtf((float)hd), d_sc, d_pr, s));
+    }
     AtcParams ap = p->attn;
     ap.work_counter = p->tp.counters + l;
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
                attention_tc_launch(p->attn_tm, ap, hp, c.causal, p->attn_grid, s));
+    if (cap) TTTJ_CUDA(debug_gather_launch(p->ctx, 1, Qw, 0, D, hd, hp, dmap, bq, S, d_pv, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
+    if (cap) {  // attention branch = x after the residual add - x before
+      TTTJ_CUDA(debug_gather_launch(p->resid, 0, D, 0, D, 1, 1, dmap, bq, S, d_x1, s));
+      TTTJ_CUDA(debug_diff_launch(d_x1, d_x0, (long)SD, d_op, s));
+    }
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_IN, gemm_launch(L.ffn_in, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_FFN_OUT, gemm_launch(L.ffn_out, s));
+    if (cap) {  // FFN branch
+      TTTJ_CUDA(debug_gather_launch(p->resid, 0, D, 0, D, 1, 1, dmap, bq, S, d_x0, s));
+      TTTJ_CUDA(debug_diff_launch(d_x0, d_x1, (long)SD, d_ffn, s));
+    }
   }
   TTTJ_TIMED(TTTJ_KCLASS_FINAL_LN,
              ln_final_launch(p->resid, p->tp.dst_map, T, D, p->lnf_w, p->lnf_b, kLnEps, out,
@@ -890,6 +959,8 @@ int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_
   p->ev_used = slot;
   return TTTJ_OK;
 }
+
+extern "C" {
 
 int tttj_plan_status(tttj_plan* p, int* device_status) {
   if (!p || !device_status) return fail(TTTJ_ERR_INVALID, "status: null argument");

@@ -103,6 +103,16 @@ cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, in
 cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
                             const float* gamma, const float* beta, float eps, void* out,
                             int out_dtype, cudaStream_t stream);
+// Per-stage capture kernels (debug.cu).
+cudaError_t debug_gather_launch(const void* src, int src_f16, int ld, int col_base, int cols, int hd,
+                                int hp, const int* dst_map, int b, int S, float* dst, cudaStream_t s);
+cudaError_t debug_ln_launch(const float* x, const float* gamma, const float* beta, float eps, int S,
+                            int D, const int* dst_map, int b, float* out, cudaStream_t s);
+cudaError_t debug_scores_launch(const float* q, const float* k, const int* dst_map, int b, int S,
+                                int H, int hd, int causal, float scale, float* scores, float* probs,
+                                cudaStream_t s);
+cudaError_t debug_diff_launch(const float* a, const float* b, long n, float* out, cudaStream_t s);
+
 cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream);
 
 }  // namespace tttj

@@ -213,6 +213,52 @@ class B200Transformer(nn.Module):
         )
         return out
 
+    # Stage names and shapes of the capture, as the reference's unpack_debug
+    # (kernels/sequence_resident.py:28-46, 112-122) returns them.
+    _DEBUG_STAGES = ("layernorm", "qkv.q", "qkv.k", "qkv.v", "scores", "softmax", "pv",
+                     "output_projection", "ffn")
+
+    def run(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
+            capture_debug: bool = False, debug_layer: int = 0, debug_sequence: int = 0):
+        """(output, stages or None), like the reference adapter's run(x, mask,
+        capture_debug) (kernels/sequence_resident.py:158-225).  With capture_debug the
+        forward runs layer by layer and also returns, for batch index ``debug_sequence``
+        at block ``debug_layer`` (the reference: sequence 0, layer 0), a dict of fp32
+        tensors: layernorm / qkv.q / qkv.k / qkv.v / pv / output_projection / ffn
+        [S, D] and scores / softmax [H, S, S]; padded positions are zeros."""
+        if not capture_debug:
+            return self.forward(x, valid_token_mask), None
+        B, S, D = x.shape
+        H = self.config.num_heads
+        plan = self.plan_for(B, S)
+        n = int(_lib.lib().tttj_debug_floats(ctypes.byref(plan.c)))
+        debug = torch.zeros(n, dtype=torch.float32, device=self.device)
+        x = x.contiguous()
+        mask = None
+        if valid_token_mask is not None:
+            mask = (valid_token_mask != 0).contiguous().view(torch.uint8)
+        out = torch.empty_like(x)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(
+            _lib.lib().tttj_forward_debug(plan.handle, ctypes.c_void_p(x.data_ptr()),
+                                          _SUPPORTED_INPUT[x.dtype],
+                                          None if mask is None else ctypes.c_void_p(mask.data_ptr()),
+                                          ctypes.c_void_p(out.data_ptr()), int(debug_layer),
+                                          int(debug_sequence), ctypes.c_void_p(debug.data_ptr()),
+                                          ctypes.c_void_p(stream)),
+            "forward_debug",
+        )
+        sizes = {"scores": (H, S, S), "softmax": (H, S, S)}
+        stages, off = {}, 0
+        for name in self._DEBUG_STAGES:
+            shape = sizes.get(name, (S, D))
+            count = 1
+            for v in shape:
+                count *= v
+            stages[name] = debug[off:off + count].view(shape)
+            off += count
+        return out, stages
+
     def launches_per_forward(self, batch: int, seq_len: int) -> int:
         """Kernel launches one forward of shape [batch, seq_len] enqueues."""
         return int(_lib.lib().tttj_plan_launch_count(self.plan_for(batch, seq_len).handle))

@@ -27,7 +27,8 @@
 //   smem ring          weight boxes streamed by TMA from L2 (all CTAs read the same
 //                      weights), as many 16 KB stages as shared memory holds.
 //
-// Roles: warp 0 TMA producer (weight boxes in the fixed order of the schedule below),
+// Roles: warp 0 TMA producer (lane 0: weight boxes in the fixed order of the schedule
+// below; lane 1: each layer's vectors, as soon as their buffer is free),
 // warp 1 TMEM owner and MMA issuer (whole warp, elected lane issues), warps 2-9
 // workers: LayerNorm passes, epilogues, softmax (two warps per TMEM lane quadrant, each
 // one half of the 32-column chunks).  Workers and the MMA warp alternate strictly: the
@@ -203,27 +204,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           ph ^= 1u;
         }
       };
-      int vloads = 0;  // layer-vector copies issued
-      auto layer_ptr = [&](const float* v, size_t stride, int l) {
-        return reinterpret_cast<const uint8_t*>(v) + (size_t)l * stride;
-      };
       for (int l = 0; l < p.L && ok; ++l) {
-        // This layer's vectors into buffer l & 1 once the workers released layer l - 2's.
-        const int vb = l & 1;
-        if (l >= 2 && !mbar_wait(bar_vempty + 8 * vb, (uint32_t)(((l >> 1) - 1) & 1), abort_flag, limit)) {
-          ok = false;
-          break;
-        }
-        const uint32_t dv = sVec + (uint32_t)(vb * ly.vec_bytes);
-        const uint32_t vbar = bar_vfull + 8 * vb;
-        mbar_arrive_expect_tx(vbar, (uint32_t)ly.vec_bytes);
-        bulk_load(dv + 4 * ly.v_bq, layer_ptr(p.bqkv, p.fold_stride, l), 12 * Q, vbar);
-        bulk_load(dv + 4 * ly.v_cq, layer_ptr(p.cqkv, p.fold_stride, l), 12 * Q, vbar);
-        bulk_load(dv + 4 * ly.v_bo, layer_ptr(p.bo, p.layer_stride, l), 4 * D, vbar);
-        bulk_load(dv + 4 * ly.v_b1, layer_ptr(p.b1, p.fold_stride, l), 4 * F, vbar);
-        bulk_load(dv + 4 * ly.v_c1, layer_ptr(p.c1, p.fold_stride, l), 4 * F, vbar);
-        bulk_load(dv + 4 * ly.v_b2, layer_ptr(p.b2, p.layer_stride, l), 4 * D, vbar);
-        ++vloads;
         for (int h0 = 0; h0 < H && ok; h0 += GH) {
           for (int kc = 0; kc < ly.KC; ++kc) {
             if (ly.qkv_merged) {  // boxes of GH * hp rows: q, k, v of the step's heads
@@ -256,6 +237,36 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
           }
           mbar_wait(bar_full + 8 * st, ph, nullptr, limit);
         }
+      }
+    } else if (lane == 1) {
+      // Layer vectors, independent of the weight ring: layer l's block goes into buffer
+      // l & 1 as soon as the workers have released layer l - 2's.
+      bool ok = true;
+      int vloads = 0;  // layer-vector copies issued
+      auto layer_ptr = [&](const float* v, size_t stride, int l) {
+        return reinterpret_cast<const uint8_t*>(v) + (size_t)l * stride;
+      };
+      for (int l = 0; l < p.L; ++l) {
+        const int vb = l & 1;
+        if (l >= 2 && !mbar_wait(bar_vempty + 8 * vb, (uint32_t)(((l >> 1) - 1) & 1), abort_flag, limit)) {
+          ok = false;
+          break;
+        }
+        const uint32_t dv = sVec + (uint32_t)(vb * ly.vec_bytes);
+        const uint32_t vbar = bar_vfull + 8 * vb;
+        mbar_arrive_expect_tx(vbar, (uint32_t)ly.vec_bytes);
+        bulk_load(dv + 4 * ly.v_bq, layer_ptr(p.bqkv, p.fold_stride, l), 12 * Q, vbar);
+        bulk_load(dv + 4 * ly.v_cq, layer_ptr(p.cqkv, p.fold_stride, l), 12 * Q, vbar);
+        bulk_load(dv + 4 * ly.v_bo, layer_ptr(p.bo, p.layer_stride, l), 4 * D, vbar);
+        bulk_load(dv + 4 * ly.v_b1, layer_ptr(p.b1, p.fold_stride, l), 4 * F, vbar);
+        bulk_load(dv + 4 * ly.v_c1, layer_ptr(p.c1, p.fold_stride, l), 4 * F, vbar);
+        bulk_load(dv + 4 * ly.v_b2, layer_ptr(p.b2, p.layer_stride, l), 4 * D, vbar);
+        ++vloads;
+      }
+      if (!ok) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
+        // Let the copies in flight land before the CTA exits.
         for (int j = vloads > 2 ? vloads - 2 : 0; j < vloads; ++j)
           mbar_wait(bar_vfull + 8 * (j & 1), (uint32_t)((j >> 1) & 1), nullptr, limit);
       }

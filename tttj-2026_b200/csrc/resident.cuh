@@ -1,9 +1,9 @@
 // K3: the whole transformer stack for short sequences in one launch.
 //
 // For sequences of at most 128 tokens (the reference's resident cases,
-// kernels/sequence_resident.py:125-233 and kernels/fused_megakernel.py:1163-1858, and
-// BASELINE config C1) the layer-by-layer path spends most of its time starting and
-// draining 5 kernels per layer.  Here one CTA owns one sequence for the whole forward:
+// kernels/sequence_resident.py:125-233 and kernels/fused_megakernel.py:1163-1858) the
+// layer-by-layer path spends most of its time starting and draining 5 kernels per
+// layer.  Here one CTA owns one sequence for the whole forward:
 // BaselineTransformerBlock x L, final LayerNorm and masking
 // (benchmarks/torch_transformer_benchmark.py:134-172), with no intermediate tensor in
 // global memory and no launch in between.
@@ -12,29 +12,32 @@
 //   TMEM [0, D)        fp32 residual stream x, row r = TMEM lane r.  out_proj and
 //                      ffn_out accumulate straight into it (tcgen05.mma with the
 //                      accumulate flag); their biases are added by the next LayerNorm pass.
-//   TMEM [D, 512)      accumulators of the current step: q|k|v of one head, then S (P
-//                      written over its first 64 columns) and O, then one FFN chunk.
+//   TMEM [D, 512)      accumulators of the current step: q|k|v of the step's heads, then
+//                      their S (P written over its first 64 columns) and O, then one FFN
+//                      chunk.
 //   smem xa            fp16 copy of x, the A operand of the LayerNorm-folded QKV and
 //                      ffn_in GEMMs (the same folded weights and epilogue as the
 //                      layer-by-layer path: out = rstd (acc - mean colsum) + b').
-//   smem q/k/v tiles   one head at a time; the head's attention output reuses the q tile
-//                      and is multiplied into the residual right away (out_proj per head,
-//                      K = hp), so no [S, D] context buffer is needed.
+//   smem q/k/v tiles   one head (or one pair of 32-wide heads) at a time; each head's
+//                      attention output reuses its q tile and is multiplied into the
+//                      residual right away (out_proj per head, K = hp), so no [S, D]
+//                      context buffer is needed.
 //   smem h             one FFN chunk of GELU(ffn_in) (<= 128 columns), multiplied into
 //                      the residual by ffn_out before the next chunk.
 //   smem vectors       each layer's biases and column sums, copied in by the producer
 //                      (two layers' worth: layer l in buffer l & 1).
 //   smem ring          weight boxes streamed by TMA from L2 (all CTAs read the same
-//                      weights), as many 16 KB stages as shared memory holds.
+//                      weights), as many 16-24 KB stages as shared memory holds.
 //
 // Roles: warp 0 TMA producer (lane 0: weight boxes in the fixed order of the schedule
 // below; lane 1: each layer's vectors, as soon as their buffer is free),
 // warp 1 TMEM owner and MMA issuer (whole warp, elected lane issues), warps 2-9
 // workers: LayerNorm passes, epilogues, softmax (two warps per TMEM lane quadrant, each
-// one half of the 32-column chunks).  Workers and the MMA warp alternate strictly: the
-// workers finish a step's inputs and arrive on `ready`, the MMA warp issues the step and
-// commits to `done`, the workers wait for `done`.  Steps per layer:
-//   QKV(h=0) | S(h) | PV(h) | out_proj(h) + QKV(h+1) ... | ffn_in(0) | ffn_out(c) + ffn_in(c+1) ...
+// one half of the 32-column chunks, or one head of a pair).  Workers and the MMA warp
+// alternate strictly: the workers finish a step's inputs and arrive on `ready`, the MMA
+// warp issues the step and commits to `done`, the workers wait for `done`.  Steps per
+// layer (g = a head, or a pair of heads):
+//   QKV(g=0) | S(g) | PV(g) | out_proj(g) + QKV(g+1) ... | ffn_in(0) | ffn_out(c) + ffn_in(c+1) ...
 // Every wait is bounded; on a timeout the role records TTTJ_DEV_TIMEOUT_RESIDENT, raises
 // the CTA abort flag and unwinds.
 //

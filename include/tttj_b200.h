@@ -157,7 +157,10 @@ int tttj_plan_status(tttj_plan* plan, int* device_status);
 
 /* ---- instrumentation ---- */
 
-/* Number of kernel launches one tttj_forward of this plan enqueues. */
+/* Number of kernel launches the next tttj_forward of this plan enqueues if it is given
+ * the same kind of mask as the last one: on the layer-by-layer path a forward without a
+ * mask reuses the all-valid token plan the previous mask-free forward built, one launch
+ * fewer. */
 int tttj_plan_launch_count(tttj_plan* plan);
 
 /* Kernel classes of the forward, for per-class timing. */

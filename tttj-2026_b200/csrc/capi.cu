@@ -442,6 +442,10 @@ struct tttj_plan {
   AtcParams attn;
   int attn_grid;
   // Resident-stack path (sequences of <= 128 tokens), built when the shape fits.
+  // The token plan in the workspace is the all-valid one (the last forward had no mask
+  // and completed): a forward without a mask skips the plan kernel.  The attention
+  // kernel resets its work counter at the end of each launch.
+  bool plan_static = false;
   bool res_ok = false;       // the resident kernel fits this shape (launch built)
   bool res_auto = false;     // ... and TTTJ_PATH_AUTO prefers it
   int path = TTTJ_PATH_AUTO;
@@ -474,7 +478,7 @@ bool use_resident(const tttj_plan* p) {
   return p->path == TTTJ_PATH_RESIDENT || (p->path == TTTJ_PATH_AUTO && p->res_auto);
 }
 int launches_per_forward(const tttj_plan* p) {
-  return use_resident(p) ? 1 : layerwise_launches(p->cfg);
+  return use_resident(p) ? 1 : layerwise_launches(p->cfg) - (p->plan_static ? 1 : 0);
 }
 
 // Fold the events of the previous timed forward into the per-class totals.
@@ -905,8 +909,13 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
     p->ev_used = slot;
     return TTTJ_OK;
   }
-  TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
-                                                  atc_item_rows(hp), ATC_BN, p->tp, s));
+  // Without a mask the plan is the all-valid one every time: built by the first such
+  // forward, reused by the next ones (the reference caches the all-valid case too,
+  // kernels/sequence_resident.py:173-192).
+  if (!(valid_mask == nullptr && p->plan_static))
+    TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
+                                                    atc_item_rows(hp), ATC_BN, p->tp, s));
+  p->plan_static = valid_mask == nullptr;
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
                               p->stats, p->parts, s));
@@ -969,6 +978,7 @@ int tttj_plan_status(tttj_plan* p, int* device_status) {
   int v = 0;
   TTTJ_CUDA(cudaMemcpy(&v, p->status, sizeof(int), cudaMemcpyDeviceToHost));
   if (v != 0) TTTJ_CUDA(cudaMemset(p->status, 0, sizeof(int)));
+  if (v != 0) p->plan_static = false;  // a kernel gave up: rebuild the plan (counters too)
   *device_status = v;
   if (v != 0) return fail(TTTJ_ERR_DEVICE_TIMEOUT, "device wait timed out (status 0x%x)", v);
   return TTTJ_OK;

@@ -260,7 +260,8 @@ class B200Transformer(nn.Module):
         return out, stages
 
     def launches_per_forward(self, batch: int, seq_len: int) -> int:
-        """Kernel launches one forward of shape [batch, seq_len] enqueues."""
+        """Kernel launches one forward of shape [batch, seq_len] enqueues, given the same
+        kind of mask (None or a tensor) as the last one of that shape."""
         return int(_lib.lib().tttj_plan_launch_count(self.plan_for(batch, seq_len).handle))
 
     def set_kernel_timing(self, batch: int, seq_len: int, enable: bool) -> None:

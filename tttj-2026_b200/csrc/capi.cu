@@ -435,7 +435,8 @@ struct tttj_plan {
   float* resid;  // fp32 residual stream
   __half *x16, *qkv, *ctx, *hid;  // x16: fp16 copy of the residual stream (GEMM A operand)
   float2* stats;  // [2][T][parts] LayerNorm statistics partials: LN1 (next QKV), LN2 (ffn_in)
-  int parts;
+  int parts;      // statistics partials per row of LN1 (ffn_out, the gather -> QKV)
+  int parts_ln2;  // ... of LN2 (out_proj -> ffn_in)
   std::vector<LayerGemms> layers;
   const float *lnf_w, *lnf_b;
   CUtensorMap attn_tm;
@@ -637,10 +638,12 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   const int B = cfg->batch_size, S = cfg->seq_len, D = cfg->d_model, F = cfg->ffn_dim;
   const int T = B * S;
   const int* rows_dev = p->tp.seq_off + B;  // number of valid tokens
-  // Statistics partials actually produced: two column halves per column tile of the
-  // residual GEMMs (N = d_model), whose tile width is fixed by (T, d_model).
-  const int res_bn = gemm_choose_bn(T, D, p->num_sms);
-  p->parts = 2 * ((D + res_bn - 1) / res_bn);
+  // Statistics partials: two column halves per column tile of the residual GEMM that
+  // writes them (out_proj -> LN2, ffn_out -> LN1), set once those GEMMs are built.
+  // The gather writes layer 0's LN1 statistics as partial 0 (the rest zero), which
+  // any count reads correctly.
+  p->parts = 0;
+  p->parts_ln2 = 0;
   const int hd = head_dim_of(*cfg), hp = layout_hd(*cfg), Q = (int)qkv_width(*cfg);
   auto W = [&](int layer, int field) -> const uint8_t* {
     size_t off = 0, bytes = 0;
@@ -681,7 +684,26 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     // Two statistics buffers, reused by every layer: ffn_out(l-1) / the gather write
     // LN1 for qkv(l); out_proj(l) writes LN2 for ffn_in(l).
     float2* st_ln1 = p->stats;
-    float2* st_ln2 = p->stats + (size_t)T * p->parts;
+    float2* st_ln2 = p->stats + (size_t)T * stats_parts(*cfg);
+    if (l == 0) {
+      // Tile widths of the residual GEMMs, which fix the partial counts.  Every layer
+      // has the same shapes, so layer 0's choice holds for all.
+      GemmLaunch probe_out, probe_ffn;
+      rc = build_gemm(&probe_out, p->ctx, Q, W(l, TTTJ_W_OUT), Q,
+                      reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
+                      T, rows_dev, D, Q, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
+      if (!rc)
+        rc = build_gemm(&probe_ffn, p->hid, F, W(l, TTTJ_W_FFN_OUT), F,
+                        reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D,
+                        p->resid, D, T, rows_dev, D, F, EPI_RESIDUAL_F32_STATS, p->status,
+                        p->num_sms);
+      if (rc) {
+        delete p;
+        return rc;
+      }
+      p->parts_ln2 = 2 * ((D + probe_out.bn - 1) / probe_out.bn);
+      p->parts = 2 * ((D + probe_ffn.bn - 1) / probe_ffn.bn);
+    }
     rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * Q, nullptr, 0, T, rows_dev,
                     3 * Q, D, EPI_LN_FOLD, p->status, p->num_sms);
     L.qkv.p.stats_in = st_ln1;
@@ -695,12 +717,12 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     L.out.p.out16 = p->x16;
     L.out.p.ld16 = D;
     L.out.p.stats_out = st_ln2;
-    L.out.p.stats_parts = p->parts;
+    L.out.p.stats_parts = p->parts_ln2;
     if (!rc)
       rc = build_gemm(&L.ffn_in, p->x16, D, w1_f, D, b1_f, p->hid, F, nullptr, 0, T, rows_dev, F,
                       D, EPI_LN_FOLD_GELU, p->status, p->num_sms);
     L.ffn_in.p.stats_in = st_ln2;
-    L.ffn_in.p.stats_parts = p->parts;
+    L.ffn_in.p.stats_parts = p->parts_ln2;
     L.ffn_in.p.colsum = c1;
     L.ffn_in.p.ln_eps = kLnEps;
     const bool last = l + 1 == cfg->num_layers;
@@ -709,7 +731,8 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
                       reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D, p->resid,
                       D, T, rows_dev, D, F, last ? EPI_BIAS_RESIDUAL_F32 : EPI_RESIDUAL_F32_STATS,
                       p->status, p->num_sms);
-    if (!rc && (L.out.bn != res_bn || L.ffn_out.bn != res_bn))
+    if (!rc && (2 * ((D + L.out.bn - 1) / L.out.bn) != p->parts_ln2 ||
+                2 * ((D + L.ffn_out.bn - 1) / L.ffn_out.bn) != p->parts))
       rc = fail(TTTJ_ERR_INVALID, "internal: residual GEMM tile width mismatch");
     if (!last) {
       L.ffn_out.p.out16 = p->x16;

@@ -65,7 +65,44 @@ int gemm_choose_bn(int rows, int n, int num_sms) {
   return 64;
 }
 
+// Long-K residual GEMMs (ffn_out: fp32 residual epilogue, K >= 2048): the tile shape
+// with the shortest estimated main loop plus epilogue tail.  Per k-block of 64, a CTA's
+// shared memory takes the TMA writes of its A and B boxes and the MMA's reads of the
+// same bytes at ~128 B/clock, and the tensor core needs 2 * (columns it computes)
+// clocks: a 128 x 128 single-CTA tile is held to half the tensor rate by shared memory,
+// a 128 x 256 one to two thirds, a CTA pair's 256 x 256 tile runs at the full rate (each
+// CTA holds half of B).  The epilogue of the last tile (fp32 residual in and out, fp16
+// copy, statistics) is not hidden behind any MMA: ~50 clocks per output column of the
+// CTA's 128 rows.  (Measured on B200 with per-k-block clock stamps, C2 ffn_out:
+// 128 x 128 tiles 21 us, 128 x 256 18 us, pair 256 x 256 17.8 us.)
+static void choose_long_k_residual(int rows, int n, int k, int num_sms, int* bn, int* pair) {
+  double best = 0.0;
+  for (int cand_pair = 0; cand_pair <= 1; ++cand_pair) {
+    for (int cand_bn : {128, 256}) {
+      if (n % cand_bn) continue;
+      const long rows_per_tile = cand_pair ? 2 * GEMM_BM : GEMM_BM;
+      const long tiles = (rows + rows_per_tile - 1) / rows_per_tile * (n / cand_bn);
+      const long units = cand_pair ? num_sms / 2 : num_sms;
+      const long waves = (tiles + units - 1) / units;
+      const double b_bytes = (cand_pair ? cand_bn / 2 : cand_bn) * GEMM_BK * 2.0;
+      const double smem_clk = 2.0 * (GEMM_BM * GEMM_BK * 2.0 + b_bytes) / 128.0;
+      const double kblock_clk = smem_clk > 2.0 * cand_bn ? smem_clk : 2.0 * cand_bn;
+      const double est = (double)waves * ((k + GEMM_BK - 1) / GEMM_BK) * kblock_clk + 50.0 * cand_bn;
+      if (best == 0.0 || est < best) {
+        best = est;
+        *bn = cand_bn;
+        *pair = cand_pair;
+      }
+    }
+  }
+}
+
 void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair) {
+  const bool residual = epi == EPI_BIAS_RESIDUAL_F32 || epi == EPI_RESIDUAL_F32_STATS;
+  if (residual && k >= 2048 && n % 128 == 0 && num_sms >= 2) {
+    choose_long_k_residual(rows, n, k, num_sms, bn, pair);
+    return;
+  }
   *bn = gemm_choose_bn(rows, n, num_sms);
   // CTA pairs (256-row tiles) cut each SM's operand traffic by a third and deepen the
   // ring, which pays where the main loop dominates: long K, and enough tiles that the

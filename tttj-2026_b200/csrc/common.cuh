@@ -185,11 +185,6 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                ::"r"(dst), "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
                : "memory");
 }
-// Hint: bring the 128-byte line holding `gptr` into this SM's L1.
-__device__ __forceinline__ void prefetch_l1(const void* gptr) {
-  asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<uint64_t>(gptr)));
-}
-
 // Hint: bring `bytes` (a multiple of 16, 16-byte aligned address) of global memory into
 // L2.  No completion tracking; a later ordinary load of the range finds it in L2.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* gptr, uint32_t bytes) {

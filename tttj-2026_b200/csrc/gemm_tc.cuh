@@ -344,13 +344,6 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       const int seg0 = n_blk * BN + col_half * (BN / 2);
       if (seg0 < p.n && (staged_res || row_ok)) load_res(staged_res, row0, row, seg0);
-      // The per-column operands of this warp's chunks (32 bias and, for the folds, 32
-      // column-sum floats each: one 128-byte line) are brought into L1 while the
-      // accumulator is computed, off the chunks' critical path.
-      if (lane < CHUNKS && seg0 + lane * 32 < p.n) {
-        prefetch_l1(p.bias + seg0 + lane * 32);
-        if (FOLD) prefetch_l1(p.colsum + seg0 + lane * 32);
-      }
       if (!mbar_wait(bar_accf + 8 * acc, acc_phase, abort_flag, limit)) {
         *abort_flag = 1;
         report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);

@@ -1,7 +1,7 @@
 """GPU: forwards without a mask reuse the all-valid token plan of the previous mask-free
-forward (the attention kernel resets its work counter at the end of each launch), and a
-masked forward in between rebuilds it (kernels/sequence_resident.py:173-192 caches the
-all-valid case the same way)."""
+forward (the gather kernel that opens each forward zeroes the attention work counters),
+and a masked forward in between rebuilds it (kernels/sequence_resident.py:173-192 caches
+the all-valid case the same way)."""
 import pytest
 import torch
 

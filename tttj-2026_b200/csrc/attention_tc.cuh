@@ -208,10 +208,6 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         // first CTA that asks for it.
         const int it = atomicAdd(p.work_counter, 1);
         const bool stop = it >= n_items;
-        // Every CTA ends with exactly one fetch past the list, so the fetch that returns
-        // n_items + gridDim.x - 1 is the launch's last: no CTA reads the counter again,
-        // and it is reset for the next launch (a forward may then skip the plan kernel).
-        if (it == n_items + (int)gridDim.x - 1) atomicExch(p.work_counter, 0);
         AtcItem w;
         if (!stop) {
           w = atc_decode<CAUSAL, NT>(p, it);

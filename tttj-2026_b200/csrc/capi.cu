@@ -443,9 +443,9 @@ struct tttj_plan {
   AtcParams attn;
   int attn_grid;
   // Resident-stack path (sequences of <= 128 tokens), built when the shape fits.
-  // The token plan in the workspace is the all-valid one (the last forward had no mask
-  // and completed): a forward without a mask skips the plan kernel.  The attention
-  // kernel resets its work counter at the end of each launch.
+  // The token plan in the workspace is the all-valid one (the last forward had no mask):
+  // a forward without a mask skips the plan kernel.  The gather kernel, first of every
+  // layer-by-layer forward, zeroes the attention work counters.
   bool plan_static = false;
   bool res_ok = false;       // the resident kernel fits this shape (launch built)
   bool res_auto = false;     // ... and TTTJ_PATH_AUTO prefers it
@@ -941,7 +941,7 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   p->plan_static = valid_mask == nullptr;
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
-                              p->stats, p->parts, s));
+                              p->stats, p->parts, p->tp.counters, s));
   // Capture buffers (floats) of tttj_forward_debug, filled at its layer.
   const size_t SD = (size_t)S * D, HSS = (size_t)c.num_heads * S * S;
   float* dg = dbg ? dbg->buf : nullptr;
@@ -1001,7 +1001,7 @@ int tttj_plan_status(tttj_plan* p, int* device_status) {
   int v = 0;
   TTTJ_CUDA(cudaMemcpy(&v, p->status, sizeof(int), cudaMemcpyDeviceToHost));
   if (v != 0) TTTJ_CUDA(cudaMemset(p->status, 0, sizeof(int)));
-  if (v != 0) p->plan_static = false;  // a kernel gave up: rebuild the plan (counters too)
+  if (v != 0) p->plan_static = false;  // a kernel gave up: rebuild the plan on the next forward
   *device_status = v;
   if (v != 0) return fail(TTTJ_ERR_DEVICE_TIMEOUT, "device wait timed out (status 0x%x)", v);
   return TTTJ_OK;

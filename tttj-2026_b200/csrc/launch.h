@@ -86,7 +86,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
                                int kv_block, const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
-                             int n_parts, cudaStream_t stream);
+                             int n_parts, int* counters, cudaStream_t stream);
 // rows_out output rows; with hd < hp the input's rows are heads of hd rows placed at
 // the start of output groups of hp rows, the rest zero (hd == hp: one row each).
 cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,

@@ -97,7 +97,7 @@ struct TokenPlan {
   int* dst_map;     // [B*S] b*S + s -> packed row, or -1
   int2* items;      // [B*H*ceil(S/128)] attention work list (bound for every item size)
   int* item_count;  // [1]
-  int* counters;    // [PLAN_COUNTERS] dynamic work counters, zeroed by the plan kernel
+  int* counters;    // [PLAN_COUNTERS] dynamic work counters, zeroed by the plan and gather kernels
 };
 
 // K3 resident stack: one CTA runs every layer of one sequence of <= 128 tokens.

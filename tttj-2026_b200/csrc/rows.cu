@@ -36,7 +36,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
 
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
-                             int n_parts, cudaStream_t stream) {
+                             int n_parts, int* counters, cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
@@ -44,12 +44,12 @@ cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, 
     TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, __half>, dim3(grid),
                                                  dim3(32 * ROWS_PER_CTA), 0, stream,
                                                  static_cast<const __half*>(x), packed_src,
-                                                 rows_dev, D, resid, x16, stats, n_parts)));
+                                                 rows_dev, D, resid, x16, stats, n_parts, counters)));
   } else {
     TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, float>, dim3(grid),
                                                  dim3(32 * ROWS_PER_CTA), 0, stream,
                                                  static_cast<const float*>(x), packed_src,
-                                                 rows_dev, D, resid, x16, stats, n_parts)));
+                                                 rows_dev, D, resid, x16, stats, n_parts, counters)));
   }
   return e;
 }

@@ -202,15 +202,20 @@ __device__ __forceinline__ void ln_normalise(float (&x)[VPL][8], int D, const fl
 // Layer-0 entry: gather the caller's rows into the packed fp32 residual stream, write
 // its fp16 copy (A operand of the LayerNorm-folded QKV GEMM) and the row's
 // (sum, sum of squares) as partial 0 of the row's n_parts statistics partials
-// (the others zero).
+// (the others zero).  Block 0 also zeroes the forward's attention work counters, so a
+// forward that reuses the token plan (no plan kernel) starts from zero as well, even
+// after an earlier launch gave up part-way.  This runs after griddep_wait, i.e. after
+// every kernel of the previous forward has completed.
 template <int VPL, typename TIn>
 __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ x,
                                                         const int* __restrict__ packed_src,
                                                         const int* __restrict__ rows_dev, int D,
                                                         float* resid, __half* x16, float2* stats,
-                                                        int n_parts) {
+                                                        int n_parts, int* counters) {
   griddep_wait();
   griddep_launch();
+  if (blockIdx.x == 0 && counters != nullptr)
+    for (int i = threadIdx.x; i < PLAN_COUNTERS; i += blockDim.x) counters[i] = 0;
   const int row = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (row >= *rows_dev) return;
   const int src = packed_src[row];

@@ -57,6 +57,28 @@ def test_baseline_config_vs_oracle(name):
     assert r.passed, r
 
 
+@pytest.mark.parametrize("batch", [4, 1])
+def test_c2_per_rank_shapes_vs_oracle(batch):
+    """C2's per-GPU share at 2 and 8 GPUs (bench.py --gpus N shards the batch): fewer
+    rows change every tile choice (ffn_out on CTA-pair 256 x 128 tiles, out_proj on
+    64-wide tiles, so the two LayerNorms read different statistics partial counts)."""
+    B, S, D, H, F, L, causal, dtype, lengths = CONFIGS["C2"]
+    cfg = tb.TransformerConfig(batch, S, D, H, F, L, causal)
+    model = tb.make_parameter_model(cfg, 0, dtype, DEV)
+    x, mask = tb.generate_inputs(cfg, 1, dtype, lengths, DEV)
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        out = opt(x, mask)
+        again = opt(x, mask)
+        ref = forward_fp32(state_dict_fp32(model, DEV), cfg, x.float(), mask)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    r = gate(ref, out, mask)
+    print("C2 batch", batch, r)
+    assert r.passed, r
+    assert opt.device_status() == 0
+
+
 def test_c4_long_sequence_vs_oracle():
     cfg, model, x, mask = _case("C4")
     opt = tb.make_optimized_transformer(model)

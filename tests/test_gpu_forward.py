@@ -60,8 +60,9 @@ def test_baseline_config_vs_oracle(name):
 @pytest.mark.parametrize("batch", [4, 1])
 def test_c2_per_rank_shapes_vs_oracle(batch):
     """C2's per-GPU share at 2 and 8 GPUs (bench.py --gpus N shards the batch): fewer
-    rows change every tile choice (ffn_out on CTA-pair 256 x 128 tiles, out_proj on
-    64-wide tiles, so the two LayerNorms read different statistics partial counts)."""
+    rows change the tile choices (at 2 GPUs ffn_out runs CTA-pair 256 x 128 tiles and
+    out_proj 64-wide ones, so the two LayerNorms read different statistics partial
+    counts; at 8 GPUs both run 64-wide tiles)."""
     B, S, D, H, F, L, causal, dtype, lengths = CONFIGS["C2"]
     cfg = tb.TransformerConfig(batch, S, D, H, F, L, causal)
     model = tb.make_parameter_model(cfg, 0, dtype, DEV)

@@ -74,8 +74,12 @@ int gemm_choose_bn(int rows, int n, int num_sms) {
 // CTA holds half of B).  The epilogue of the last tile (fp32 residual in and out, fp16
 // copy, statistics) is not hidden behind any MMA: ~50 clocks per output column of the
 // CTA's 128 rows.  (Measured on B200 with per-k-block clock stamps, C2 ffn_out:
-// 128 x 128 tiles 21 us, 128 x 256 18 us, pair 256 x 256 17.8 us.)
-static void choose_long_k_residual(int rows, int n, int k, int num_sms, int* bn, int* pair) {
+// 128 x 128 tiles 21 us, 128 x 256 18 us, pair 256 x 256 17.8 us.)  Only shapes whose
+// tiles occupy at least three quarters of the SMs compete: with fewer, the busy SMs'
+// own feed, not shared memory, sets the pace (measured: C2 at 1024-2048 rows runs
+// faster on 64-wide single-CTA tiles than on half-empty pairs).  Returns false when no
+// shape qualifies.
+static bool choose_long_k_residual(int rows, int n, int k, int num_sms, int* bn, int* pair) {
   double best = 0.0;
   for (int cand_pair = 0; cand_pair <= 1; ++cand_pair) {
     for (int cand_bn : {128, 256}) {
@@ -83,6 +87,7 @@ static void choose_long_k_residual(int rows, int n, int k, int num_sms, int* bn,
       const long rows_per_tile = cand_pair ? 2 * GEMM_BM : GEMM_BM;
       const long tiles = (rows + rows_per_tile - 1) / rows_per_tile * (n / cand_bn);
       const long units = cand_pair ? num_sms / 2 : num_sms;
+      if (tiles * 4 < units * 3) continue;
       const long waves = (tiles + units - 1) / units;
       const double b_bytes = (cand_pair ? cand_bn / 2 : cand_bn) * GEMM_BK * 2.0;
       const double smem_clk = 2.0 * (GEMM_BM * GEMM_BK * 2.0 + b_bytes) / 128.0;
@@ -95,14 +100,14 @@ static void choose_long_k_residual(int rows, int n, int k, int num_sms, int* bn,
       }
     }
   }
+  return best != 0.0;
 }
 
 void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair) {
   const bool residual = epi == EPI_BIAS_RESIDUAL_F32 || epi == EPI_RESIDUAL_F32_STATS;
-  if (residual && k >= 2048 && n % 128 == 0 && num_sms >= 2) {
-    choose_long_k_residual(rows, n, k, num_sms, bn, pair);
+  if (residual && k >= 2048 && n % 128 == 0 && num_sms >= 2 &&
+      choose_long_k_residual(rows, n, k, num_sms, bn, pair))
     return;
-  }
   *bn = gemm_choose_bn(rows, n, num_sms);
   // CTA pairs (256-row tiles) cut each SM's operand traffic by a third and deepen the
   // ring, which pays where the main loop dominates: long K, and enough tiles that the

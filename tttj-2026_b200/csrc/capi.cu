@@ -686,23 +686,13 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     float2* st_ln1 = p->stats;
     float2* st_ln2 = p->stats + (size_t)T * stats_parts(*cfg);
     if (l == 0) {
-      // Tile widths of the residual GEMMs, which fix the partial counts.  Every layer
-      // has the same shapes, so layer 0's choice holds for all.
-      GemmLaunch probe_out, probe_ffn;
-      rc = build_gemm(&probe_out, p->ctx, Q, W(l, TTTJ_W_OUT), Q,
-                      reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid, D,
-                      T, rows_dev, D, Q, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
-      if (!rc)
-        rc = build_gemm(&probe_ffn, p->hid, F, W(l, TTTJ_W_FFN_OUT), F,
-                        reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_OUT)), p->resid, D,
-                        p->resid, D, T, rows_dev, D, F, EPI_RESIDUAL_F32_STATS, p->status,
-                        p->num_sms);
-      if (rc) {
-        delete p;
-        return rc;
-      }
-      p->parts_ln2 = 2 * ((D + probe_out.bn - 1) / probe_out.bn);
-      p->parts = 2 * ((D + probe_ffn.bn - 1) / probe_ffn.bn);
+      // Tile widths of the residual GEMMs (the choice build_gemm makes below), which
+      // fix the partial counts; every layer has the same shapes.
+      int out_bn = 0, ffn_bn = 0, pair = 0;
+      gemm_choose(T, D, Q, EPI_RESIDUAL_F32_STATS, p->num_sms, &out_bn, &pair);
+      gemm_choose(T, D, F, EPI_RESIDUAL_F32_STATS, p->num_sms, &ffn_bn, &pair);
+      p->parts_ln2 = 2 * ((D + out_bn - 1) / out_bn);
+      p->parts = 2 * ((D + ffn_bn - 1) / ffn_bn);
     }
     rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * Q, nullptr, 0, T, rows_dev,
                     3 * Q, D, EPI_LN_FOLD, p->status, p->num_sms);

@@ -251,6 +251,15 @@ int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream)
 /* Number of SMs of `device` (grid sizing of the persistent kernels). */
 int tttj_device_sm_count(int device);
 
+/* Tile shape of a GEMM of rows x n x k with `epilogue` on num_sms SMs, as tttj_linear
+ * and the forward choose it: *bn = output columns per tile (64, 128 or 256), *pair = 1
+ * for 256-row tiles computed by a CTA pair.  Host-only (no device is touched).
+ * `epilogue` is a TTTJ_EPI_* code or one of the forward's fused epilogues below. */
+#define TTTJ_EPI_RESIDUAL_F32_STATS 4 /* out_proj / ffn_out: fp32 residual + LN statistics */
+#define TTTJ_EPI_LN_FOLD 5            /* QKV: LayerNorm folded into the weights */
+#define TTTJ_EPI_LN_FOLD_GELU 6       /* ffn_in: LayerNorm fold + erf-GELU */
+int tttj_gemm_tile(int rows, int n, int k, int epilogue, int num_sms, int* bn, int* pair);
+
 #ifdef __cplusplus
 }
 #endif

@@ -131,3 +131,52 @@ def test_linear_argument_checks_do_not_launch():
     assert rc == _lib.TTTJ_ERR_INVALID
     assert b"multiple of 32" in lib.tttj_last_error()
     assert lib.tttj_attention_workspace_bytes(4, 300, 3) > 0
+
+
+def _tile(rows, n, k, epi, sms=148):
+    bn, pair = ctypes.c_int(), ctypes.c_int()
+    assert _lib.lib().tttj_gemm_tile(rows, n, k, epi, sms, ctypes.byref(bn), ctypes.byref(pair)) == 0
+    return bn.value, pair.value
+
+
+STATS, FOLD, FOLD_GELU, RES_F32 = 4, 5, 6, 3
+
+
+@pytest.mark.parametrize(
+    "what,rows,n,k,epi,expect",
+    [
+        # C2 on one B200 (the launch list in profiles/launches_c2_forward.md)
+        ("C2 qkv", 8192, 1536, 512, FOLD, (256, 0)),
+        ("C2 out_proj", 8192, 512, 512, STATS, (128, 0)),
+        ("C2 ffn_in", 8192, 2048, 512, FOLD_GELU, (256, 0)),
+        ("C2 ffn_out", 8192, 512, 2048, STATS, (256, 1)),
+        # C2's per-GPU share at 2 and at 4 / 8 GPUs
+        ("C2/2 ffn_out", 4096, 512, 2048, STATS, (128, 1)),
+        ("C2/2 out_proj", 4096, 512, 512, STATS, (64, 0)),
+        ("C2/4 ffn_out", 2048, 512, 2048, STATS, (64, 0)),
+        ("C2/8 ffn_out", 1024, 512, 2048, STATS, (64, 0)),
+        # C4 / C5: CTA pairs where the main loop dominates, not under the GELU epilogue
+        ("C4 qkv", 32768, 2304, 768, FOLD, (256, 0)),
+        ("C4 ffn_out", 32768, 768, 3072, STATS, (256, 1)),
+        ("C5 qkv", 65536, 3072, 1024, FOLD, (256, 1)),
+        ("C5 out_proj", 65536, 1024, 1024, STATS, (256, 1)),
+        ("C5 ffn_in", 65536, 4096, 1024, FOLD_GELU, (256, 0)),
+        ("C5 ffn_out", 65536, 1024, 4096, STATS, (256, 1)),
+        # small shapes fall back to narrow single-CTA tiles
+        ("C1 ffn_out", 256, 256, 1024, RES_F32, (64, 0)),
+        ("C3 ffn_out", 16384, 256, 1024, STATS, (128, 0)),
+    ],
+)
+def test_gemm_tile_choices(what, rows, n, k, epi, expect):
+    """The tile-shape rules (widest tile filling the SMs; CTA pairs for long K; the
+    shared-memory model for long-K residual GEMMs) give the shapes measured best."""
+    assert _tile(rows, n, k, epi) == expect, what
+
+
+def test_gemm_tile_rejects_bad_arguments():
+    bn, pair = ctypes.c_int(), ctypes.c_int()
+    L = _lib.lib()
+    assert L.tttj_gemm_tile(128, 0, 64, 0, 148, ctypes.byref(bn), ctypes.byref(pair)) != 0
+    assert L.tttj_gemm_tile(128, 128, 64, 7, 148, ctypes.byref(bn), ctypes.byref(pair)) != 0
+    assert L.tttj_gemm_tile(128, 128, 64, 0, 0, ctypes.byref(bn), ctypes.byref(pair)) != 0
+    assert L.tttj_gemm_tile(128, 128, 64, 0, 148, None, ctypes.byref(pair)) != 0

@@ -601,6 +601,19 @@ size_t tttj_workspace_bytes(const tttj_config* cfg) {
 
 int tttj_device_sm_count(int device) { return sm_count(device); }
 
+int tttj_gemm_tile(int rows, int n, int k, int epilogue, int num_sms, int* bn, int* pair) {
+  static_assert(TTTJ_EPI_RESIDUAL_F32_STATS == EPI_RESIDUAL_F32_STATS &&
+                    TTTJ_EPI_LN_FOLD == EPI_LN_FOLD && TTTJ_EPI_LN_FOLD_GELU == EPI_LN_FOLD_GELU &&
+                    TTTJ_EPI_BIAS_RESIDUAL_F32 == EPI_BIAS_RESIDUAL_F32,
+                "public and internal epilogue codes differ");
+  if (!bn || !pair) return fail(TTTJ_ERR_INVALID, "gemm_tile: null output");
+  if (rows < 0 || n <= 0 || k <= 0 || num_sms <= 0 || epilogue < 0 ||
+      epilogue > TTTJ_EPI_LN_FOLD_GELU)
+    return fail(TTTJ_ERR_INVALID, "gemm_tile: bad arguments");
+  gemm_choose(rows, n, k, epilogue, num_sms, bn, pair);
+  return TTTJ_OK;
+}
+
 int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
                      size_t workspace_bytes, tttj_plan** out_plan) {
   int rc = check_config(cfg);

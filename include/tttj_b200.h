@@ -132,6 +132,10 @@ int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* val
 int tttj_plan_set_path(tttj_plan* plan, int path);
 /* 1 if tttj_forward of this plan runs the resident-stack kernel, 0 if layer by layer. */
 int tttj_plan_path(tttj_plan* plan);
+/* Host-only view of the same decision for a configuration: *fits = 1 if the resident
+ * kernel can run it (TTTJ_PATH_RESIDENT accepted), *preferred = 1 if TTTJ_PATH_AUTO
+ * takes it, *heads_per_step = heads per attention step inside the resident kernel. */
+int tttj_path_choice(const tttj_config* cfg, int* fits, int* preferred, int* heads_per_step);
 
 /* Per-stage capture for numerics bisection: the same forward as tttj_forward (always
  * layer by layer), which also writes, for batch index `sequence` at block `layer`, the

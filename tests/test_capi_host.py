@@ -180,3 +180,37 @@ def test_gemm_tile_rejects_bad_arguments():
     assert L.tttj_gemm_tile(128, 128, 64, 7, 148, ctypes.byref(bn), ctypes.byref(pair)) != 0
     assert L.tttj_gemm_tile(128, 128, 64, 0, 0, ctypes.byref(bn), ctypes.byref(pair)) != 0
     assert L.tttj_gemm_tile(128, 128, 64, 0, 148, None, ctypes.byref(pair)) != 0
+
+
+def _path_choice(shape):
+    c = _c(*shape)
+    fits, preferred, gh = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    rc = _lib.lib().tttj_path_choice(ctypes.byref(c), ctypes.byref(fits), ctypes.byref(preferred),
+                                     ctypes.byref(gh))
+    assert rc == 0
+    return fits.value, preferred.value, gh.value
+
+
+@pytest.mark.parametrize("n", range(1, 15))
+def test_path_choice_for_the_reference_cases(n):
+    """The reference's 14 cases (optimized_transformer.py:22-42): the resident kernel
+    fits and is auto-selected for sequences of <= 128 tokens with d_model <= 256 (cases
+    1-7, 9-12), heads paired when 32 wide and even in number; cases 8 (d_model 1024),
+    13 (1024 tokens) and 14 (100k tokens) run layer by layer."""
+    from tttj_2026_b200.cases import case_config
+    c = case_config(n)
+    shape = (c.batch_size, c.seq_len, c.d_model, c.num_heads, c.ffn_dim, c.num_layers, c.causal)
+    fits, preferred, gh = _path_choice(shape)
+    resident = n not in (8, 13, 14)
+    assert (fits, preferred) == ((1, 1) if resident else (0, 0))
+    if resident:
+        assert gh == (1 if n in (9, 10) else 2)  # hd 128 / 64 heads go one at a time
+
+
+@pytest.mark.parametrize("name", sorted(CONFIGS))
+def test_path_choice_for_the_baseline_configs(name):
+    """C1 fits the resident kernel but stays layer by layer (1.6 MB of weights per
+    layer: measured 0.156 vs 0.076 ms); C2-C5 have sequences longer than 128 tokens."""
+    B, S, D, H, F, L, causal, _, _ = CONFIGS[name]
+    fits, preferred, _ = _path_choice((B, S, D, H, F, L, causal))
+    assert (fits, preferred) == ((1, 0) if name == "C1" else (0, 0))

@@ -58,6 +58,9 @@ _SIGNATURES = {
         _c.c_int, [_vp, _vp, _c.c_int, _c.c_int, _vp, _vp, _c.c_float, _vp]
     ),
     "tttj_attention_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int, _c.c_int]),
+    "tttj_path_choice": (
+        _c.c_int, [_vp, _c.POINTER(_c.c_int), _c.POINTER(_c.c_int), _c.POINTER(_c.c_int)]
+    ),
     "tttj_gemm_tile": (
         _c.c_int,
         [_c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.POINTER(_c.c_int),

@@ -601,6 +601,16 @@ size_t tttj_workspace_bytes(const tttj_config* cfg) {
 
 int tttj_device_sm_count(int device) { return sm_count(device); }
 
+int tttj_path_choice(const tttj_config* cfg, int* fits, int* preferred, int* heads_per_step) {
+  int rc = check_config(cfg);
+  if (rc) return rc;
+  if (!fits || !preferred || !heads_per_step) return fail(TTTJ_ERR_INVALID, "path_choice: null output");
+  *fits = resident_fits(*cfg) ? 1 : 0;
+  *preferred = (*fits && resident_preferred(*cfg)) ? 1 : 0;
+  *heads_per_step = resident_gh(*cfg);
+  return TTTJ_OK;
+}
+
 int tttj_gemm_tile(int rows, int n, int k, int epilogue, int num_sms, int* bn, int* pair) {
   static_assert(TTTJ_EPI_RESIDUAL_F32_STATS == EPI_RESIDUAL_F32_STATS &&
                     TTTJ_EPI_LN_FOLD == EPI_LN_FOLD && TTTJ_EPI_LN_FOLD_GELU == EPI_LN_FOLD_GELU &&

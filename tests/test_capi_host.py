@@ -150,7 +150,7 @@ STATS, FOLD, FOLD_GELU, RES_F32 = 4, 5, 6, 3
         ("C2 out_proj", 8192, 512, 512, STATS, (128, 0)),
         ("C2 ffn_in", 8192, 2048, 512, FOLD_GELU, (256, 0)),
         ("C2 ffn_out", 8192, 512, 2048, STATS, (256, 1)),
-        # C2's per-GPU share at 2 and at 4 / 8 GPUs
+        # C2's batch sharded over 2 and over 4 / 8 GPUs (distributed_forward)
         ("C2/2 ffn_out", 4096, 512, 2048, STATS, (128, 1)),
         ("C2/2 out_proj", 4096, 512, 512, STATS, (64, 0)),
         ("C2/4 ffn_out", 2048, 512, 2048, STATS, (64, 0)),

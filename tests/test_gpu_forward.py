@@ -59,8 +59,8 @@ def test_baseline_config_vs_oracle(name):
 
 @pytest.mark.parametrize("batch", [4, 1])
 def test_c2_per_rank_shapes_vs_oracle(batch):
-    """C2's per-GPU share at 2 and 8 GPUs (bench.py --gpus N shards the batch): fewer
-    rows change the tile choices (at 2 GPUs ffn_out runs CTA-pair 256 x 128 tiles and
+    """C2's batch sharded over 2 and 8 GPUs (distributed_forward / MultiDeviceTransformer
+    give each GPU an LPT share of the sequences): fewer rows change the tile choices (at 2 GPUs ffn_out runs CTA-pair 256 x 128 tiles and
     out_proj 64-wide ones, so the two LayerNorms read different statistics partial
     counts; at 8 GPUs both run 64-wide tiles)."""
     B, S, D, H, F, L, causal, dtype, lengths = CONFIGS["C2"]

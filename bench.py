@@ -119,7 +119,7 @@ def make_case(name: str, seed: int, rank: int, device):
     return cfg, model, x, mask
 
 
-def useful_work(cfg, mask, out_bytes: int = 2):
+def useful_work(cfg, mask, x_bytes: int = 2):
     """Valid tokens, attention pairs and per-class FLOPs / bytes of one forward."""
     import torch
 
@@ -141,9 +141,10 @@ def useful_work(cfg, mask, out_bytes: int = 2):
         "gemm_ffn_in_gelu": ("tensor", 2.0 * Tv * F * D),
         "gemm_ffn_out": ("tensor", 2.0 * Tv * D * F),
         "attention": ("tensor", 4.0 * hd * H * pairs),
-        # bytes: fp16 row read + fp16 row write
-        "layernorm": ("hbm", 4.0 * Tv * D),
-        "final_layernorm_scatter": ("hbm", 2.0 * Tv * D + B * S * D * out_bytes),
+        # bytes.  Gather: x row in (x's dtype), fp32 residual row + its fp16 copy out.
+        # Final: fp32 residual row in, every [B, S] output row out (zeros included).
+        "layernorm": ("hbm", (x_bytes + 4.0 + 2.0) * Tv * D),
+        "final_layernorm_scatter": ("hbm", 4.0 * Tv * D + B * S * D * x_bytes),
         "plan_tokens": ("hbm", float(B * S)),
     }
     flops = (2.0 * Tv * (4 * D * D + 2 * D * F) + 4.0 * hd * H * pairs) * cfg.num_layers

@@ -70,3 +70,44 @@ def test_traffic_lookup_reads_the_committed_summaries(bench):
 def test_workload_labels(bench):
     assert bench.workload_desc("C2").startswith("C2: L4 D512 H8 hd64 F2048 B8 S1024 causal, mask=None")
     assert "reference case 5" in bench.workload_desc("R5")
+
+
+def _run_bench(args, env_extra=None, timeout=300):
+    import json
+    import os
+    import subprocess
+    import sys
+    env = dict(os.environ)
+    env.update(env_extra or {})
+    r = subprocess.run([sys.executable, str(REPO / "bench.py"), *args], cwd=REPO, env=env,
+                       capture_output=True, text=True, timeout=timeout)
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    return r.returncode, [json.loads(l) for l in lines], r.stdout
+
+
+def test_reference_arm_prints_one_contract_line():
+    """`bench.py --impl reference` (the CPU arm the driver runs beside ours): one JSON
+    line with the metric, a cpu_baseline block and a zero-copy e2e block."""
+    rc, lines, _ = _run_bench(["--impl", "reference", "--config", "C1", "--steps", "2",
+                               "--warmup", "1"])
+    assert rc == 0 and len(lines) == 1
+    d = lines[0]
+    assert d["impl"] == "reference" and d["metric"] == "forward tokens/sec"
+    assert d["unit"] == "tokens/s" and d["higher_is_better"] is True and d["value"] > 0
+    assert d["steps"] == 2 and d["warmup"] == 1 and d["n_gpus"] == 1
+    assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
+    assert d["e2e"] == {"value": d["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}
+
+
+def test_reference_arm_other_ranks_stay_silent():
+    rc, lines, out = _run_bench(["--impl", "reference", "--config", "C1", "--steps", "1",
+                                 "--warmup", "0"], {"RANK": "1", "WORLD_SIZE": "2"})
+    assert rc == 0 and lines == [] and out.strip() == ""
+
+
+def test_reference_arm_without_a_bounded_sample_says_unavailable():
+    rc, lines, _ = _run_bench(["--impl", "reference", "--config", "R14", "--steps", "1",
+                               "--warmup", "0"])
+    assert rc == 0 and len(lines) == 1
+    assert lines[0]["impl"] == "reference" and "unavailable" in lines[0]

@@ -1,22 +1,27 @@
 #!/usr/bin/env python3
 """Forward tokens/s of the B200 transformer path (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C2] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C5] [--impl b200|reference]
 
 A step is one forward of the whole stack (L blocks + final LayerNorm + masking)
-over one batch of the chosen BASELINE.json configuration (default C2 =
-L4 D512 H8 F2048, batch 8 x seq 1024, causal, fp16).  With N > 1 the
-script runs under torchrun, one process per GPU; every rank processes its own
-batch of the configuration (weak scaling, no collective on the data path) and the
-reported time is the max over ranks.
+over one batch of the chosen BASELINE.json configuration.  The default is C5
+(configs[4]: L24 D1024 H16 F4096, batch 256 x seq 256, causal + prefix padding, fp16),
+the largest configuration that fits one GPU.  With N > 1 the script runs under
+torchrun, one process per GPU, and the configuration's batch is split across the
+ranks (strong scaling: the same 256 sequences in total, each rank an LPT share by
+predicted cost, tttj_2026_b200.sharding.local_shard); no collective runs on the data
+path and the reported time is the max over ranks.
 
 --impl b200 (default): the CUDA path through make_optimized_transformer.
-  value      tokens/s, inputs resident in HBM, L2 flushed between steps
+  value      tokens/s of the whole batch, each rank's shard resident in its HBM,
+             L2 flushed between steps
   e2e        the same through the public module call with pinned host buffers:
-             H2D of x and the mask + forward + D2H of the output every step, run
-             as a serving loop runs it (the next step's H2D and the previous step's
-             D2H on a copy stream, overlapping the current forward; the L2 flush
-             between forwards stays inside the timed span)
+             H2D of each rank's x and mask + forward + D2H of its output every step,
+             run as a serving loop runs it (the next step's H2D and the previous
+             step's D2H on a copy stream, overlapping the current forward; the L2
+             flush between forwards stays inside the timed span)
+  gather_to_rank0  (N > 1) distributed_forward with the whole batch on every rank:
+             shard select + forward + NCCL gather of the outputs to rank 0
   roofline   the dominant kernel class, timed with CUDA events inside real forwards
   cpu_baseline  the fp32 oracle (op-for-op restatement of the reference module's
              PyTorch eager forward) on the host cores, bounded sample (rank 0, N=1)
@@ -80,7 +85,7 @@ def parse_args(argv=None):
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", default="C2", choices=list(CONFIGS))
+    ap.add_argument("--config", default="C5", choices=list(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--path", default="auto", choices=["auto", "layerwise", "resident"],
@@ -104,7 +109,8 @@ def workload_desc(name: str) -> str:
             f"{'causal' if causal else 'non-causal'}, {mask}, {dt}")
 
 
-def make_case(name: str, seed: int, rank: int, device):
+def make_case(name: str, seed: int, device):
+    """Weights and the whole batch of inputs (the same seeds on every rank)."""
     import torch
 
     import optimized_transformer  # noqa: F401
@@ -114,9 +120,18 @@ def make_case(name: str, seed: int, rank: int, device):
     dtype = getattr(torch, dt)
     cfg = tb.TransformerConfig(B, S, D, H, F, L, causal)
     model = tb.make_parameter_model(cfg, seed, dtype, device)
-    # Each rank gets its own batch (different input seed), same weights.
-    x, mask = tb.generate_inputs(cfg, seed + 1 + 1000 * rank, dtype, lens, device)
+    x, mask = tb.generate_inputs(cfg, seed + 1, dtype, lens, device)
     return cfg, model, x, mask
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def useful_work(cfg, mask, x_bytes: int = 2):
@@ -181,6 +196,7 @@ class ClockSampler:
 
         self.proc = None
         self.path = None
+        self.out = None
         try:
             props = torch.cuda.get_device_properties(device_index)
             self.bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
@@ -188,16 +204,29 @@ class ClockSampler:
             self.bus = None
 
     def start(self):
+        self.out = None
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
             if self.bus:
                 cmd += ["-i", self.bus]
-            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.out = open(self.path, "w")
+            self.proc = subprocess.Popen(cmd, stdout=self.out, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            self._cleanup()
         return self
+
+    def _cleanup(self):
+        if self.out is not None:
+            self.out.close()
+            self.out = None
+        if self.path is not None:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
 
     def stop(self):
         if self.proc is None:
@@ -207,6 +236,9 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
+            self.proc.wait()
+        self.out.close()
+        self.out = None
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
@@ -216,7 +248,7 @@ class ClockSampler:
                 rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
             except ValueError:
                 continue
-        os.unlink(self.path)
+        self._cleanup()
         if not rows:
             return None
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -307,12 +339,12 @@ def run_reference(args, rank: int, world: int):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic",
         "config": {"workload": workload_desc(name), "global_batch": B, "seq_len": S,
                    "parallelism": "cpu"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": sample},
+                         "cpu_model": cpu_model(), "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -327,10 +359,20 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     torch.cuda.set_device(dev)
     import optimized_transformer  # noqa: F401
     import tttj_2026_b200 as tb
+    from tttj_2026_b200 import sharding
 
     name = args.config
     B, S = CONFIGS[name][0], CONFIGS[name][1]
-    cfg, model, x, mask = make_case(name, args.seed, rank, dev)
+    cfg_full, model, x_full, mask_full = make_case(name, args.seed, dev)
+    # This rank's LPT share of the batch (every sequence at N = 1), resident in HBM.
+    lengths = sharding.lengths_of(mask_full, B, S)
+    mine = sharding.local_shard(lengths, cfg_full, rank, world)
+    sel = torch.as_tensor(mine, device=dev, dtype=torch.long)
+    x = x_full.index_select(0, sel).contiguous()
+    mask = None if mask_full is None else mask_full.index_select(0, sel).contiguous()
+    b_local = len(mine)
+    cfg = tb.TransformerConfig(b_local, S, cfg_full.d_model, cfg_full.num_heads, cfg_full.ffn_dim,
+                               cfg_full.num_layers, cfg_full.causal)
     opt = tb.make_optimized_transformer(model)
     opt.set_path(args.path)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
@@ -424,25 +466,60 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         barrier()
         e2e_total_ms = max_over_ranks(e2e_span_ms)
         ok_e2e = torch.equal(out_last, opt(x, mask).cpu())
+        if world > 1:  # bytes copied per step by all ranks together
+            nb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+            dist.all_reduce(nb)
+            h2d, d2h = int(nb[0].item()), int(nb[1].item())
+
+        # ---- N > 1: the whole batch on every rank, gathered to rank 0 ----
+        gathered = None
+        if world > 1:
+            def gather_step():
+                out, _ = sharding.distributed_forward(opt, x_full, mask_full, dst=0)
+                return out
+
+            for _ in range(args.warmup):
+                gather_step()
+                flush.zero_()
+            g0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            g1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+            barrier()
+            torch.cuda.synchronize(dev)
+            for i in range(args.steps):
+                g0[i].record(stream)
+                out_full = gather_step()
+                g1[i].record(stream)
+                flush.zero_()
+            torch.cuda.synchronize(dev)
+            barrier()
+            g_ms = max_over_ranks(sum(a.elapsed_time(b_) for a, b_ in zip(g0, g1)))
+            gathered = {"value": B * S * args.steps / (g_ms / 1e3), "unit": UNIT,
+                        "ms_per_step": g_ms / args.steps,
+                        "what": "distributed_forward(module, x, mask, dst=0): every rank holds "
+                                "the whole batch, runs its LPT shard, NCCL gather to rank 0"}
+            if rank == 0:
+                gathered["output_matches_local_shard"] = bool(torch.equal(
+                    out_full.index_select(0, sel), opt(x, mask)))
 
         # ---- per-kernel-class timing inside real forwards ----
-        opt.set_kernel_timing(B, S, True)
+        opt.set_kernel_timing(b_local, S, True)
         for _ in range(args.steps):
             opt(x, mask)
             flush.zero_()
-        ktimes = opt.kernel_times(B, S)
-        opt.set_kernel_timing(B, S, False)
-        launches = opt.launches_per_forward(B, S)
+        ktimes = opt.kernel_times(b_local, S)
+        opt.set_kernel_timing(b_local, S, False)
+        launches = opt.launches_per_forward(b_local, S)
         opt.device_status()
     clk = clocks.stop()
 
     if rank != 0:
         return 0
 
-    tokens = B * S
-    value = world * tokens * args.steps / (total_ms / 1e3)
-    e2e_value = world * tokens * args.steps / (e2e_total_ms / 1e3)
-    Tv, pairs, per_launch, flops = useful_work(cfg, mask, x.element_size())
+    tokens = B * S  # the whole batch, all ranks together
+    value = tokens * args.steps / (total_ms / 1e3)
+    e2e_value = tokens * args.steps / (e2e_total_ms / 1e3)
+    Tv, pairs, per_launch, flops_local = useful_work(cfg, mask, x.element_size())
+    Tv_full, _, _, flops_full = useful_work(cfg_full, mask_full, x.element_size())
     peaks = load_peaks()
     ms_per_step = total_ms / args.steps
     long_step = ms_per_step >= LONG_STEP_MS
@@ -468,7 +545,7 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         v["share"] = round(v["total_ms"] / ksum, 4) if ksum else None
     dom = max(kernels, key=lambda k: kernels[k]["total_ms"])
     dk = kernels[dom]
-    traffic = _profile_traffic(dom, name)
+    traffic = _profile_traffic(dom, name) if world == 1 else None
     roofline = {"kernel": dom, "bound": dk["bound"], "achieved": dk["achieved"],
                 "peak": tensor_peak if dk["bound"] == "tensor" else peaks["hbm_gbs"],
                 "unit": dk["unit"], "frac": dk["frac"], "traffic": traffic,
@@ -479,7 +556,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
         threads = os.cpu_count() or 1
         cval, sample, _ = cpu_oracle_rate(name, args.seed, args.cpu_seconds, threads)
         if cval is not None:
-            cpu = {"value": cval, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample}
+            cpu = {"value": cval, "unit": UNIT, "cores": threads, "kind": "port",
+                   "cpu_model": cpu_model(), "sample": sample}
 
     vs_baseline = None
     if name.startswith("R") and world == 1:
@@ -488,22 +566,27 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": vs_baseline, "dtype": "fp16", "data": "synthetic",
-        "config": {"workload": workload_desc(name), "global_batch": world * B, "seq_len": S,
-                   "parallelism": f"dp{world}", "l2": "flushed between steps (256 MiB write)",
-                   "path": ("resident stack (1 launch per forward)" if opt.uses_resident(B, S)
+        "scaling": "strong", "vs_baseline": vs_baseline, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": workload_desc(name), "global_batch": B, "seq_len": S,
+                   "parallelism": f"dp{world} (batch split, LPT by predicted cost; "
+                                  f"rank 0 runs {b_local} of {B} sequences)",
+                   "l2": "flushed between steps (256 MiB write)",
+                   "path": ("resident stack (1 launch per forward)" if opt.uses_resident(b_local, S)
                             else f"layer by layer ({launches} launches per forward)"),
                    "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",
-                   "inputs": f"x~N(0,1), input seed {args.seed + 1} (+1000*rank)"},
+                   "inputs": f"x~N(0,1), input seed {args.seed + 1}"},
         "p50_ms": statistics.median(step_ms),
-        "valid_tokens_per_s": world * Tv * args.steps / (total_ms / 1e3),
-        "useful_tflops": flops / (ms_per_step * 1e-3) / 1e12,
-        "useful_frac_of_peak": flops / (ms_per_step * 1e-3) / 1e12 / tensor_peak,
+        "valid_tokens_per_s": Tv_full * args.steps / (total_ms / 1e3),
+        "useful_tflops_per_gpu": flops_full / world / (ms_per_step * 1e-3) / 1e12,
+        "useful_frac_of_peak": flops_full / world / (ms_per_step * 1e-3) / 1e12 / tensor_peak,
         "roofline": roofline,
         "kernels": kernels,
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_total_ms / args.steps, "output_matches_device_path": ok_e2e},
+                "ms_per_step": e2e_total_ms / args.steps, "output_matches_device_path": ok_e2e,
+                "copies": "each rank copies its own shard in and its output shard out "
+                          "(bytes summed over ranks)"},
+        "gather_to_rank0": gathered,
         "clocks": clk,
         "gpu_launches": launches * args.steps,
         "launches_per_step": launches,

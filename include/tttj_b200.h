@@ -88,31 +88,54 @@ size_t tttj_weights_bytes(const tttj_config* cfg);
 int tttj_weight_offset(const tttj_config* cfg, int layer, int field, size_t* offset,
                        size_t* bytes);
 
-/* Device workspace the forward needs (activations of the packed valid tokens,
- * LayerNorm statistics, the LayerNorm-folded QKV / ffn_in weights, token plan, device
- * status word).  It must be zero-filled once before the first
- * forward (the plan never reads a byte the same call did not write, except rows of
- * earlier calls, which stay finite). */
+/* LayerNorm-folded weights.  Each block's LN1 affine is folded into a copy of its QKV
+ * weights and LN2's into ffn_in (W' = W diag(gamma) in fp16, b' = b + W beta, column
+ * sums of W'), so the GEMMs consume the raw residual and apply the row statistics in
+ * their epilogue; padded-head layouts (head_dim < 32 or between kernel sizes) also get
+ * a zero-column copy of out_proj here.  The folded weights depend on the layer shapes
+ * only (not on batch_size / seq_len): one buffer serves every plan of a model.
+ * tttj_fold_weights enqueues the one-time fold kernels on `stream`; the packed weights
+ * must be complete in stream order, and plans may be created at once (they launch
+ * nothing).  Buffers are device memory, 256-byte aligned.  Replaces the reference's
+ * one-time packing step SequenceResidentTransformer.prepare
+ * (kernels/sequence_resident.py:143-150). */
+size_t tttj_folded_bytes(const tttj_config* cfg);
+int tttj_fold_weights(const tttj_config* cfg, const void* weights, void* folded,
+                      size_t folded_bytes, void* stream);
+
+/* Device workspace of a plan (activations of the packed valid tokens, LayerNorm
+ * statistics with their per-row pivots, token plan, device status word).  It must be
+ * zero-filled once before the first forward (the plan never reads a byte the same
+ * call did not write, except rows of earlier calls, which no result depends on). */
 size_t tttj_workspace_bytes(const tttj_config* cfg);
 
-/* A plan binds a configuration to one device, one packed weight buffer and one
- * workspace (all owned by the caller), and pre-builds every TMA descriptor.  It also
- * folds each block's LayerNorm affine into a copy of the QKV / ffn_in weights kept in
- * the workspace (one-time kernels on the legacy default stream, which it synchronises;
- * the weight buffer must be complete when it is called).  Replaces
- * SequenceResidentTransformer.prepare (kernels/sequence_resident.py:143-150). */
+/* A plan binds a configuration (batch_size, seq_len included) to one device, one packed
+ * weight buffer, one folded weight buffer and one workspace (all owned by the caller),
+ * and pre-builds every TMA descriptor.  Creating it launches nothing and does not
+ * synchronise.  It owns a pinned host word mirroring its device status (see
+ * tttj_forward) and an event ordering its forwards across streams; destroying it
+ * waits for its last forward, so the caller may then free or reuse the workspace.
+ * Replaces SequenceResidentTransformer's per-shape state
+ * (kernels/sequence_resident.py:125-233). */
 typedef struct tttj_plan tttj_plan;
-int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
-                     size_t workspace_bytes, tttj_plan** out_plan);
+int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                     void* workspace, size_t workspace_bytes, tttj_plan** out_plan);
 int tttj_plan_destroy(tttj_plan* plan);
 
 /* One forward pass, enqueued on `stream` (no host synchronisation).
  *   x          [B, S, D] in x_dtype (TTTJ_DTYPE_F16 or TTTJ_DTYPE_F32)
  *   valid_mask [B, S] bytes (0 = padded token), or NULL = every token valid
  *   out        [B, S, D] in x_dtype; padded rows are written as exact zeros.
+ * A forward on another stream than the plan's previous forward first waits for that
+ * one (the workspace is the plan's): forwards of one plan never overlap.
+ * Device errors surface without a synchronisation: the last kernel of each forward
+ * copies a non-zero device status word (a bounded device wait gave up) into the plan's
+ * pinned host mirror, and the next tttj_forward of the plan that finds it set returns
+ * TTTJ_ERR_DEVICE_TIMEOUT (launching nothing) and clears it.
  * Replaces the pybind forward(input, valid_mask, packed_weights, capture_debug)
- * (kernels/csrc/sequence_resident.cpp:23-32) and the Python forward
- * SequenceResidentTransformer.forward (kernels/sequence_resident.py:227-233). */
+ * (kernels/csrc/sequence_resident.cpp:23-32), its per-launch error check
+ * (C10_CUDA_KERNEL_LAUNCH_CHECK, kernels/csrc/sequence_resident.cu:531) and the Python
+ * forward SequenceResidentTransformer.forward (kernels/sequence_resident.py:227-233). */
 int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
                  void* out, void* stream);
 
@@ -156,7 +179,8 @@ int tttj_forward_debug(tttj_plan* plan, const void* x, int x_dtype, const uint8_
                        void* out, int layer, int sequence, float* debug, void* stream);
 
 /* Synchronise the plan's device and read (then clear) the device status word that
- * bounded device waits write on timeout.  *device_status = 0 when healthy. */
+ * bounded device waits write on timeout, and its host mirror.  *device_status = 0
+ * when healthy. */
 int tttj_plan_status(tttj_plan* plan, int* device_status);
 
 /* ---- instrumentation ---- */
@@ -238,10 +262,13 @@ int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* vali
  * in a fixed device array of TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES inside the library
  * (held on every GPU that loads the library until the process exits).  Shapes whose
  * plan does not fit return TTTJ_ERR_INVALID without launching anything.  It calls no
- * allocation routine.  The first call on a device looks up the array's device address
- * (with that device current); make that first call before any stream capture.  All
- * calls on a device share the array, so calls that overlap on the GPU race; nothing in
- * it needs clearing between calls. */
+ * allocation routine itself.  The first call in each CUDA context (the first call on a
+ * device, and again after cudaDeviceReset) looks up the array's device address with
+ * that device current, and under lazy module loading may make the CUDA runtime load
+ * the library's device code, which allocates: make that first call -- a warm-up call
+ * at start-up will do -- before any stream capture and outside any allocator or
+ * memory-pool callback.  All calls on a device share the array, so calls that overlap
+ * on the GPU race; nothing in it needs clearing between calls. */
 #define TTTJ_ATTENTION_NOALLOC_SCRATCH_BYTES (4u << 20)
 int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows, const uint8_t* valid_mask,
                            int batch, int seq_len, int d_model, int num_heads, int causal,
@@ -251,6 +278,10 @@ int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows, const uint8
  * that is never signalled gives up after limit_ns and writes 0x1ff into *status_dev.
  * No counterpart in the reference (its device waits are unbounded). */
 int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream);
+/* The same wait, reported through a plan (its device status word and host mirror, as a
+ * forward's kernel would report it): the plan's next tttj_forward returns
+ * TTTJ_ERR_DEVICE_TIMEOUT.  limit_ns <= 1 s. */
+int tttj_plan_selftest_timeout(tttj_plan* plan, uint64_t limit_ns, void* stream);
 
 /* Number of SMs of `device` (grid sizing of the persistent kernels). */
 int tttj_device_sm_count(int device);

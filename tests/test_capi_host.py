@@ -117,8 +117,15 @@ def test_plan_create_rejects_bad_arguments():
     lib = _lib.lib()
     c = _c(2, 16, 64, 1, 128, 1, False)
     out = ctypes.c_void_p()
-    assert lib.tttj_plan_create(ctypes.byref(c), 0, None, None, 0, ctypes.byref(out)) == _lib.TTTJ_ERR_INVALID
+    assert lib.tttj_plan_create(ctypes.byref(c), 0, None, None, None, 0, ctypes.byref(out)) == _lib.TTTJ_ERR_INVALID
     assert b"null" in lib.tttj_last_error()
+    # A misaligned folded-weight buffer is refused before any device is touched.
+    assert lib.tttj_fold_weights(ctypes.byref(c), ctypes.c_void_p(256), ctypes.c_void_p(272),
+                                 1 << 30, None) == _lib.TTTJ_ERR_INVALID
+    assert b"aligned" in lib.tttj_last_error()
+    assert lib.tttj_fold_weights(ctypes.byref(c), ctypes.c_void_p(256), ctypes.c_void_p(512),
+                                 16, None) == _lib.TTTJ_ERR_INVALID
+    assert b"too small" in lib.tttj_last_error()
     bad = _c(2, 16, 64, 1, 128, 0, False)
     assert lib.tttj_validate_config(ctypes.byref(bad)) == _lib.TTTJ_ERR_INVALID
 

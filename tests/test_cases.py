@@ -43,17 +43,23 @@ def test_case_lookup_rejects_other_shapes():
 
 def test_padded_heads_workspace_holds_the_padded_layout():
     """hd 8 runs on 32-column layout heads: the workspace grows by the padded q/k/v and
-    context columns and the padded out_proj weight, and nothing else changes."""
+    context columns, the folded weights by the padded QKV rows and the padded out_proj
+    weight, and nothing else changes."""
     lib = _lib.lib()
     base = tb.TransformerConfig(4, 128, 128, 4, 128, 1, True)   # hd 32, unpadded
     pad = tb.TransformerConfig(4, 128, 128, 16, 128, 1, True)   # hd 8, padded x4
-    ws_base = lib.tttj_workspace_bytes(ctypes.byref(_lib.TttjConfig.from_config(base)))
-    ws_pad = lib.tttj_workspace_bytes(ctypes.byref(_lib.TttjConfig.from_config(pad)))
+    cb, cp = _lib.TttjConfig.from_config(base), _lib.TttjConfig.from_config(pad)
+    ws_base = lib.tttj_workspace_bytes(ctypes.byref(cb))
+    ws_pad = lib.tttj_workspace_bytes(ctypes.byref(cp))
     T, D, Q = 4 * 128, 128, 16 * 32
-    extra = T * 3 * (Q - D) * 2 + T * (Q - D) * 2 + 3 * (Q - D) * (D * 2 + 8) + D * Q * 2
+    extra = T * 3 * (Q - D) * 2 + T * (Q - D) * 2
     # 16 heads instead of 4 also lengthen the attention work list (8 bytes per item).
     extra += 4 * (16 - 4) * 1 * 8
     assert abs((ws_pad - ws_base) - extra) <= 8 * 256  # alignment slack
+    fold_extra = 3 * (Q - D) * (D * 2 + 8) + D * Q * 2
+    f_base = lib.tttj_folded_bytes(ctypes.byref(cb))
+    f_pad = lib.tttj_folded_bytes(ctypes.byref(cp))
+    assert abs((f_pad - f_base) - fold_extra) <= 8 * 256
     # The packed weights are the caller's unpadded layout either way.
     w_base = lib.tttj_weights_bytes(ctypes.byref(_lib.TttjConfig.from_config(base)))
     w_pad = lib.tttj_weights_bytes(ctypes.byref(_lib.TttjConfig.from_config(pad)))

@@ -1,6 +1,7 @@
 """GPU: the reference's 14 benchmark cases (optimized_transformer.py:22-42) through
 make_optimized_transformer, against the fp32 oracle, at the padding ratios of the
-reference's regression harness (benchmarks/regression.py:56-60: 0.0 and 0.25).
+reference's regression harness (benchmarks/regression.py:56-60: 0.0 and 0.25) and
+of its fused-path gate (profiling/validate_fused_gate.py:17-20: 0.75 as well).
 
 Case 14 runs one 100k-token sequence, as the reference's harness does
 (benchmarks/regression.py:86-97), with the oracle's attention chunked over queries
@@ -47,9 +48,11 @@ def _run(n: int, padding: float, batch=None, query_chunk: int = 4096):
     assert opt.device_status() == 0
 
 
-@pytest.mark.parametrize("padding", [0.0, 0.25])
+@pytest.mark.parametrize("padding", [0.0, 0.25, 0.75])
 @pytest.mark.parametrize("n", list(range(1, 14)))
 def test_reference_case(n, padding):
+    """Padding 0.75 is the third ratio of the reference's fused-path gate
+    (profiling/validate_fused_gate.py:17-20)."""
     _run(n, padding)
 
 

@@ -80,6 +80,23 @@ def test_c2_per_rank_shapes_vs_oracle(batch):
     assert opt.device_status() == 0
 
 
+def test_c3_padding_075_vs_oracle():
+    """C3's shape with lengths in [128, 512] (padding ratio 0.75, the third ratio of the
+    reference's gate, profiling/validate_fused_gate.py:17-20)."""
+    B, S, D, H, F, L, causal, dtype, _ = CONFIGS["C3"]
+    cfg = tb.TransformerConfig(B, S, D, H, F, L, causal)
+    model = tb.make_parameter_model(cfg, 0, dtype, DEV)
+    x, mask = tb.generate_inputs(cfg, 31, dtype, (128, 512), DEV)
+    opt = tb.make_optimized_transformer(model)
+    with torch.inference_mode():
+        out = opt(x, mask)
+        ref = forward_fp32(state_dict_fp32(model, DEV), cfg, x.float(), mask)
+    torch.cuda.synchronize()
+    r = gate(ref, out, mask)
+    print("C3 padding 0.75", r)
+    assert r.passed, r
+
+
 def test_c4_long_sequence_vs_oracle():
     cfg, model, x, mask = _case("C4")
     opt = tb.make_optimized_transformer(model)

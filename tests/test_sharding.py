@@ -92,6 +92,16 @@ def _rank_main(rank, world, port, mode, q):
             out, idx = sh.distributed_forward(mod, x, mask)
             full = mod(x, mask)
             q.put((rank, "ok", float((out - full).abs().max()), [len(i) for i in idx]))
+        elif mode == "dst":
+            # Gather to rank 0 only: rank 0 gets the whole batch, the others None.
+            out, idx = sh.distributed_forward(mod, x, mask, dst=0)
+            mine = sh.local_shard(sh.lengths_of(mask, 5, 24), cfg, rank, world)
+            assert mine == idx[rank]
+            if rank == 0:
+                full = mod(x, mask)
+                q.put((rank, "ok", float((out - full).abs().max()), [len(i) for i in idx]))
+            else:
+                q.put((rank, "none" if out is None else "output", 0.0, [len(i) for i in idx]))
         else:
             # rank 1 dies before the gather; rank 0 must get an error, not hang
             if rank == 1:
@@ -141,6 +151,13 @@ def test_distributed_forward_two_ranks_matches_single_process():
         assert status == "ok"
         assert err == 0.0  # sequences are independent: sharding is exact
         assert sum(sizes) == 5
+
+
+def test_distributed_forward_gathers_to_one_rank():
+    res = _run(2, "dst")
+    assert len(res) == 2, res
+    assert res[0][1] == "ok" and res[0][2] == 0.0 and sum(res[0][3]) == 5
+    assert res[1][1] == "none"
 
 
 def test_rank_failure_surfaces_as_error_on_the_survivor():

@@ -6,7 +6,9 @@ start-up, runtimes that pass only pre-placed buffers).  Instead of a caller
 workspace it uses a fixed scratch array inside the library.  These tests call it
 through the C ABI and check that two calls in a row -- different shapes and masks,
 so the second call runs over the first call's leftovers in the shared scratch --
-give the same output as tttj_attention with a caller-provided workspace.
+give the same output as tttj_attention with a caller-provided workspace, and, so that
+a fault shared by both entry points cannot pass, the same output as an fp32 attention
+computed by torch, within the attention tolerance of tests/test_gpu_kernels.py.
 
 This file is named so that pytest collects it last.
 """
@@ -17,6 +19,7 @@ import torch
 
 import tttj_2026_b200 as tb  # noqa: F401  (package registration via conftest)
 from tttj_2026_b200 import _lib, ops
+from test_gpu_kernels import _attention_ref
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
@@ -67,6 +70,7 @@ def test_noalloc_matches_workspace_entry_on_two_calls_in_a_row():
         out = _noalloc(qkv, mask, B, c["S"], c["H"], c["causal"])
         torch.cuda.synchronize()
         _close(out, ref)
+        _close(out, _attention_ref(qkv, c["lengths"], c["H"], c["causal"]))
 
 
 def test_noalloc_repeat_and_mask_none():

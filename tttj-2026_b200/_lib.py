@@ -44,8 +44,10 @@ _SIGNATURES = {
         _c.c_int,
         [_vp, _c.c_int, _c.c_int, _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t)],
     ),
+    "tttj_folded_bytes": (_c.c_size_t, [_vp]),
+    "tttj_fold_weights": (_c.c_int, [_vp, _vp, _vp, _c.c_size_t, _vp]),
     "tttj_workspace_bytes": (_c.c_size_t, [_vp]),
-    "tttj_plan_create": (_c.c_int, [_vp, _c.c_int, _vp, _vp, _c.c_size_t, _c.POINTER(_vp)]),
+    "tttj_plan_create": (_c.c_int, [_vp, _c.c_int, _vp, _vp, _vp, _c.c_size_t, _c.POINTER(_vp)]),
     "tttj_plan_destroy": (_c.c_int, [_vp]),
     "tttj_forward": (_c.c_int, [_vp, _vp, _c.c_int, _vp, _vp, _vp]),
     "tttj_plan_status": (_c.c_int, [_vp, _c.POINTER(_c.c_int)]),
@@ -75,6 +77,7 @@ _SIGNATURES = {
         _c.c_int, [_vp, _vp, _c.c_int, _vp, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_int, _vp]
     ),
     "tttj_selftest_wait_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
+    "tttj_plan_selftest_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
     "tttj_device_sm_count": (_c.c_int, [_c.c_int]),
     "tttj_plan_launch_count": (_c.c_int, [_vp]),
     "tttj_plan_enable_timing": (_c.c_int, [_vp, _c.c_int]),

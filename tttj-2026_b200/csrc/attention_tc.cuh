@@ -40,9 +40,13 @@
 // Every wait is bounded (TTTJ wait limit); on a timeout the role records
 // TTTJ_DEV_TIMEOUT_ATTN in the status word, raises the CTA abort flag and unwinds.
 //
-// Rows of other sequences inside a partial K/V tile are masked by P = 0; they are
-// finite whenever the inputs are finite (the workspace is zero-filled once and only
-// ever holds values computed from the inputs).
+// Sequence isolation: the K/V tile holding a sequence's last keys also holds rows of
+// the next sequence of the packed layout (or rows no forward of this shape wrote
+// since), which may be NaN or Inf.  Their scores are replaced by -inf (P = 0), and
+// before the first P V of such a tile the MMA warp zeroes its V rows past the sequence
+// end in shared memory, since 0 * NaN would still reach the output.  Query rows past
+// the end (the next sequence's) never decide whether a warp rescales O, so a
+// sequence's output does not depend on any other sequence's values.
 #pragma once
 #include "common.cuh"
 #include "params.h"
@@ -318,6 +322,28 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
           mma_commit_warp(bar_s_full + 8 * t);
           issued = true;
         };
+        // V rows of the tile at item key tile j_rel past the sequence end: zeroed in
+        // shared memory (every 16-byte chunk of a row stays in that row under the
+        // swizzle) and made visible to the tensor core before any P V reads them.  Both
+        // MMA warps may do it for the same tile; they write the same zeros.
+        const int seq_len = __shfl_sync(FULL, info[qb].len, 0);
+        auto clean_v = [&](long kv_idx, int j_rel) {
+          const int keep = seq_len - j_rel * ATC_BN;  // rows of this sequence (>= 1)
+          if (keep >= ATC_BN) return;                 // warp-uniform
+          constexpr int ROW_BYTES = SM::BOX_COLS * 2;
+          constexpr int CH = ROW_BYTES / 16;
+          const uint32_t vaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE + SM::KV_TILE;
+          const int n16 = (ATC_BN - keep) * CH;
+#pragma unroll 1
+          for (int x = 0; x < SM::NBOX; ++x)
+            for (int i = lane; i < n16; i += 32) {
+              const uint32_t a = vaddr + (uint32_t)(x * SM::BOX_BYTES + (keep + i / CH) * ROW_BYTES +
+                                                    (i % CH) * 16);
+              asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(a), "r"(0u) : "memory");
+            }
+          fence_proxy_async_smem();
+          __syncwarp();
+        };
         auto issue_pv = [&](long kv_idx, bool accumulate) {
           const uint32_t vaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE + SM::KV_TILE;
           const uint64_t vd = atc_desc_v<HD>(vaddr);
@@ -331,6 +357,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (n > 0) {
           if (!ensure_kv(kvc)) break;
           issue_s(kvc);
+          clean_v(kvc, 0);
         }
         for (int j = 0; j < n_kv && ok; ++j) {
           const long kv_j = kvc + j;
@@ -340,6 +367,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
               if (!wait(bar_s_free + 8 * t, (uint32_t)(sfc++ & 1))) break;
               if (!ensure_kv(kv_j + 1)) break;
               issue_s(kv_j + 1);
+              clean_v(kv_j + 1, j + 1);
             }
             if (!wait(bar_p_full + 8 * t, (uint32_t)(pc++ & 1))) break;
             // The first P V of an item overwrites O: the previous item's O must be read.
@@ -355,6 +383,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
               if (j + 1 < n) {
                 if (!ensure_kv(kv_j + 1)) break;
                 issue_s(kv_j + 1);
+                clean_v(kv_j + 1, j + 1);
               }
             }
             ++pvc;
@@ -455,8 +484,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (j == 0) {
           m_run = m_tile;
         } else {
-          // Lazy rescale: keep the old base unless the max grew by more than 2^8.
-          const bool grow = m_tile > m_run + 8.0f;
+          // Lazy rescale: keep the old base unless the max grew by more than 2^8.  Only
+          // this sequence's query rows vote (rows past its end belong to the next one).
+          const bool grow = qrow < w.len && m_tile > m_run + 8.0f;
           if (__any_sync(0xffffffff, grow)) {
             const float m_new = fmaxf(m_run, m_tile);
             alpha = (m_run == -INFINITY) ? 0.f : ex2_approx(m_run - m_new);

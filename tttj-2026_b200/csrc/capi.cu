@@ -102,9 +102,7 @@ bool weight_offset(const tttj_config& c, int layer, int field, size_t* off, size
 // ---------------------------------------------------------------- workspace layout
 struct WsLayout {
   size_t seq_len, seq_off, packed_src, dst_map, items, item_count, counters, status;
-  size_t resid, x16, qkv, ctx, hid, stats;
-  size_t fold;        // LayerNorm-folded QKV / ffn_in weights, per layer
-  size_t fold_layer;  // bytes per layer in the fold region
+  size_t resid, x16, qkv, ctx, hid, stats, pivot;
   size_t total;
 };
 
@@ -165,11 +163,15 @@ WsLayout ws_layout(const tttj_config& c) {
   w.ctx = o; o += align_up(T * Q * 2);
   w.hid = o; o += align_up(T * F * 2);
   w.stats = o; o += align_up((size_t)2 * T * stats_parts(c) * 8);
-  w.fold_layer = fold_layout(c).total;
-  w.fold = o; o += (size_t)c.num_layers * w.fold_layer;
+  w.pivot = o; o += align_up((size_t)2 * T * 4);
   w.total = o;
   return w;
 }
+
+// The LayerNorm-folded weights (FoldLayout per layer) depend on the configuration's
+// layer shapes only, not on batch or sequence length: one buffer per module, shared
+// by every plan.
+size_t folded_bytes(const tttj_config& c) { return (size_t)c.num_layers * fold_layout(c).total; }
 
 TokenPlan token_plan_at(uint8_t* base, const WsLayout& w) {
   TokenPlan tp;
@@ -428,13 +430,25 @@ struct tttj_plan {
   int device;
   int num_sms;
   const uint8_t* weights;
+  const uint8_t* folded;  // LayerNorm-folded weights (tttj_fold_weights), per layer
+  size_t fold_layer;      // bytes per layer of `folded`
   uint8_t* ws;
   WsLayout lay;
   TokenPlan tp;
   int* status;
+  // Pinned, device-mapped mirror of the status word: the last kernel of every forward
+  // copies a non-zero device status into it, and the next forward reads it without
+  // synchronising.
+  int* status_host = nullptr;
+  // Cross-stream ordering of the plan's workspace: completion of the last forward and
+  // the stream it ran on.  A forward on another stream first waits for it.
+  cudaEvent_t done = nullptr;
+  cudaStream_t last_stream = nullptr;
+  bool has_last = false;
   float* resid;  // fp32 residual stream
-  __half *x16, *qkv, *ctx, *hid;  // x16: fp16 copy of the residual stream (GEMM A operand)
+  __half *x16, *qkv, *ctx, *hid;  // x16: fp16 copy of resid - pivot (GEMM A operand)
   float2* stats;  // [2][T][parts] LayerNorm statistics partials: LN1 (next QKV), LN2 (ffn_in)
+  float* pivot;   // [2][T] per-row pivot of each statistics buffer
   int parts;      // statistics partials per row of LN1 (ffn_out, the gather -> QKV)
   int parts_ln2;  // ... of LN2 (out_proj -> ffn_in)
   std::vector<LayerGemms> layers;
@@ -505,6 +519,22 @@ void destroy_events(tttj_plan* p) {
   p->ev_used = 0;
 }
 
+// Host-side resources of a plan (the device memory is the caller's).  Waits for the
+// plan's last forward first, so that the caller may free or reuse the workspace once
+// the plan is destroyed.
+void plan_release(tttj_plan* p) {
+  if (p->done) {
+    if (p->has_last) cudaEventSynchronize(p->done);
+    cudaEventDestroy(p->done);
+    p->done = nullptr;
+  }
+  destroy_events(p);
+  if (p->status_host) {
+    cudaFreeHost(p->status_host);
+    p->status_host = nullptr;
+  }
+}
+
 // TMA maps and parameters of the resident-stack kernel: the plan's folded QKV / ffn_in
 // weights and (for padded heads) padded out_proj weight in the workspace, the caller's
 // out_proj / ffn_out weights, all as 3-D maps over the layers.
@@ -513,8 +543,8 @@ int build_resident(tttj_plan* p, const FoldLayout& fl) {
   const int D = c.d_model, F = c.ffn_dim, hp = layout_hd(c), Q = (int)qkv_width(c), L = c.num_layers;
   const int gh = resident_gh(c);
   const ResLayout ly = res_layout(D, F, hp, Q, gh);
-  const uint8_t* fold = p->ws + p->lay.fold;
-  const size_t fstride = p->lay.fold_layer, lstride = layer_stride(c);
+  const uint8_t* fold = p->folded;
+  const size_t fstride = p->fold_layer, lstride = layer_stride(c);
   auto W = [&](int field) -> const uint8_t* {
     size_t off = 0, bytes = 0;
     weight_offset(c, 0, field, &off, &bytes);
@@ -563,6 +593,7 @@ int build_resident(tttj_plan* p, const FoldLayout& fl) {
   q.lnf_w = p->lnf_w;
   q.lnf_b = p->lnf_b;
   q.status = p->status;
+  q.status_host = p->status_host;
   q.wait_limit_ns = kWaitLimitNs;
   p->res_ok = true;
   p->res_auto = resident_preferred(c);
@@ -624,16 +655,68 @@ int tttj_gemm_tile(int rows, int n, int k, int epilogue, int num_sms, int* bn, i
   return TTTJ_OK;
 }
 
-int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, void* workspace,
-                     size_t workspace_bytes, tttj_plan** out_plan) {
+size_t tttj_folded_bytes(const tttj_config* cfg) {
+  if (check_config(cfg)) return 0;
+  return folded_bytes(*cfg);
+}
+
+int tttj_fold_weights(const tttj_config* cfg, const void* weights, void* folded,
+                      size_t folded_bytes_given, void* stream) {
   int rc = check_config(cfg);
   if (rc) return rc;
-  if (!weights || !workspace || !out_plan) return fail(TTTJ_ERR_INVALID, "null pointer argument");
+  if (!weights || !folded) return fail(TTTJ_ERR_INVALID, "fold_weights: null pointer argument");
+  if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(folded)) & (kAlign - 1))
+    return fail(TTTJ_ERR_INVALID, "fold_weights: weights and folded must be 256-byte aligned");
+  const size_t need = folded_bytes(*cfg);
+  if (folded_bytes_given < need)
+    return fail(TTTJ_ERR_INVALID, "fold_weights: buffer too small: %zu < %zu", folded_bytes_given,
+                need);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int D = cfg->d_model, F = cfg->ffn_dim, hd = head_dim_of(*cfg), hp = layout_hd(*cfg);
+  const int Q = (int)qkv_width(*cfg);
+  const FoldLayout fl = fold_layout(*cfg);
+  const uint8_t* wb = static_cast<const uint8_t*>(weights);
+  auto W = [&](int layer, int field) -> const uint8_t* {
+    size_t off = 0, bytes = 0;
+    weight_offset(*cfg, layer, field, &off, &bytes);
+    return wb + off;
+  };
+  for (int l = 0; l < cfg->num_layers; ++l) {
+    uint8_t* fb = static_cast<uint8_t*>(folded) + (size_t)l * fl.total;
+    // LN1 into the QKV weights (head-padded layout), LN2 into ffn_in.
+    TTTJ_CUDA(fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_QKV)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_LN1_W)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_LN1_B)), 3 * Q, D, hd, hp,
+                             reinterpret_cast<__half*>(fb + fl.wqkv),
+                             reinterpret_cast<float*>(fb + fl.bqkv),
+                             reinterpret_cast<float*>(fb + fl.cqkv), s));
+    TTTJ_CUDA(fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_FFN_IN)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_LN2_W)),
+                             reinterpret_cast<const float*>(W(l, TTTJ_LN2_B)), F, D, 1, 1,
+                             reinterpret_cast<__half*>(fb + fl.w1),
+                             reinterpret_cast<float*>(fb + fl.b1),
+                             reinterpret_cast<float*>(fb + fl.c1), s));
+    if (heads_padded(*cfg))
+      TTTJ_CUDA(pad_head_cols_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_OUT)), D, D, hd,
+                                     hp, reinterpret_cast<__half*>(fb + fl.wo), s));
+  }
+  return TTTJ_OK;
+}
+
+int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                     void* workspace, size_t workspace_bytes, tttj_plan** out_plan) {
+  int rc = check_config(cfg);
+  if (rc) return rc;
+  if (!weights || !folded || !workspace || !out_plan)
+    return fail(TTTJ_ERR_INVALID, "null pointer argument");
   const WsLayout lay = ws_layout(*cfg);
   if (workspace_bytes < lay.total)
     return fail(TTTJ_ERR_INVALID, "workspace too small: %zu < %zu", workspace_bytes, lay.total);
-  if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(workspace)) & (kAlign - 1))
-    return fail(TTTJ_ERR_INVALID, "weights and workspace must be 256-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(workspace) |
+       reinterpret_cast<uintptr_t>(folded)) & (kAlign - 1))
+    return fail(TTTJ_ERR_INVALID, "weights, folded weights and workspace must be 256-byte aligned");
   DeviceGuard guard(device);
   int cc_major = 0, cc_minor = 0;
   TTTJ_CUDA(cudaDeviceGetAttribute(&cc_major, cudaDevAttrComputeCapabilityMajor, device));
@@ -643,10 +726,17 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
                 device, cc_major, cc_minor);
 
   tttj_plan* p = new tttj_plan();
+  auto bail = [&](int code) {
+    plan_release(p);
+    delete p;
+    return code;
+  };
   p->cfg = *cfg;
   p->device = device;
   p->num_sms = sm_count(device);
   p->weights = static_cast<const uint8_t*>(weights);
+  p->folded = static_cast<const uint8_t*>(folded);
+  p->fold_layer = fold_layout(*cfg).total;
   p->ws = static_cast<uint8_t*>(workspace);
   p->lay = lay;
   p->tp = token_plan_at(p->ws, lay);
@@ -654,9 +744,19 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   p->resid = reinterpret_cast<float*>(p->ws + lay.resid);
   p->x16 = reinterpret_cast<__half*>(p->ws + lay.x16);
   p->stats = reinterpret_cast<float2*>(p->ws + lay.stats);
+  p->pivot = reinterpret_cast<float*>(p->ws + lay.pivot);
   p->qkv = reinterpret_cast<__half*>(p->ws + lay.qkv);
   p->ctx = reinterpret_cast<__half*>(p->ws + lay.ctx);
   p->hid = reinterpret_cast<__half*>(p->ws + lay.hid);
+  {
+    void* h = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, sizeof(int), cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaHostAlloc(status mirror)"));
+    p->status_host = static_cast<int*>(h);
+    *reinterpret_cast<volatile int*>(p->status_host) = 0;
+    e = cudaEventCreateWithFlags(&p->done, cudaEventDisableTiming);
+    if (e != cudaSuccess) return bail(cuda_fail(e, "cudaEventCreate(plan)"));
+  }
 
   const int B = cfg->batch_size, S = cfg->seq_len, D = cfg->d_model, F = cfg->ffn_dim;
   const int T = B * S;
@@ -675,39 +775,28 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
   };
   p->layers.resize(cfg->num_layers);
   const FoldLayout fl = fold_layout(*cfg);
+  // Two statistics buffers with their pivots, reused by every layer: ffn_out(l-1) /
+  // the gather write LN1 for qkv(l); out_proj(l) writes LN2 for ffn_in(l).  Each
+  // residual GEMM takes its pivot from the other buffer (the statistics of the
+  // residual it adds to).
+  float2* st_ln1 = p->stats;
+  float2* st_ln2 = p->stats + (size_t)T * stats_parts(*cfg);
+  float* pv_ln1 = p->pivot;
+  float* pv_ln2 = p->pivot + T;
   for (int l = 0; l < cfg->num_layers; ++l) {
     LayerGemms& L = p->layers[l];
     L.ln1_w = reinterpret_cast<const float*>(W(l, TTTJ_LN1_W));
     L.ln1_b = reinterpret_cast<const float*>(W(l, TTTJ_LN1_B));
     L.ln2_w = reinterpret_cast<const float*>(W(l, TTTJ_LN2_W));
     L.ln2_b = reinterpret_cast<const float*>(W(l, TTTJ_LN2_B));
-    // LayerNorm folds: LN1 into the QKV weights, LN2 into ffn_in (one-time kernels).
-    uint8_t* fb = p->ws + lay.fold + (size_t)l * lay.fold_layer;
-    __half* wqkv_f = reinterpret_cast<__half*>(fb + fl.wqkv);
-    __half* w1_f = reinterpret_cast<__half*>(fb + fl.w1);
-    float* bqkv_f = reinterpret_cast<float*>(fb + fl.bqkv);
-    float* cqkv = reinterpret_cast<float*>(fb + fl.cqkv);
-    float* b1_f = reinterpret_cast<float*>(fb + fl.b1);
-    float* c1 = reinterpret_cast<float*>(fb + fl.c1);
-    __half* wo_pad = heads_padded(*cfg) ? reinterpret_cast<__half*>(fb + fl.wo) : nullptr;
-    cudaError_t fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_QKV)),
-                                    reinterpret_cast<const float*>(W(l, TTTJ_B_QKV)), L.ln1_w,
-                                    L.ln1_b, 3 * Q, D, hd, hp, wqkv_f, bqkv_f, cqkv, 0);
-    if (fe == cudaSuccess)
-      fe = fold_ln_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_FFN_IN)),
-                          reinterpret_cast<const float*>(W(l, TTTJ_B_FFN_IN)), L.ln2_w, L.ln2_b, F,
-                          D, 1, 1, w1_f, b1_f, c1, 0);
-    if (fe == cudaSuccess && wo_pad)
-      fe = pad_head_cols_launch(reinterpret_cast<const __half*>(W(l, TTTJ_W_OUT)), D, D, hd, hp,
-                                wo_pad, 0);
-    if (fe != cudaSuccess) {
-      delete p;
-      return cuda_fail(fe, "fold_ln_launch");
-    }
-    // Two statistics buffers, reused by every layer: ffn_out(l-1) / the gather write
-    // LN1 for qkv(l); out_proj(l) writes LN2 for ffn_in(l).
-    float2* st_ln1 = p->stats;
-    float2* st_ln2 = p->stats + (size_t)T * stats_parts(*cfg);
+    const uint8_t* fb = p->folded + (size_t)l * p->fold_layer;
+    const __half* wqkv_f = reinterpret_cast<const __half*>(fb + fl.wqkv);
+    const __half* w1_f = reinterpret_cast<const __half*>(fb + fl.w1);
+    const float* bqkv_f = reinterpret_cast<const float*>(fb + fl.bqkv);
+    const float* cqkv = reinterpret_cast<const float*>(fb + fl.cqkv);
+    const float* b1_f = reinterpret_cast<const float*>(fb + fl.b1);
+    const float* c1 = reinterpret_cast<const float*>(fb + fl.c1);
+    const __half* wo_pad = heads_padded(*cfg) ? reinterpret_cast<const __half*>(fb + fl.wo) : nullptr;
     if (l == 0) {
       // Tile widths of the residual GEMMs (the choice build_gemm makes below), which
       // fix the partial counts; every layer has the same shapes.
@@ -731,6 +820,10 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
     L.out.p.ld16 = D;
     L.out.p.stats_out = st_ln2;
     L.out.p.stats_parts = p->parts_ln2;
+    L.out.p.pivot_out = pv_ln2;
+    L.out.p.stats_prev = st_ln1;
+    L.out.p.pivot_prev = pv_ln1;
+    L.out.p.stats_prev_parts = p->parts;
     if (!rc)
       rc = build_gemm(&L.ffn_in, p->x16, D, w1_f, D, b1_f, p->hid, F, nullptr, 0, T, rows_dev, F,
                       D, EPI_LN_FOLD_GELU, p->status, p->num_sms);
@@ -752,34 +845,22 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, vo
       L.ffn_out.p.ld16 = D;
       L.ffn_out.p.stats_out = st_ln1;  // LN1 of layer l+1
       L.ffn_out.p.stats_parts = p->parts;
+      L.ffn_out.p.pivot_out = pv_ln1;
+      L.ffn_out.p.stats_prev = st_ln2;
+      L.ffn_out.p.pivot_prev = pv_ln2;
+      L.ffn_out.p.stats_prev_parts = p->parts_ln2;
     }
-    if (rc) {
-      delete p;
-      return rc;
-    }
-  }
-  {
-    cudaError_t fe = cudaStreamSynchronize(0);  // folded weights ready before any forward
-    if (fe != cudaSuccess) {
-      delete p;
-      return cuda_fail(fe, "cudaStreamSynchronize(fold)");
-    }
+    if (rc) return bail(rc);
   }
   p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
   p->lnf_b = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_B));
 
   rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S,
                        cfg->num_heads, hd, hp, p->tp, p->status, p->num_sms);
-  if (rc) {
-    delete p;
-    return rc;
-  }
+  if (rc) return bail(rc);
   if (resident_fits(*cfg)) {
     rc = build_resident(p, fl);
-    if (rc) {
-      delete p;
-      return rc;
-    }
+    if (rc) return bail(rc);
   }
   *out_plan = p;
   return TTTJ_OK;
@@ -802,7 +883,7 @@ int tttj_plan_path(tttj_plan* p) { return p && use_resident(p) ? 1 : 0; }
 int tttj_plan_destroy(tttj_plan* plan) {
   if (plan) {
     DeviceGuard guard(plan->device);
-    destroy_events(plan);
+    plan_release(plan);
   }
   delete plan;
   return TTTJ_OK;
@@ -912,6 +993,36 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   const int hp = layout_hd(c);
   const int* rows_dev = p->tp.seq_off + B;
 
+  // A bounded device wait of an earlier forward gave up (its last kernel copied the
+  // status word into the pinned mirror): report it now, without synchronising, clear
+  // it, and launch nothing.  The next call runs normally.
+  {
+    volatile int* mirror = p->status_host;
+    const int v = mirror ? *mirror : 0;
+    if (v != 0) {
+      *mirror = 0;
+      TTTJ_CUDA(cudaMemsetAsync(p->status, 0, sizeof(int), s));
+      p->plan_static = false;
+      return fail(TTTJ_ERR_DEVICE_TIMEOUT,
+                  "a device wait of an earlier forward of this plan timed out (status 0x%x); "
+                  "that forward's output is invalid",
+                  v);
+    }
+  }
+  // The workspace belongs to the plan: a forward on another stream than the previous
+  // one first waits for the previous one.
+  if (p->has_last && s != p->last_stream) TTTJ_CUDA(cudaStreamWaitEvent(s, p->done, 0));
+  struct DoneRecord {  // record completion on every return path after launches began
+    tttj_plan* p;
+    cudaStream_t s;
+    ~DoneRecord() {
+      if (cudaEventRecord(p->done, s) == cudaSuccess) {
+        p->last_stream = s;
+        p->has_last = true;
+      }
+    }
+  } done_record{p, s};
+
   // Per-class timing: an event pair around every launch when enabled.
   if (p->timing) {
     int rc = collect_timing(p);
@@ -954,7 +1065,7 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   p->plan_static = valid_mask == nullptr;
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
-                              p->stats, p->parts, p->tp.counters, s));
+                              p->stats, p->pivot, p->parts, p->tp.counters, s));
   // Capture buffers (floats) of tttj_forward_debug, filled at its layer.
   const size_t SD = (size_t)S * D, HSS = (size_t)c.num_heads * S * S;
   float* dg = dbg ? dbg->buf : nullptr;
@@ -999,7 +1110,7 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   }
   TTTJ_TIMED(TTTJ_KCLASS_FINAL_LN,
              ln_final_launch(p->resid, p->tp.dst_map, T, D, p->lnf_w, p->lnf_b, kLnEps, out,
-                             x_dtype, s));
+                             x_dtype, p->status, p->status_host, s));
 #undef TTTJ_TIMED
   p->ev_used = slot;
   return TTTJ_OK;
@@ -1013,6 +1124,8 @@ int tttj_plan_status(tttj_plan* p, int* device_status) {
   TTTJ_CUDA(cudaDeviceSynchronize());
   int v = 0;
   TTTJ_CUDA(cudaMemcpy(&v, p->status, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v == 0 && p->status_host) v = *reinterpret_cast<volatile int*>(p->status_host);
+  if (p->status_host) *reinterpret_cast<volatile int*>(p->status_host) = 0;
   if (v != 0) TTTJ_CUDA(cudaMemset(p->status, 0, sizeof(int)));
   if (v != 0) p->plan_static = false;  // a kernel gave up: rebuild the plan on the next forward
   *device_status = v;
@@ -1089,7 +1202,20 @@ int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* vali
 
 int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream) {
   if (!status_dev) return fail(TTTJ_ERR_INVALID, "selftest: null status");
-  TTTJ_CUDA(selftest_wait_launch(status_dev, limit_ns, static_cast<cudaStream_t>(stream)));
+  TTTJ_CUDA(selftest_wait_launch(status_dev, nullptr, limit_ns, static_cast<cudaStream_t>(stream)));
+  return TTTJ_OK;
+}
+
+int tttj_plan_selftest_timeout(tttj_plan* p, uint64_t limit_ns, void* stream) {
+  if (!p) return fail(TTTJ_ERR_INVALID, "selftest: null plan");
+  if (limit_ns > 1000000000ull) return fail(TTTJ_ERR_INVALID, "selftest: limit above 1 s");
+  DeviceGuard guard(p->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (p->has_last && s != p->last_stream) TTTJ_CUDA(cudaStreamWaitEvent(s, p->done, 0));
+  TTTJ_CUDA(selftest_wait_launch(p->status, p->status_host, limit_ns, s));
+  TTTJ_CUDA(cudaEventRecord(p->done, s));
+  p->last_stream = s;
+  p->has_last = true;
   return TTTJ_OK;
 }
 
@@ -1109,11 +1235,13 @@ int tttj_selftest_wait_timeout(int* status_dev, uint64_t limit_ns, void* stream)
 // process exits.
 //
 // Host code must not pass g_attn_noalloc_scratch itself to a kernel: on the host the
-// name is only a stand-in for the device symbol.  The device address is looked up
-// once per device with cudaGetSymbolAddress, with that device current, on the first
-// call made on the device.  Because that first call does this set-up (and may make
-// the CUDA runtime load the library's device code), it should come before any stream
-// capture.
+// name is only a stand-in for the device symbol.  The device address is looked up with
+// cudaGetSymbolAddress, with the device current, on the first call in each CUDA
+// context (the first call on a device, and again after a device reset or in a new
+// context: the cache is keyed by the context's process-unique id, so a stale address
+// is never reused).  That first call may also make the CUDA runtime load the
+// library's device code (lazy module loading), which allocates: it should come before
+// any stream capture and outside any allocator or memory-pool callback.
 //
 // All calls on a device share the one array and it keeps whatever the last call
 // wrote.  Nothing in it needs clearing: each call's plan kernel rewrites every value
@@ -1127,21 +1255,55 @@ static __device__ __align__(256) unsigned char g_attn_noalloc_scratch[kNoallocSc
 
 constexpr int kNoallocMaxDevices = 64;
 std::mutex g_noalloc_mu;
-void* g_noalloc_addr[kNoallocMaxDevices] = {};
+struct NoallocSlot {
+  unsigned long long ctx_id = 0;  // 0: empty
+  void* addr = nullptr;
+};
+NoallocSlot g_noalloc_slot[kNoallocMaxDevices];
+
+// Process-unique id of the calling thread's current CUDA context (driver entry points
+// cuCtxGetCurrent / cuCtxGetId), or 0 when it cannot be determined.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr ||
+      get_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
 
 // Device address of the scratch array on `device` (the current device).
 int noalloc_scratch_address(int device, void** out) {
   if (device < 0 || device >= kNoallocMaxDevices)
     return fail(TTTJ_ERR_INVALID, "attention_noalloc: device %d out of range", device);
+  const unsigned long long ctx_id = current_context_id();
   std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[device] == nullptr) {
+  NoallocSlot& slot = g_noalloc_slot[device];
+  if (ctx_id == 0 || slot.ctx_id != ctx_id || slot.addr == nullptr) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(attention scratch)");
     if (p == nullptr) return fail(TTTJ_ERR_CUDA, "attention_noalloc: null scratch address");
-    g_noalloc_addr[device] = p;
+    slot.ctx_id = ctx_id;  // 0 (id unknown): looked up again on every call
+    slot.addr = p;
   }
-  *out = g_noalloc_addr[device];
+  *out = slot.addr;
   return TTTJ_OK;
 }
 

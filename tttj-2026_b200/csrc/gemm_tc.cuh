@@ -337,10 +337,22 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           ssum += v2.x;
           ssq += v2.y;
         }
+        // Partials are of x - pivot, so ln_mean is small against the spread of the row
+        // and the variance does not cancel.
         const float inv_k = 1.0f / (float)p.k;
         ln_mean = ssum * inv_k;
         const float var = fmaxf(ssq * inv_k - ln_mean * ln_mean, 0.f);
         ln_rstd = rsqrtf(var + p.ln_eps);
+      }
+      // EPI_RESIDUAL_F32_STATS: the pivot of this row's new statistics is the mean of
+      // the residual before the add (the previous LayerNorm's statistics, summed in
+      // the same fixed order by every CTA, so all column tiles of a row agree on it).
+      float shift = 0.f;
+      if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
+        float ssum = 0.f;
+        const float2* st = p.stats_prev + (size_t)row * p.stats_prev_parts;
+        for (int j = 0; j < p.stats_prev_parts; ++j) ssum += st[j].x;
+        shift = p.pivot_prev[row] + ssum * (1.0f / (float)p.n);
       }
       const int seg0 = n_blk * BN + col_half * (BN / 2);
       if (seg0 < p.n && (staged_res || row_ok)) load_res(staged_res, row0, row, seg0);
@@ -444,8 +456,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              s4[i & 3] += v[i];
-              q4[i & 3] = fmaf(v[i], v[i], q4[i & 3]);
+              const float d = v[i] - shift;
+              s4[i & 3] += d;
+              q4[i & 3] = fmaf(d, d, q4[i & 3]);
             }
             row_sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
             row_sq += (q4[0] + q4[1]) + (q4[2] + q4[3]);
@@ -457,11 +470,13 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             bulk_commit();
           }
           if (EPI == EPI_RESIDUAL_F32_STATS) {
-            // fp16 copy of the new residual (the next LayerNorm-folded GEMM's A operand),
-            // read back from the staging block four whole rows per instruction.
+            // fp16 copy of the new residual minus its row's pivot (the next
+            // LayerNorm-folded GEMM's A operand), read back from the staging block four
+            // whole rows per instruction; row rr's pivot comes from lane rr.
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               const int rr = 4 * q + (lane >> 3), j = lane & 7;
+              const float sh = __shfl_sync(0xffffffffu, shift, rr);
               const uint32_t a = stage_out + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
               float4 x;
               asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
@@ -469,7 +484,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                            : "r"(a)
                            : "memory");
               *reinterpret_cast<uint2*>(p.out16 + (size_t)(row0 + rr) * p.ld16 + col0 + 4 * j) =
-                  make_uint2(pack_half2(x.x, x.y), pack_half2(x.z, x.w));
+                  make_uint2(pack_half2(x.x - sh, x.y - sh), pack_half2(x.z - sh, x.w - sh));
             }
           }
           continue;
@@ -485,21 +500,23 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           if (more) load_res(false, row0, row, col0 + 32);
         }
         if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
+          float d[32];
           float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
-            s4[i & 3] += v[i];
-            q4[i & 3] = fmaf(v[i], v[i], q4[i & 3]);
+            d[i] = v[i] - shift;
+            s4[i & 3] += d[i];
+            q4[i & 3] = fmaf(d[i], d[i], q4[i & 3]);
           }
           row_sum += (s4[0] + s4[1]) + (s4[2] + s4[3]);
           row_sq += (q4[0] + q4[1]) + (q4[2] + q4[3]);
           uint4* d16 = reinterpret_cast<uint4*>(p.out16 + (size_t)row * p.ld16 + col0);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            d16[q] = make_uint4(pack_half2(v[8 * q + 0], v[8 * q + 1]),
-                                pack_half2(v[8 * q + 2], v[8 * q + 3]),
-                                pack_half2(v[8 * q + 4], v[8 * q + 5]),
-                                pack_half2(v[8 * q + 6], v[8 * q + 7]));
+            d16[q] = make_uint4(pack_half2(d[8 * q + 0], d[8 * q + 1]),
+                                pack_half2(d[8 * q + 2], d[8 * q + 3]),
+                                pack_half2(d[8 * q + 4], d[8 * q + 5]),
+                                pack_half2(d[8 * q + 6], d[8 * q + 7]));
         }
         if (full_tile) {
           // The previous TMA store from this warp's staging block must have read it.
@@ -568,9 +585,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
-      if (EPI == EPI_RESIDUAL_F32_STATS && row_ok)
+      if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
         p.stats_out[(size_t)row * p.stats_parts + 2 * n_blk + col_half] =
             make_float2(row_sum, row_sq);
+        if (n_blk == 0 && col_half == 0) p.pivot_out[row] = shift;
+      }
     }
     // Stores issued by this warp must complete before the CTA exits.
     if (lane == 0) bulk_wait_all();

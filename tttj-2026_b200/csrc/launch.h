@@ -86,7 +86,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
                                int kv_block, const TokenPlan& plan, cudaStream_t stream);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
-                             int n_parts, int* counters, cudaStream_t stream);
+                             float* pivot, int n_parts, int* counters, cudaStream_t stream);
 // rows_out output rows; with hd < hp the input's rows are heads of hd rows placed at
 // the start of output groups of hp rows, the rest zero (hd == hp: one row each).
 cudaError_t fold_ln_launch(const __half* w, const float* b, const float* gamma, const float* beta,
@@ -102,7 +102,8 @@ cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, in
                            cudaStream_t stream);
 cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
                             const float* gamma, const float* beta, float eps, void* out,
-                            int out_dtype, cudaStream_t stream);
+                            int out_dtype, const int* status, int* status_host,
+                            cudaStream_t stream);
 // Per-stage capture kernels (debug.cu).
 cudaError_t debug_gather_launch(const void* src, int src_f16, int ld, int col_base, int cols, int hd,
                                 int hp, const int* dst_map, int b, int S, float* dst, cudaStream_t s);
@@ -113,6 +114,7 @@ cudaError_t debug_scores_launch(const float* q, const float* k, const int* dst_m
                                 cudaStream_t s);
 cudaError_t debug_diff_launch(const float* a, const float* b, long n, float* out, cudaStream_t s);
 
-cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream);
+cudaError_t selftest_wait_launch(int* status, int* status_host, unsigned long long limit_ns,
+                                 cudaStream_t stream);
 
 }  // namespace tttj

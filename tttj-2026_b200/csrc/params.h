@@ -30,12 +30,17 @@ enum GemmEpilogue : int {
   EPI_BIAS_GELU = 1,      // out = fp16(gelu_erf(acc + bias))
   EPI_BIAS_RESIDUAL = 2,  // out = fp16(residual + acc + bias), out may alias residual
   EPI_BIAS_RESIDUAL_F32 = 3,  // fp32 out = fp32 residual + acc + bias (the residual stream)
-  // EPI_BIAS_RESIDUAL_F32 that also writes out16 = fp16(out) and adds each row's
-  // (sum, sum of squares) of out into stats_out[row] (the next LayerNorm's statistics).
+  // EPI_BIAS_RESIDUAL_F32 that also prepares the next LayerNorm, relative to a per-row
+  // pivot c = the row mean of the residual before this add (from stats_prev /
+  // pivot_prev): out16 = fp16(out - c), stats_out[row] = (sum, sum of squares) of
+  // out - c over this tile's columns, pivot_out[row] = c.  Shifting by a value close to
+  // the row mean keeps the variance and the fp16 copy exact for rows whose mean is
+  // large against their spread (no sum-of-squares cancellation).
   EPI_RESIDUAL_F32_STATS = 4,
-  // LayerNorm folded into the GEMM: A = fp16 x, W = W * gamma (per K column), and
-  // out = fp16(rstd * (acc - mean * colsum[n]) + bias[n]) with mean/rstd of each row
-  // from stats_in[row] = (sum, sum of squares) over K, bias = b + W beta.
+  // LayerNorm folded into the GEMM: A = fp16(x - c), W = W * gamma (per K column), and
+  // out = fp16(rstd * (acc - m * colsum[n]) + bias[n]) with m = mean(x - c) and rstd
+  // of each row from stats_in[row] = (sum, sum of squares) of x - c over K,
+  // bias = b + W beta.  (x - c - m = x - mean(x), whatever the pivot c.)
   EPI_LN_FOLD = 5,
   EPI_LN_FOLD_GELU = 6,  // the same followed by exact erf-GELU
 };
@@ -53,9 +58,13 @@ struct GemmParams {
   int* status;          // device status word (nullable)
   unsigned long long wait_limit_ns;
   // EPI_RESIDUAL_F32_STATS
-  __half* out16;        // [rows, ld16] fp16 copy of out
+  __half* out16;        // [rows, ld16] fp16 copy of out - pivot
   int ld16;
-  float2* stats_out;    // [rows][stats_parts] (sum, sum of squares) partials
+  float2* stats_out;    // [rows][stats_parts] (sum, sum of squares) partials of out - pivot
+  float* pivot_out;     // [rows] pivot of stats_out / out16
+  const float2* stats_prev;  // [rows][stats_prev_parts] partials of the residual before the add
+  const float* pivot_prev;   // [rows] their pivot
+  int stats_prev_parts;
   // EPI_LN_FOLD*
   const float2* stats_in;  // [rows][stats_parts] partials of the LayerNorm input rows
   int stats_parts;
@@ -133,6 +142,7 @@ struct ResParams {
   const float* lnf_w;     // [D]
   const float* lnf_b;     // [D]
   int* status;
+  int* status_host;       // pinned host mirror of the status word (nullable)
   unsigned long long wait_limit_ns;
 };
 

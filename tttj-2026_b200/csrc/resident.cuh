@@ -145,6 +145,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
   float* rowmax = reinterpret_cast<float*>(misc + 2560);    // [2][128] softmax partial max
   float* rowsum = reinterpret_cast<float*>(misc + 3584);    // [2][128] softmax partial sum
   int* pos = reinterpret_cast<int*>(misc + 4608);           // [128] token of each row
+  float* rowpiv = reinterpret_cast<float*>(misc + 5120);    // [2][128] layer-0 row sums
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -494,9 +495,12 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     const bool row_valid = r < len;
     const bool warp_has_pad = quad * 32 + 31 >= len;  // warp-uniform
 
-    // Residual <- x (fp32), padded rows zero.
+    // Residual <- x (fp32), padded rows zero.  The row's exact mean is layer 0's
+    // LayerNorm pivot (both halves' sums meet in shared memory).
+    float pivot = 0.f;
     if (ok) {
       const int src = row_valid ? pos[r] : 0;
+      float xsum = 0.f;
       for (int c = half; c < nchunk; c += 2) {
         float v[32];
         if (row_valid) {
@@ -524,16 +528,25 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 32; ++e) v[e] = 0.f;
         }
+#pragma unroll
+        for (int e = 0; e < 32; ++e) xsum += v[e];
         res_tmem_st_f32(tr + (uint32_t)(c * 32), v);
       }
       tmem_wait_st();
+      rowpiv[half * RES_ROWS + r] = xsum;
+      if (wsync()) pivot = (rowpiv[r] + rowpiv[RES_ROWS + r]) * invD;
     }
 
     // LayerNorm statistics pass over the residual: adds a pending bias (the previous
     // residual GEMM's), keeps padded rows at zero (masked_fill after every block,
-    // :143-144), writes the fp16 copy into xa when asked, and returns mean / rstd of
-    // the row (both halves' partial sums exchanged through shared memory).
-    auto ln_pass = [&](const float* pbias, bool write_xa, float& mean, float& rstd) -> bool {
+    // :143-144), and works relative to the row's pivot c (a value close to the row
+    // mean, the same in both halves' threads): the (sum, sum of squares) of x - c meet
+    // in shared memory, `mean` returns mean(x - c) (small, so the variance does not
+    // cancel for rows whose mean is large against their spread) and rstd, and the fp16
+    // copy written into xa when asked holds x - c -- the folded epilogues subtract
+    // `mean` times the column sums, as in the layer-by-layer path.
+    auto ln_pass = [&](const float* pbias, bool write_xa, float c0, float& mean,
+                       float& rstd) -> bool {
       float s = 0.f, q = 0.f;
       const bool store_back = pbias != nullptr || warp_has_pad;
       for (int c = half; c < nchunk; c += 2) {
@@ -550,12 +563,15 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             v[4 * k + e] = row_valid ? t4[e] : 0.f;
-            s += v[4 * k + e];
-            q = fmaf(v[4 * k + e], v[4 * k + e], q);
+            const float d = v[4 * k + e] - c0;
+            s += d;
+            q = fmaf(d, d, q);
           }
         }
         if (store_back) res_tmem_st_f32(tr + (uint32_t)(c * 32), v);
         if (write_xa) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) v[e] -= c0;
 #pragma unroll
           for (int j = 0; j < 4; ++j) res_store_sw128(sXA, r, c * 32 + 8 * j, res_pack8(v + 8 * j));
         }
@@ -583,7 +599,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       const float* bq = V + ly.v_bq;
       const float* cq = V + ly.v_cq;
       // LN1 statistics (the previous block's ffn_out bias is still pending in TMEM).
-      if (!ln_pass(l > 0 ? layer_vec(l - 1) + ly.v_b2 : nullptr, true, mean, rstd)) break;
+      if (!ln_pass(l > 0 ? layer_vec(l - 1) + ly.v_b2 : nullptr, true, pivot, mean, rstd)) break;
+      pivot += mean;  // this row's mean: the next pass's pivot
       // Layer l - 1's vectors are no longer needed: the producer may reuse the buffer.
       if (l > 0) mbar_arrive(bar_vempty + 8 * ((l - 1) & 1));
       if (!step_sync()) break;  // -> QKV(0) done
@@ -787,7 +804,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
       }
       if (!ok) break;
       // LN2 statistics (out_proj bias pending), fp16 copy for ffn_in.
-      if (!ln_pass(V + ly.v_bo, true, mean, rstd)) break;
+      if (!ln_pass(V + ly.v_bo, true, pivot, mean, rstd)) break;
+      pivot += mean;
       if (!step_sync()) break;  // -> ffn_in(0) done
       const float* b1 = V + ly.v_b1;
       const float* c1 = V + ly.v_c1;
@@ -825,7 +843,7 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     }
 
     // Final LayerNorm of the valid rows into out; masked positions are written as zeros.
-    if (ok && ln_pass(layer_vec(p.L - 1) + ly.v_b2, false, mean, rstd)) {
+    if (ok && ln_pass(layer_vec(p.L - 1) + ly.v_b2, false, pivot, mean, rstd)) {
       // tcgen05.ld is warp-wide: every lane loads, only valid rows store.
       const int dst = row_valid ? pos[r] : 0;
       for (int c = half; c < nchunk; c += 2) {
@@ -837,7 +855,8 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int col = c * 32 + e;
-          v[e] = fmaf((__uint_as_float(u[e]) - mean) * rstd, __ldg(p.lnf_w + col), __ldg(p.lnf_b + col));
+          v[e] = fmaf(((__uint_as_float(u[e]) - pivot) - mean) * rstd, __ldg(p.lnf_w + col),
+                      __ldg(p.lnf_b + col));
         }
         if (p.x_f32) {
           float4* o = reinterpret_cast<float4*>(static_cast<float*>(p.out) + ((size_t)b * p.S + dst) * D + c * 32);
@@ -863,6 +882,9 @@ __global__ void __launch_bounds__(RES_THREADS, 1)
     if (!ok) {
       *abort_flag = 1;
       report_status(p.status, TTTJ_DEV_TIMEOUT_RESIDENT);
+      // This kernel is the whole forward: copy the code to the host mirror as well.
+      if (p.status_host != nullptr)
+        *reinterpret_cast<volatile int*>(p.status_host) = TTTJ_DEV_TIMEOUT_RESIDENT;
     }
   }
 

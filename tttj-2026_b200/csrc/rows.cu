@@ -36,7 +36,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
 
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
-                             int n_parts, int* counters, cudaStream_t stream) {
+                             float* pivot, int n_parts, int* counters, cudaStream_t stream) {
   const int grid = (rows_max + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
@@ -44,12 +44,14 @@ cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, 
     TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, __half>, dim3(grid),
                                                  dim3(32 * ROWS_PER_CTA), 0, stream,
                                                  static_cast<const __half*>(x), packed_src,
-                                                 rows_dev, D, resid, x16, stats, n_parts, counters)));
+                                                 rows_dev, D, resid, x16, stats, pivot, n_parts,
+                                                 counters)));
   } else {
     TTTJ_VPL_DISPATCH(ln_vpl(D), (e = launch_pdl(ln_gather_kernel<V, float>, dim3(grid),
                                                  dim3(32 * ROWS_PER_CTA), 0, stream,
                                                  static_cast<const float*>(x), packed_src,
-                                                 rows_dev, D, resid, x16, stats, n_parts, counters)));
+                                                 rows_dev, D, resid, x16, stats, pivot, n_parts,
+                                                 counters)));
   }
   return e;
 }
@@ -93,7 +95,8 @@ cudaError_t ln_rows_launch(const void* in, int in_dtype, const int* rows_dev, in
 
 cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, int D,
                             const float* gamma, const float* beta, float eps, void* out,
-                            int out_dtype, cudaStream_t stream) {
+                            int out_dtype, const int* status, int* status_host,
+                            cudaStream_t stream) {
   const int grid = (tokens + ROWS_PER_CTA - 1) / ROWS_PER_CTA;
   if (grid == 0) return cudaSuccess;
   cudaError_t e = cudaSuccess;
@@ -101,18 +104,19 @@ cudaError_t ln_final_launch(const float* resid, const int* dst_map, int tokens, 
     TTTJ_VPL_DISPATCH(ln_vpl(D),
                       (e = launch_pdl(ln_final_scatter_kernel<V, __half>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0,
                                      stream, resid, dst_map, tokens, D, gamma, beta, eps,
-                                     static_cast<__half*>(out))));
+                                     static_cast<__half*>(out), status, status_host)));
   } else {
     TTTJ_VPL_DISPATCH(ln_vpl(D),
                       (e = launch_pdl(ln_final_scatter_kernel<V, float>, dim3(grid), dim3(32 * ROWS_PER_CTA), 0,
                                      stream, resid, dst_map, tokens, D, gamma, beta, eps,
-                                     static_cast<float*>(out))));
+                                     static_cast<float*>(out), status, status_host)));
   }
   return e;
 }
 
-cudaError_t selftest_wait_launch(int* status, unsigned long long limit_ns, cudaStream_t stream) {
-  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(status, limit_ns);
+cudaError_t selftest_wait_launch(int* status, int* status_host, unsigned long long limit_ns,
+                                 cudaStream_t stream) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, stream>>>(status, status_host, limit_ns);
   return cudaGetLastError();
 }
 

@@ -199,19 +199,21 @@ __device__ __forceinline__ void ln_normalise(float (&x)[VPL][8], int D, const fl
   }
 }
 
-// Layer-0 entry: gather the caller's rows into the packed fp32 residual stream, write
-// its fp16 copy (A operand of the LayerNorm-folded QKV GEMM) and the row's
-// (sum, sum of squares) as partial 0 of the row's n_parts statistics partials
-// (the others zero).  Block 0 also zeroes the forward's attention work counters, so a
-// forward that reuses the token plan (no plan kernel) starts from zero as well, even
-// after an earlier launch gave up part-way.  This runs after griddep_wait, i.e. after
-// every kernel of the previous forward has completed.
+// Layer-0 entry: gather the caller's rows into the packed fp32 residual stream and
+// prepare layer 0's LN1 the way the residual GEMM epilogues prepare every later
+// LayerNorm: the row's exact mean (two passes over the row held in registers) is its
+// pivot c, the fp16 copy (A operand of the LayerNorm-folded QKV GEMM) holds x - c, and
+// partial 0 of the row's n_parts statistics partials holds the (sum, sum of squares)
+// of x - c (the other partials zero).  Block 0 also zeroes the forward's attention
+// work counters, so a forward that reuses the token plan (no plan kernel) starts from
+// zero as well, even after an earlier launch gave up part-way.  This runs after
+// griddep_wait, i.e. after every kernel of the previous forward has completed.
 template <int VPL, typename TIn>
 __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ x,
                                                         const int* __restrict__ packed_src,
                                                         const int* __restrict__ rows_dev, int D,
                                                         float* resid, __half* x16, float2* stats,
-                                                        int n_parts, int* counters) {
+                                                        float* pivot, int n_parts, int* counters) {
   griddep_wait();
   griddep_launch();
   if (blockIdx.x == 0 && counters != nullptr)
@@ -220,28 +222,42 @@ __global__ void __launch_bounds__(256) ln_gather_kernel(const TIn* __restrict__ 
   if (row >= *rows_dev) return;
   const int src = packed_src[row];
   const int lane = lane_id();
-  float sum = 0.f, sq = 0.f;
+  float v[VPL][8];
+  float sum = 0.f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
     const int c = (lane + 32 * i) * 8;
     if (c < D) {
-      float v[8];
-      load8<TIn>(x + (size_t)src * D + c, v);
-      store8(resid + (size_t)row * D + c, v);
-      store8(x16 + (size_t)row * D + c, v);
+      load8<TIn>(x + (size_t)src * D + c, v[i]);
+      store8(resid + (size_t)row * D + c, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sum += v[i][e];
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffff, sum, o);
+  const float mean = sum / (float)D;
+  float dsum = 0.f, dsq = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = (lane + 32 * i) * 8;
+    if (c < D) {
+      float d[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) {
-        sum += v[e];
-        sq = fmaf(v[e], v[e], sq);
+        d[e] = v[i][e] - mean;
+        dsum += d[e];
+        dsq = fmaf(d[e], d[e], dsq);
       }
+      store8(x16 + (size_t)row * D + c, d);
     }
   }
   for (int o = 16; o > 0; o >>= 1) {
-    sum += __shfl_xor_sync(0xffffffff, sum, o);
-    sq += __shfl_xor_sync(0xffffffff, sq, o);
+    dsum += __shfl_xor_sync(0xffffffff, dsum, o);
+    dsq += __shfl_xor_sync(0xffffffff, dsq, o);
   }
+  if (lane == 0) pivot[row] = mean;
   for (int j = lane; j < n_parts; j += 32)
-    stats[(size_t)row * n_parts + j] = j == 0 ? make_float2(sum, sq) : make_float2(0.f, 0.f);
+    stats[(size_t)row * n_parts + j] = j == 0 ? make_float2(dsum, dsq) : make_float2(0.f, 0.f);
 }
 
 // One-time LayerNorm fold of a weight matrix W [rows, k] (fp16) consumed by
@@ -335,15 +351,24 @@ __global__ void __launch_bounds__(256) ln_rows_kernel(const TIn* __restrict__ in
 }
 
 // Final LayerNorm over every output token; padded tokens are written as exact zeros.
+// As the last kernel of a forward it also copies a non-zero device status word (a
+// bounded wait of an earlier kernel of the forward gave up) into the caller's pinned
+// host mirror, which the host reads without synchronising.
 template <int VPL, typename TOut>
 __global__ void __launch_bounds__(256) ln_final_scatter_kernel(const float* __restrict__ resid,
                                                                const int* __restrict__ dst_map,
                                                                int tokens, int D,
                                                                const float* gamma,
                                                                const float* beta, float eps,
-                                                               TOut* __restrict__ out) {
+                                                               TOut* __restrict__ out,
+                                                               const int* status,
+                                                               int* status_host) {
   griddep_wait();
   griddep_launch();
+  if (blockIdx.x == 0 && threadIdx.x == 0 && status != nullptr && status_host != nullptr) {
+    const int v = *reinterpret_cast<const volatile int*>(status);
+    if (v != 0) *reinterpret_cast<volatile int*>(status_host) = v;
+  }
   const int tok = blockIdx.x * (blockDim.x >> 5) + warp_id();
   if (tok >= tokens) return;
   const int lane = lane_id();
@@ -375,7 +400,10 @@ __global__ void __launch_bounds__(256) ln_final_scatter_kernel(const float* __re
 // Self-test of the bounded wait: waits on an mbarrier that nothing arrives on, with
 // a short limit, and reports TTTJ_DEV_TIMEOUT_SELFTEST.  Used by the failure
 // detection test; it never hangs.
-__global__ void wait_timeout_selftest_kernel(int* status, unsigned long long limit_ns) {
+// With status_host (a plan's pinned mirror) the code is copied there too, as the last
+// kernel of a forward would copy it.
+__global__ void wait_timeout_selftest_kernel(int* status, int* status_host,
+                                             unsigned long long limit_ns) {
   __shared__ __align__(8) uint64_t bar;
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&bar), 1);
@@ -383,8 +411,11 @@ __global__ void wait_timeout_selftest_kernel(int* status, unsigned long long lim
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    if (!mbar_wait(smem_u32(&bar), 0, nullptr, limit_ns))
+    if (!mbar_wait(smem_u32(&bar), 0, nullptr, limit_ns)) {
       report_status(status, TTTJ_DEV_TIMEOUT_SELFTEST);
+      if (status_host != nullptr)
+        *reinterpret_cast<volatile int*>(status_host) = TTTJ_DEV_TIMEOUT_SELFTEST;
+    }
   }
 }
 

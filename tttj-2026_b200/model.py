@@ -2,8 +2,9 @@
 
 It packs the parameter model's weights once into the library's device layout
 (fp16 matrices in nn.Linear's [out, in] layout, fp32 vectors; see
-include/tttj_b200.h) and runs every forward as one ``tttj_forward`` call on the
-caller's current CUDA stream.  Replaces the reference adapters
+include/tttj_b200.h), folds the LayerNorm affines into copies of the QKV / ffn_in
+weights once, and runs every forward as one ``tttj_forward`` call on the caller's
+current CUDA stream.  Replaces the reference adapters
 SequenceResidentTransformer (kernels/sequence_resident.py:125-233),
 Case8OptimizedTransformer (kernels/layerwise_hybrid.py:449-465), GraphedCase13Hybrid
 (kernels/case13_hybrid.py:641-748) and Case14OptimizedTransformer
@@ -12,6 +13,7 @@ Case8OptimizedTransformer (kernels/layerwise_hybrid.py:449-465), GraphedCase13Hy
 from __future__ import annotations
 
 import ctypes
+from collections import OrderedDict
 from typing import Optional
 
 import torch
@@ -82,24 +84,47 @@ def pack_weights(parameter_model: nn.Module, device: torch.device) -> torch.Tens
     return buf
 
 
-class _Plan:
-    """One C plan (TMA descriptors + workspace) for one (batch, seq_len) shape."""
+def fold_weights(cfg, packed: torch.Tensor) -> torch.Tensor:
+    """LayerNorm-folded copies of every block's QKV / ffn_in weights (and the padded
+    out_proj of narrow heads), computed once per model on the current stream
+    (``tttj_fold_weights``).  They depend on the layer shapes only, so every (B, S)
+    plan of the model shares them."""
+    L = _lib.lib()
+    c = _lib.TttjConfig.from_config(cfg)
+    nbytes = L.tttj_folded_bytes(ctypes.byref(c))
+    if nbytes == 0:
+        _lib.check(L.tttj_validate_config(ctypes.byref(c)), "fold_weights")
+    folded = torch.empty(nbytes, dtype=torch.uint8, device=packed.device)
+    stream = torch.cuda.current_stream(packed.device).cuda_stream
+    _lib.check(L.tttj_fold_weights(ctypes.byref(c), ctypes.c_void_p(packed.data_ptr()),
+                                   ctypes.c_void_p(folded.data_ptr()), nbytes,
+                                   ctypes.c_void_p(stream)), "fold_weights")
+    return folded
 
-    def __init__(self, cfg, batch: int, seq_len: int, weights: torch.Tensor, device: torch.device):
+
+class _Plan:
+    """One C plan (TMA descriptors + workspace) for one (batch, seq_len) shape.
+
+    Creating it launches nothing but the workspace's zero fill, on the current stream
+    (the stream of the forward that needs the plan); the plan orders its own forwards
+    across streams, and destroying it waits for its last forward."""
+
+    def __init__(self, cfg, batch: int, seq_len: int, weights: torch.Tensor,
+                 folded: torch.Tensor, device: torch.device):
         L = _lib.lib()
         self.c = _lib.TttjConfig.from_config(cfg, batch, seq_len)
+        self.handle = ctypes.c_void_p()
         ws_bytes = L.tttj_workspace_bytes(ctypes.byref(self.c))
         if ws_bytes == 0:
             _lib.check(L.tttj_validate_config(ctypes.byref(self.c)), "plan")
         # Zero-filled once: rows a call does not write stay finite for later calls.
         self.workspace = torch.zeros(ws_bytes, dtype=torch.uint8, device=device)
-        # Plan creation runs one-time weight-folding kernels on the legacy default
-        # stream; the packed weights and the workspace must be complete first.
-        torch.cuda.synchronize(device)
         handle = ctypes.c_void_p()
         _lib.check(
             L.tttj_plan_create(ctypes.byref(self.c), device.index, ctypes.c_void_p(weights.data_ptr()),
-                               ctypes.c_void_p(self.workspace.data_ptr()), ws_bytes, ctypes.byref(handle)),
+                               ctypes.c_void_p(folded.data_ptr()),
+                               ctypes.c_void_p(self.workspace.data_ptr()), ws_bytes,
+                               ctypes.byref(handle)),
             "plan",
         )
         self.handle = handle
@@ -144,18 +169,38 @@ class B200Transformer(nn.Module):
         # Keep a reference to the caller's model, as the reference adapter does
         # (kernels/sequence_resident.py:134-137).
         self.parameter_model = parameter_model
-        self.register_buffer("packed_weights", pack_weights(parameter_model, device), persistent=False)
-        self._plans: dict[tuple[int, int], _Plan] = {}
+        with torch.cuda.device(device):
+            self.register_buffer("packed_weights", pack_weights(parameter_model, device), persistent=False)
+            self.register_buffer("folded_weights", fold_weights(cfg, self.packed_weights), persistent=False)
+            # Plans are built on whichever stream first runs their shape: each waits
+            # for the fold once (an event, no host synchronisation).
+            self._weights_ready = torch.cuda.Event()
+            self._weights_ready.record(torch.cuda.current_stream(device))
+        self._plans: "OrderedDict[tuple[int, int], _Plan]" = OrderedDict()
         self._path = _lib.PATH_AUTO
+        self.max_plans = self.DEFAULT_MAX_PLANS
+
+    # Plans (workspace + descriptors) kept per module, least recently used evicted.
+    DEFAULT_MAX_PLANS = 8
 
     def plan_for(self, batch: int, seq_len: int) -> _Plan:
         key = (batch, seq_len)
         plan = self._plans.get(key)
-        if plan is None:
-            plan = _Plan(self.config, batch, seq_len, self.packed_weights, self.device)
-            _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, self._path), "set_path")
-            self._plans[key] = plan
+        if plan is not None:
+            self._plans.move_to_end(key)
+            return plan
+        while len(self._plans) >= max(1, int(self.max_plans)):
+            _, old = self._plans.popitem(last=False)
+            old.close()  # waits for the evicted plan's last forward, then frees it
+        torch.cuda.current_stream(self.device).wait_event(self._weights_ready)
+        plan = _Plan(self.config, batch, seq_len, self.packed_weights, self.folded_weights, self.device)
+        _lib.check(_lib.lib().tttj_plan_set_path(plan.handle, self._path), "set_path")
+        self._plans[key] = plan
         return plan
+
+    def cached_shapes(self) -> list[tuple[int, int]]:
+        """(batch, seq_len) of the plans currently held, least recently used first."""
+        return list(self._plans)
 
     def set_path(self, path: str) -> None:
         """Forward path for every shape: "auto" (default: the resident whole-stack
@@ -281,8 +326,19 @@ class B200Transformer(nn.Module):
 
     def device_status(self) -> int:
         """Synchronise and read the device status word of every plan; raise
-        RuntimeError if a bounded device wait gave up (returns 0 when healthy)."""
+        RuntimeError if a bounded device wait gave up (returns 0 when healthy).
+        Without this call, the next forward of the affected shape raises instead."""
         for plan in self._plans.values():
             v = ctypes.c_int(0)
             _lib.check(_lib.lib().tttj_plan_status(plan.handle, ctypes.byref(v)), "device status")
         return 0
+
+    def selftest_device_timeout(self, batch: int, seq_len: int, limit_ns: int = 2_000_000) -> None:
+        """Failure-detection self test: a bounded device wait on nothing gives up after
+        ``limit_ns`` and reports through the plan of shape [batch, seq_len] exactly as a
+        forward's kernel would, so that the next forward of that shape raises
+        RuntimeError.  No GPU fault is involved."""
+        plan = self.plan_for(batch, seq_len)
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.check(_lib.lib().tttj_plan_selftest_timeout(plan.handle, int(limit_ns),
+                                                         ctypes.c_void_p(stream)), "selftest")

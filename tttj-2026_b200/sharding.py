@@ -10,10 +10,10 @@ its north star.
   (projection FLOPs ~ len, attention FLOPs ~ len^2, causal halves the latter).
 * ``lpt_partition`` assigns sequences to shards longest-processing-time first, so
   padded batches with ragged lengths still balance.
-* ``shard_indices`` / ``gather_shards``: the one-process-per-GPU layout
-  (torch.distributed): every rank selects its sequences, runs its replica, and the
-  outputs are reassembled in the original batch order on the caller's request
-  (all_gather of the output; not part of the timed forward).
+* ``shard_indices`` / ``local_shard`` / ``gather_shards`` / ``distributed_forward``: the
+  one-process-per-GPU layout (torch.distributed): every rank selects its sequences,
+  runs its replica, and the outputs are reassembled in the original batch order on
+  the caller's request (all_gather to every rank, or a gather to one rank).
 * ``MultiDeviceTransformer``: one process driving several GPUs -- replicas on each
   device, peer copies of the shards, per-device streams, gather on the caller's device.
 """
@@ -76,14 +76,22 @@ def gather_shards(shards: Sequence[torch.Tensor], indices: Sequence[Sequence[int
     return out
 
 
+def local_shard(lengths: Sequence[int], cfg, rank: int, world_size: int) -> list[int]:
+    """Sequence indices rank ``rank`` of ``world_size`` runs (its LPT share, batch order).
+    A serving process that feeds only its own sequences selects them with this."""
+    return shard_indices(lengths, cfg, world_size)[rank]
+
+
 def distributed_forward(module, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor],
-                        group=None, gather: bool = True):
+                        group=None, gather: bool = True, dst: Optional[int] = None):
     """One-process-per-GPU forward: every rank holds the full batch (or the same
     seeded inputs), runs only its LPT shard on its own GPU, and -- if ``gather`` --
-    all-gathers the shard outputs so every rank returns the full [B, S, D] output.
+    collects the shard outputs into the full [B, S, D] output in batch order:
+    on every rank (``dst`` None: all_gather) or on rank ``dst`` only (a gather; the
+    other ranks return None for the output).  Returns (output, shard indices).
 
-    ``module`` is this rank's B200Transformer.  The gather is an all_gather of
-    fixed-size padded shard buffers (torch.distributed, any backend).
+    ``module`` is this rank's B200Transformer.  The collectives move fixed-size padded
+    shard buffers (torch.distributed, any backend; NCCL over NVLink on a B200 node).
     """
     import torch.distributed as dist
 
@@ -102,11 +110,17 @@ def distributed_forward(module, x: torch.Tensor, valid_token_mask: Optional[torc
     if not gather:
         return local, idx
     cap = max(len(i) for i in idx)
-    buf = x.new_zeros((cap, S, D))
-    if len(mine):
+    buf = x.new_zeros((cap, S, D)) if len(mine) < cap else local
+    if len(mine) < cap and len(mine):
         buf[: len(mine)] = local
-    bufs = [torch.empty_like(buf) for _ in range(world)]
-    dist.all_gather(bufs, buf, group=group)
+    if dst is None:
+        bufs = [torch.empty_like(buf) for _ in range(world)]
+        dist.all_gather(bufs, buf, group=group)
+    else:
+        bufs = [torch.empty_like(buf) for _ in range(world)] if rank == dst else None
+        dist.gather(buf, bufs, dst=dst, group=group)
+        if rank != dst:
+            return None, idx
     shards = [b[: len(i)] for b, i in zip(bufs, idx)]
     return gather_shards(shards, idx, B), idx
 

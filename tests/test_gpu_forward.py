@@ -80,6 +80,33 @@ def test_c2_per_rank_shapes_vs_oracle(batch):
     assert opt.device_status() == 0
 
 
+def test_organizer_slot_pattern():
+    """The organizer harness's slot (UserOptimizedTransformer.forward building the B200
+    module from itself, as INTEGRATION.md shows; the reference's class itself is
+    exercised on the CPU by tests/test_reference_classes.py): the output matches the
+    oracle, a second call reuses the module, and the model's state_dict still works."""
+    cfg = tb.TransformerConfig(4, 200, 256, 4, 512, 2, True)
+
+    class Slot(tb.TransformerParameters):
+        def forward(self, x, valid_token_mask=None):
+            if "_b200" not in self.__dict__:
+                self.__dict__["_b200"] = tb.make_optimized_transformer(self)
+            return self._b200(x, valid_token_mask)
+
+    torch.manual_seed(3)
+    model = Slot(cfg).to(device=DEV, dtype=torch.float16).eval()
+    x, mask = tb.generate_inputs(cfg, 4, torch.float16, (50, 200), DEV)
+    with torch.inference_mode():
+        out = model(x, mask)
+        again = model(x, mask)
+        ref = forward_fp32(state_dict_fp32(model, DEV), cfg, x.float(), mask)
+    torch.cuda.synchronize()
+    assert torch.equal(out, again)
+    r = gate(ref, out, mask)
+    assert r.passed, r
+    assert set(model.state_dict()) == set(tb.TransformerParameters(cfg).state_dict())
+
+
 def test_c3_padding_075_vs_oracle():
     """C3's shape with lengths in [128, 512] (padding ratio 0.75, the third ratio of the
     reference's gate, profiling/validate_fused_gate.py:17-20)."""

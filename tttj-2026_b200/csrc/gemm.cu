@@ -12,11 +12,20 @@ constexpr int STAGES_BN256 = 4;  // 4 x 48 KB ring (+32 KB output staging)
 // CTA pairs hold half of B per CTA: the same shared memory buys deeper rings.
 constexpr int STAGES_PAIR_BN128 = 8;  // 8 x 24 KB
 constexpr int STAGES_PAIR_BN256 = 6;  // 6 x 32 KB
+// With two TMA-fed residual staging blocks per epilogue warp (64 KB), the rings that
+// still fit: 5 x 32 KB or 6 x 24 KB.  (Measured on C5 out_proj: two blocks and five
+// stages 149 us, three blocks and four stages 150 us at a higher clock, one block
+// prefetched through registers with six stages 173 us.)
+constexpr int RBUF = 2;
+constexpr int STAGES_RB_PAIR_BN256 = 5;
+constexpr int STAGES_RB_PAIR_BN128 = 6;
+constexpr int STAGES_RB_BN128 = 5;
+constexpr int STAGES_RB_BN64 = 6;
 
-template <int BN, int EPI, int STAGES, bool PAIR>
+template <int BN, int EPI, int STAGES, bool PAIR, int RB = 0>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-  auto kern = gemm_tc_kernel<BN, EPI, STAGES, PAIR>;
-  constexpr int smem = GemmSmem<BN, STAGES, PAIR>::TOTAL;
+  auto kern = gemm_tc_kernel<BN, EPI, STAGES, PAIR, RB>;
+  constexpr int smem = GemmSmem<BN, STAGES, PAIR, RB>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the 227 KB per-CTA limit");
@@ -48,7 +57,34 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
   }
 }
 
+// The in-place fp32 residual epilogues with TMA-fed residual staging.
+template <int BN, int STAGES, bool PAIR>
+cudaError_t launch_rbuf(const GemmLaunch& g, cudaStream_t stream) {
+  switch (g.epi) {
+    case EPI_BIAS_RESIDUAL_F32:
+      return launch_t<BN, EPI_BIAS_RESIDUAL_F32, STAGES, PAIR, RBUF>(g, stream);
+    case EPI_RESIDUAL_F32_STATS:
+      return launch_t<BN, EPI_RESIDUAL_F32_STATS, STAGES, PAIR, RBUF>(g, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
+
+// The residual epilogue (fp32 residual in and out, fp16 copy, statistics) moves ~10 bytes
+// per output element against 2 K FLOPs; at short K it, not the MMA, sets the pace, and
+// with the residual prefetched only one 32-column chunk ahead through registers each
+// chunk waits for its load (measured: C5 out_proj, K = 1024, at half the DRAM
+// bandwidth, long-scoreboard stalls first).  TMA-fed staging blocks let the residual
+// loads run ahead without registers; they cost ring stages, so long-K GEMMs keep the
+// deep ring.
+int gemm_choose_rbuf(int bn, int pair, int k, int epi, bool in_place) {
+  const bool residual = epi == EPI_BIAS_RESIDUAL_F32 || epi == EPI_RESIDUAL_F32_STATS;
+  if (!residual || !in_place || k > 1536) return 0;
+  if (bn == 256 && !pair) return 0;  // a 48 KB stage: too few would fit
+  return RBUF;
+}
 
 int gemm_choose_bn(int rows, int n, int num_sms) {
   // The widest column tile whose tile count (128-row tiles) still fills >= 90% of the
@@ -124,6 +160,14 @@ void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pai
 }
 
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream) {
+  if (g.rbuf) {
+    if (g.rbuf != RBUF) return cudaErrorInvalidValue;
+    if (g.pair && g.bn == 256) return launch_rbuf<256, STAGES_RB_PAIR_BN256, true>(g, stream);
+    if (g.pair && g.bn == 128) return launch_rbuf<128, STAGES_RB_PAIR_BN128, true>(g, stream);
+    if (!g.pair && g.bn == 128) return launch_rbuf<128, STAGES_RB_BN128, false>(g, stream);
+    if (!g.pair && g.bn == 64) return launch_rbuf<64, STAGES_RB_BN64, false>(g, stream);
+    return cudaErrorInvalidValue;
+  }
   if (g.pair) {
     if (g.bn == 256) return launch_bn<256, STAGES_PAIR_BN256, true>(g, stream);
     if (g.bn == 128) return launch_bn<128, STAGES_PAIR_BN128, true>(g, stream);

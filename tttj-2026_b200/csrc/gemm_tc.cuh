@@ -33,23 +33,33 @@ namespace tttj {
 // PAIR: the tile is 256 x BN, computed by a CTA pair (cluster of 2) with cta_group::2
 // MMAs; each CTA holds 128 rows of A and BN/2 rows of B per stage and drains its own
 // 128 x BN accumulator.
-template <int BN, int STAGES, bool PAIR = false>
+// RBUF (fp32 residual epilogues updating the residual in place): each epilogue warp
+// owns RBUF 32 x 32 fp32 staging blocks into which TMA loads the residual chunks
+// RBUF - 1 chunks ahead of the one being drained (0: one staging block, the residual
+// prefetched one chunk ahead through registers).
+template <int BN, int STAGES, bool PAIR = false, int RBUF = 0>
 struct GemmSmem {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
-  static constexpr int OUT_BYTES = GEMM_EPI_WARPS * GEMM_STAGE_OUT_BYTES;
-  static constexpr int BAR_BYTES = (2 * STAGES + 4 + 1) * 8 + 16;
+  static constexpr int OUT_BUFS = RBUF > 0 ? RBUF : 1;
+  static constexpr int OUT_BYTES = GEMM_EPI_WARPS * GEMM_STAGE_OUT_BYTES * OUT_BUFS;
+  // full / empty per stage, 2 + 2 accumulator barriers, drain, TMEM slot + abort flag,
+  // one residual-load barrier per staging block.
+  static constexpr int BAR_BYTES = (2 * STAGES + 6 + GEMM_EPI_WARPS * RBUF) * 8 + 16;
   // +1024 so the tile ring can be aligned to the 1024-byte swizzle atom.
   static constexpr int TOTAL = TILE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int EPI, int STAGES, bool PAIR>
+template <int BN, int EPI, int STAGES, bool PAIR, int RBUF = 0>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using L = GemmSmem<BN, STAGES, PAIR>;
+  using L = GemmSmem<BN, STAGES, PAIR, RBUF>;
+  static_assert(RBUF == 0 || RBUF >= 2, "residual staging: one block, or at least two");
+  static_assert(RBUF == 0 || EPI == EPI_BIAS_RESIDUAL_F32 || EPI == EPI_RESIDUAL_F32_STATS,
+                "TMA residual loads serve the in-place fp32 residual epilogues");
   constexpr int CTAS = PAIR ? 2 : 1;
   constexpr int TM = GEMM_BM * CTAS;  // rows of a tile
   // Scheduling unit: the CTA, or the CTA pair (CTAs 2c and 2c+1 form cluster c).
@@ -71,6 +81,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const uint32_t bar_drain = bar_acce + 16;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const uint32_t bar_res = smem_u32(bars + 2 * STAGES + 6);  // [GEMM_EPI_WARPS][RBUF]
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -93,6 +104,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       mbar_init(bar_acce + 8 * b, GEMM_EPI_WARPS * CTAS);
     }
     mbar_init(bar_drain, 1);
+    for (int i = 0; i < GEMM_EPI_WARPS * RBUF; ++i) mbar_init(bar_res + 8 * i, 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -273,7 +285,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // first chunk of the current tile before the accumulator is ready, and loads chunk
     // c + 1 as soon as chunk c's values are consumed.
     auto prefetch_residual = [&](int t) {
-      if (!(RES_F32 || EPI == EPI_BIAS_RESIDUAL) || t >= num_tiles) return;
+      // (RBUF > 0: the TMA loads run ahead already.)
+      if (!(RES_F32 || EPI == EPI_BIAS_RESIDUAL) || RBUF > 0 || t >= num_tiles) return;
       const int mb = t / n_tiles;
       const int c0 = (t - mb * n_tiles) * BN + col_half * (BN / 2);
       const int r = mb * TM + (int)rank * GEMM_BM + row_in_tile;
@@ -314,6 +327,70 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
       }
     };
+    // RBUF > 0: the residual chunks of full tiles come by TMA (from tmC: the residual is
+    // updated in place) into this warp's staging blocks, in the order the warp drains
+    // them, RBUF - 1 chunks ahead.  Load j goes to block j % RBUF and completes on its
+    // barrier's phase (j / RBUF) & 1; block j % RBUF is refilled (load j + RBUF - 1)
+    // once the TMA store of chunk j - 1, which read it, has finished reading.  Every lane
+    // walks the same cursor; lane 0 issues.
+    const uint32_t res_buf0 = sOut + (uint32_t)((warp - 2) * RBUF * GEMM_STAGE_OUT_BYTES);
+    const uint32_t res_bar0 = bar_res + (uint32_t)(8 * (warp - 2) * RBUF);
+    int ld_k = 0, ld_cc = 0;        // load cursor: k-th tile of this unit, chunk in the tile
+    long ld_issued = 0, ld_used = 0;
+    auto issue_next_load = [&]() {
+      if constexpr (RBUF > 0) {
+        while (true) {
+          const int t = unit + ld_k * n_units;
+          if (t >= num_tiles) return;
+          const int cc = ld_cc;
+          if (++ld_cc == CHUNKS) {
+            ld_cc = 0;
+            ++ld_k;
+          }
+          const int mb = t / n_tiles;
+          const int cta_r0 = mb * TM + (int)rank * GEMM_BM;
+          const int c0 = (t - mb * n_tiles) * BN + (col_half * CHUNKS + cc) * 32;
+          if (cta_r0 + GEMM_BM > rows || c0 >= p.n) continue;  // drained without TMA
+          const int b = (int)(ld_issued % RBUF);
+          if (lane == 0) {
+            mbar_arrive_expect_tx(res_bar0 + 8 * b, GEMM_STAGE_OUT_BYTES);
+            tma_load_2d(res_buf0 + (uint32_t)(b * GEMM_STAGE_OUT_BYTES), &tmC, res_bar0 + 8 * b,
+                        c0, cta_r0 + quad * 32);
+          }
+          ++ld_issued;
+          return;
+        }
+      }
+    };
+    if constexpr (RBUF > 0) {
+      for (int i = 0; i < RBUF - 1; ++i) issue_next_load();
+    }
+    // Row statistics of the LayerNorm this epilogue applies (FOLD), or whose mean
+    // pivots the statistics it writes (EPI_RESIDUAL_F32_STATS), are loaded one tile
+    // ahead: the loads for tile t + n_units issue when tile t starts and land while
+    // its chunks drain.  (Loaded at the start of their own tile they cost each tile
+    // several thousand clocks, measured with per-tile clock stamps.)  Counts above
+    // MAXP partials are loaded in place.
+    constexpr int MAXP = 16;
+    constexpr bool ROWSTATS = FOLD || EPI == EPI_RESIDUAL_F32_STATS;
+    const float2* st_src = FOLD ? p.stats_in : p.stats_prev;
+    const int st_parts = FOLD ? p.stats_parts : p.stats_prev_parts;
+    const bool st_ahead = ROWSTATS && st_parts <= MAXP;
+    float2 pst[ROWSTATS ? MAXP : 1];
+    float ppiv = 0.f;
+    auto fetch_row_stats = [&](int t) {
+      if constexpr (ROWSTATS) {
+        if (!st_ahead || t >= num_tiles) return;
+        const int r = (t / n_tiles) * TM + (int)rank * GEMM_BM + row_in_tile;
+        if (r >= rows) return;
+        const float2* st = st_src + (size_t)r * st_parts;
+#pragma unroll
+        for (int j = 0; j < MAXP; ++j)
+          if (j < st_parts) pst[j] = __ldg(st + j);
+        if (EPI == EPI_RESIDUAL_F32_STATS) ppiv = __ldg(p.pivot_prev + r);
+      }
+    };
+    fetch_row_stats(unit);
     prefetch_residual(unit);
     for (int tile = unit; tile < num_tiles; tile += n_units) {
       const int m_blk = tile / n_tiles;
@@ -329,39 +406,53 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       // Everything that does not depend on the accumulator is fetched before waiting
       // for it: the LayerNorm statistics of this row and the first residual chunk.
       float ln_mean = 0.f, ln_rstd = 0.f;
-      if (FOLD && row_ok) {
-        float ssum = 0.f, ssq = 0.f;
-        const float2* st = p.stats_in + (size_t)row * p.stats_parts;
-        for (int j = 0; j < p.stats_parts; ++j) {  // fixed order: deterministic
-          const float2 v2 = st[j];
-          ssum += v2.x;
-          ssq += v2.y;
-        }
-        // Partials are of x - pivot, so ln_mean is small against the spread of the row
-        // and the variance does not cancel.
-        const float inv_k = 1.0f / (float)p.k;
-        ln_mean = ssum * inv_k;
-        const float var = fmaxf(ssq * inv_k - ln_mean * ln_mean, 0.f);
-        ln_rstd = rsqrtf(var + p.ln_eps);
-      }
       // EPI_RESIDUAL_F32_STATS: the pivot of this row's new statistics is the mean of
-      // the residual before the add (the previous LayerNorm's statistics, summed in
-      // the same fixed order by every CTA, so all column tiles of a row agree on it).
+      // the residual before the add (the previous LayerNorm's statistics).
       float shift = 0.f;
-      if (EPI == EPI_RESIDUAL_F32_STATS && row_ok) {
-        float ssum = 0.f;
-        const float2* st = p.stats_prev + (size_t)row * p.stats_prev_parts;
-        for (int j = 0; j < p.stats_prev_parts; ++j) ssum += st[j].x;
-        shift = p.pivot_prev[row] + ssum * (1.0f / (float)p.n);
+      if (ROWSTATS && row_ok) {
+        // Partials summed in a fixed order: deterministic, and every CTA of a row
+        // agrees on the result.
+        float ssum = 0.f, ssq = 0.f, piv = 0.f;
+        if (st_ahead) {
+#pragma unroll
+          for (int j = 0; j < MAXP; ++j) {
+            if (j < st_parts) {
+              ssum += pst[j].x;
+              ssq += pst[j].y;
+            }
+          }
+          piv = ppiv;
+        } else {
+          const float2* st = st_src + (size_t)row * st_parts;
+          for (int j = 0; j < st_parts; ++j) {
+            const float2 v2 = st[j];
+            ssum += v2.x;
+            ssq += v2.y;
+          }
+          if (EPI == EPI_RESIDUAL_F32_STATS) piv = p.pivot_prev[row];
+        }
+        if (FOLD) {
+          // Partials are of x - pivot, so ln_mean is small against the spread of the
+          // row and the variance does not cancel.
+          const float inv_k = 1.0f / (float)p.k;
+          ln_mean = ssum * inv_k;
+          const float var = fmaxf(ssq * inv_k - ln_mean * ln_mean, 0.f);
+          ln_rstd = rsqrtf(var + p.ln_eps);
+        } else {
+          shift = piv + ssum * (1.0f / (float)p.n);
+        }
       }
+      fetch_row_stats(tile + n_units);
       const int seg0 = n_blk * BN + col_half * (BN / 2);
-      if (seg0 < p.n && (staged_res || row_ok)) load_res(staged_res, row0, row, seg0);
+      if (seg0 < p.n && ((staged_res && RBUF == 0) || (!staged_res && row_ok)))
+        load_res(staged_res, row0, row, seg0);
       if (!mbar_wait(bar_accf + 8 * acc, acc_phase, abort_flag, limit)) {
         *abort_flag = 1;
         report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);
         break;
       }
       tc_fence_after();
+      bool res_failed = false;            // a residual load did not arrive in time
       float row_sum = 0.f, row_sq = 0.f;  // EPI_RESIDUAL_F32_STATS
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
@@ -422,19 +513,31 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         const bool more = cc + 1 < CHUNKS && col0 + 32 < p.n;
         if (staged_res) {
           // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk j of row r at j ^ (r % 8).
-          // The previous TMA store from this warp's staging block must have read it.
-          if (lane == 0) bulk_wait_read_all();
-          __syncwarp();
+          uint32_t blk = stage_out;
+          if constexpr (RBUF > 0) {
+            // The residual chunk was loaded into block ld_used % RBUF by TMA.
+            const int b = (int)(ld_used % RBUF);
+            blk = res_buf0 + (uint32_t)(b * GEMM_STAGE_OUT_BYTES);
+            if (!__all_sync(0xffffffffu, mbar_wait(res_bar0 + 8 * b, (uint32_t)((ld_used / RBUF) & 1),
+                                                   abort_flag, limit))) {
+              res_failed = true;
+              break;
+            }
+          } else {
+            // The previous TMA store from this warp's staging block must have read it.
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {  // residual in, transposed by position
-            const int rr = 4 * q + (lane >> 3), j = lane & 7;
-            const uint32_t dst = stage_out + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(rc[q].x),
-                         "f"(rc[q].y), "f"(rc[q].z), "f"(rc[q].w)
-                         : "memory");
+            for (int q = 0; q < 8; ++q) {  // residual in, transposed by position
+              const int rr = 4 * q + (lane >> 3), j = lane & 7;
+              const uint32_t dst = blk + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
+              asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "f"(rc[q].x),
+                           "f"(rc[q].y), "f"(rc[q].z), "f"(rc[q].w)
+                           : "memory");
+            }
+            __syncwarp();
           }
-          __syncwarp();
-          const uint32_t rbase = stage_out + (uint32_t)(lane * 128);
+          const uint32_t rbase = blk + (uint32_t)(lane * 128);
 #pragma unroll
           for (int j = 0; j < 8; ++j) {  // this row's residual; the sum goes to the same slot
             const uint32_t a = rbase + (uint32_t)(((j ^ (lane & 7)) & 7) << 4);
@@ -451,7 +554,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                          "f"(v[4 * j + 1]), "f"(v[4 * j + 2]), "f"(v[4 * j + 3])
                          : "memory");
           }
-          if (more) load_res(true, row0, row, col0 + 32);
+          if (RBUF == 0 && more) load_res(true, row0, row, col0 + 32);
           if (EPI == EPI_RESIDUAL_F32_STATS) {
             float s4[4] = {0.f, 0.f, 0.f, 0.f}, q4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -466,7 +569,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stage_out, col0, row0);
+            tma_store_2d(&tmC, blk, col0, row0);
             bulk_commit();
           }
           if (EPI == EPI_RESIDUAL_F32_STATS) {
@@ -477,7 +580,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             for (int q = 0; q < 8; ++q) {
               const int rr = 4 * q + (lane >> 3), j = lane & 7;
               const float sh = __shfl_sync(0xffffffffu, shift, rr);
-              const uint32_t a = stage_out + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
+              const uint32_t a = blk + (uint32_t)(rr * 128 + ((j ^ (rr & 7)) << 4));
               float4 x;
               asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
                            : "=f"(x.x), "=f"(x.y), "=f"(x.z), "=f"(x.w)
@@ -486,6 +589,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
               *reinterpret_cast<uint2*>(p.out16 + (size_t)(row0 + rr) * p.ld16 + col0 + 4 * j) =
                   make_uint2(pack_half2(x.x - sh, x.y - sh), pack_half2(x.z - sh, x.w - sh));
             }
+          }
+          if constexpr (RBUF > 0) {
+            // Refill the block of the previous chunk (load ld_used + RBUF - 1) once its TMA
+            // store has read it; order this warp's generic reads of that block before the
+            // async-proxy write.
+            ++ld_used;
+            if (lane == 0) bulk_wait_read_1();
+            __syncwarp();
+            fence_proxy_async_smem();
+            issue_next_load();
           }
           continue;
         }
@@ -573,15 +686,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
         }
       }
+      if (res_failed) {
+        *abort_flag = 1;
+        report_status(p.status, TTTJ_DEV_TIMEOUT_EPILOGUE);
+        break;
+      }
       // The warp's TMEM reads are complete (tcgen05.wait::ld in every lane): release
-      // the accumulator to the (leader's) MMA thread.
+      // the accumulator to the (leader's) MMA thread.  The arrival orders nothing else
+      // (a release would first wait for this thread's global stores).
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
         if (PAIR)
-          mbar_arrive_cluster(map_to_cta(bar_acce + 8 * acc, 0));
+          mbar_arrive_cluster_relaxed(map_to_cta(bar_acce + 8 * acc, 0));
         else
-          mbar_arrive(bar_acce + 8 * acc);
+          mbar_arrive_relaxed(bar_acce + 8 * acc);
       }
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
@@ -591,7 +710,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         if (n_blk == 0 && col_half == 0) p.pivot_out[row] = shift;
       }
     }
-    // Stores issued by this warp must complete before the CTA exits.
+    // Residual loads still in flight (only after a timeout) land before the CTA exits,
+    // and so do the stores issued by this warp.
+    if constexpr (RBUF > 0) {
+      for (long j = ld_used; j < ld_issued; ++j)
+        mbar_wait(res_bar0 + 8 * (int)(j % RBUF), (uint32_t)((j / RBUF) & 1), nullptr, limit);
+    }
     if (lane == 0) bulk_wait_all();
     __syncwarp();
   }

@@ -56,6 +56,7 @@ struct GemmLaunch {
   int pair;  // 1: 256 x bn tiles on CTA pairs (cta_group::2), 0: 128 x bn tiles per CTA
   int epi;   // GemmEpilogue
   int grid;  // persistent CTAs (even for pairs)
+  int rbuf;  // fp32 residual staging blocks per epilogue warp fed by TMA (0: none)
 };
 
 // Tile shape for a GEMM of `rows` x `n` x `k` with epilogue `epi` on `num_sms` SMs:
@@ -63,6 +64,9 @@ struct GemmLaunch {
 // shape uses the same width) and whether CTA pairs compute it (see gemm.cu).
 int gemm_choose_bn(int rows, int n, int num_sms);
 void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pair);
+// Residual staging blocks (gemm_tc.cuh RBUF) for a GEMM with that tile shape: 2 for the
+// in-place fp32 residual epilogues with short K, else 0.
+int gemm_choose_rbuf(int bn, int pair, int k, int epi, bool in_place);
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
 // tcgen05 attention for a head-dim layout of 32, 64, 128 or 256 (plan with q_block

@@ -8,7 +8,7 @@
 // mask is "key < valid length" and the causal mask compares packed positions.
 //
 // Work item = one (sequence, head, NT x 128 query rows) = NT 128-row query tiles (NT = 2,
-// or 1 at head_dim 256).  The CTA is persistent over the longest-first work list and runs
+// or 1 at head_dim 256); the two sides swap query tiles on alternate items.  The CTA is persistent over the longest-first work list and runs
 // 11 warps:
 //   warp 8      TMA: Q tiles (double-buffered across items), K/V tiles (STAGES ring)
 //   warps 9/10  issue tcgen05.mma for query tile 0 / 1 (the whole warp runs the loop,
@@ -119,6 +119,16 @@ __device__ __forceinline__ uint64_t atc_desc_qk(uint32_t tile, int kk) {
            (uint64_t)(2 * (kk & 3));
   }
 }
+// Which query tile of the CTA's k-th item side t (a softmax warpgroup with its MMA warp
+// and TMEM buffers) handles.  Causal items are uneven -- the upper query tile streams
+// one key tile more than the lower one, and for sequences of <= 256 tokens that is
+// twice the work -- so the sides swap tiles on alternate items and share the long ones
+// (measured: C5 attention about 5% fewer cycles, C2 / C3 unchanged).
+template <int NT>
+__device__ __forceinline__ int atc_query_tile(int t, int k) {
+  return NT == 2 ? (t ^ (k & 1)) : t;
+}
+
 template <int HD>
 __device__ __forceinline__ uint64_t atc_desc_v(uint32_t addr) {
   // V tile [128 keys][HD] is the B operand (K = keys, N = HD) stored N-contiguous; the
@@ -311,8 +321,10 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         if (!wait(bar_q_full + 8 * qb, (k / QBUF) & 1)) break;
         const int n_kv = __shfl_sync(FULL, info[qb].n_kv, 0);
         if (n_kv < 0) break;  // no more items
-        const int n = __shfl_sync(FULL, info[qb].n[t], 0);
-        const uint32_t qaddr = sQ + (qb * NT + t) * SM::Q_TILE;
+        // Query tile of this item handled by this warp's side (see atc_query_tile).
+        const int tq = atc_query_tile<NT>(t, k);
+        const int n = __shfl_sync(FULL, info[qb].n[tq], 0);
+        const uint32_t qaddr = sQ + (qb * NT + tq) * SM::Q_TILE;
         auto issue_s = [&](long kv_idx) {
           const uint32_t kaddr = sKV + (int)(kv_idx % STAGES) * 2 * SM::KV_TILE;
 #pragma unroll
@@ -432,10 +444,11 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
       const AtcItem w = info[qb];
       if (w.n_kv < 0) break;  // no more items
       mbar_arrive(bar_q_empty + 8 * qb);  // this thread no longer needs the info slot
-      const int n = w.n[t];
+      const int tq = atc_query_tile<NT>(t, k);  // query tile of this item on this side
+      const int n = w.n[tq];
       if (n == 0) continue;
-      const int qrow = w.q0 + t * ATC_BM + row;  // query index inside the sequence
-      const int kv_end = w.kv_end[t];
+      const int qrow = w.q0 + tq * ATC_BM + row;  // query index inside the sequence
+      const int kv_end = w.kv_end[tq];
       float m_run = -INFINITY;  // running max (log2 domain) used as the exp base
       float l_run = 0.f;
       for (int j = 0; j < n; ++j) {
@@ -460,7 +473,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
         const int k0 = j * ATC_BN;
         const bool need_mask =
-            (k0 + ATC_BN > kv_end) || (CAUSAL && k0 + ATC_BN - 1 > w.q0 + t * ATC_BM);
+            (k0 + ATC_BN > kv_end) || (CAUSAL && k0 + ATC_BN - 1 > w.q0 + tq * ATC_BM);
         if (need_mask) {
           // Column c of this tile is masked when c > lim (key >= kv_end, or key > query).
           const int lim = (CAUSAL ? min(kv_end - 1, qrow) : kv_end - 1) - k0;
@@ -594,7 +607,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         {
           constexpr int RPI = 32 / NCH;  // rows per store instruction
           const int j = lane % NCH;
-          const int q0row = w.q0 + t * ATC_BM + quad * 32;  // first query row of this warp
+          const int q0row = w.q0 + tq * ATC_BM + quad * 32;  // first query row of this warp
 #pragma unroll
           for (int it = 0; it < 32 / RPI; ++it) {
             const int rr = it * RPI + lane / NCH;
@@ -611,7 +624,7 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
       } else {
         // Wide heads: each thread stores its own row, 64 bytes per 32 columns.
-        const int qr = w.q0 + t * ATC_BM + row;
+        const int qr = w.q0 + tq * ATC_BM + row;
         const bool store = qr < w.len && w.seq0 + qr < p.rows_max;
         __half* dst = p.ctx + (size_t)(w.seq0 + qr) * W + w.h * HD;
 #pragma unroll 1

@@ -139,6 +139,37 @@ int tttj_plan_destroy(tttj_plan* plan);
 int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* valid_mask,
                  void* out, void* stream);
 
+/* ---- context parallelism: one sequence split across ranks ----
+ *
+ * For batches smaller than the number of GPUs (the north star's C4, 4 sequences of
+ * 8192 tokens, on 8 GPUs): the valid tokens [0, seq_len_valid) of ONE sequence are
+ * shared out between ranks in contiguous slices; rank r runs every GEMM of the stack on
+ * its own rows only, and after each layer's QKV GEMM one exchange -- an all-gather of
+ * the ranks' q|k|v rows, enqueued by the caller -- gives every rank the whole
+ * sequence's keys and values, so its attention (its own queries against all earlier
+ * keys) is exact.  No counterpart in the reference (single-GPU only).
+ *
+ * A split plan: cfg->batch_size = 1 and cfg->seq_len = this rank's row count; its rows
+ * are [row_lo, row_lo + seq_len) of the sequence (row_lo a multiple of the attention
+ * work item: 256 rows, 128 at head_dim 256; a share that ends before the sequence does
+ * ends on such a multiple too).  The plan's q|k|v buffer holds full_rows (>= the valid
+ * length) rows of the whole sequence, this rank's at their positions: with shares of
+ * at most m rows, rank r's rows at r * m and full_rows = ranks * m, an in-place
+ * all-gather of m-row slices fills it (the first rank takes the largest share, so the
+ * slices are contiguous).  tttj_plan_cp_qkv reports where that buffer lives in the
+ * workspace.  tttj_forward_cp calls exchange(user, layer, stream) once per layer,
+ * after the rank's q|k|v rows are enqueued on `stream`; the callback enqueues the
+ * all-gather on the same stream (returning non-zero aborts the forward).  x and out are
+ * the rank's own rows [seq_len, d_model]. */
+typedef int (*tttj_exchange_fn)(void* user, int layer, void* stream);
+size_t tttj_workspace_bytes_cp(const tttj_config* cfg, int full_rows);
+int tttj_plan_create_cp(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                        int seq_len_valid, int row_lo, int full_rows, void* workspace,
+                        size_t workspace_bytes, tttj_plan** out_plan);
+int tttj_plan_cp_qkv(tttj_plan* plan, size_t* offset, size_t* row_bytes, int* full_rows);
+int tttj_forward_cp(tttj_plan* plan, const void* x, int x_dtype, void* out,
+                    tttj_exchange_fn exchange, void* user, void* stream);
+
 /* Forward path of a plan.  The resident-stack kernel runs the whole forward of
  * sequences of at most 128 tokens in one launch (one CTA per sequence); it fits
  * d_model <= 128 or 256 with layout head_dim 32/64/128 and enough TMEM / shared memory.

@@ -32,6 +32,9 @@ B_QKV, B_OUT, B_FFN_IN, B_FFN_OUT = 4, 5, 6, 7
 LN1_W, LN1_B, LN2_W, LN2_B = 8, 9, 10, 11
 LNF_W, LNF_B = 12, 13
 
+# int exchange(void* user, int layer, void* stream) -- see tttj_forward_cp.
+EXCHANGE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p)
+
 # Every symbol include/tttj_b200.h declares, with (restype, argtypes).
 _c = ctypes
 _vp = _c.c_void_p
@@ -78,6 +81,15 @@ _SIGNATURES = {
     ),
     "tttj_selftest_wait_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
     "tttj_plan_selftest_timeout": (_c.c_int, [_vp, _c.c_uint64, _vp]),
+    "tttj_workspace_bytes_cp": (_c.c_size_t, [_vp, _c.c_int]),
+    "tttj_plan_create_cp": (
+        _c.c_int,
+        [_vp, _c.c_int, _vp, _vp, _c.c_int, _c.c_int, _c.c_int, _vp, _c.c_size_t, _c.POINTER(_vp)],
+    ),
+    "tttj_plan_cp_qkv": (
+        _c.c_int, [_vp, _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_size_t), _c.POINTER(_c.c_int)]
+    ),
+    "tttj_forward_cp": (_c.c_int, [_vp, _vp, _c.c_int, _vp, EXCHANGE_FN, _vp, _vp]),
     "tttj_device_sm_count": (_c.c_int, [_c.c_int]),
     "tttj_plan_launch_count": (_c.c_int, [_vp]),
     "tttj_plan_enable_timing": (_c.c_int, [_vp, _c.c_int]),

@@ -102,6 +102,7 @@ bool weight_offset(const tttj_config& c, int layer, int field, size_t* off, size
 // ---------------------------------------------------------------- workspace layout
 struct WsLayout {
   size_t seq_len, seq_off, packed_src, dst_map, items, item_count, counters, status;
+  size_t attn_plan;  // split plans: token plan of the whole sequence's attention
   size_t resid, x16, qkv, ctx, hid, stats, pivot;
   size_t total;
 };
@@ -152,15 +153,25 @@ size_t plan_layout(size_t B, size_t S, size_t H, WsLayout* w) {
   return o;
 }
 
-WsLayout ws_layout(const tttj_config& c) {
+// full_rows > 0: a split plan (one sequence whose tokens are shared out between ranks):
+// the rank's own rows (T = seq_len of the config) everywhere, except qkv and ctx, which
+// hold the whole sequence (full_rows rows, the rank's at their sequence positions), and
+// a second token plan for the whole sequence's attention.
+WsLayout ws_layout(const tttj_config& c, size_t full_rows = 0) {
   WsLayout w{};
   const size_t T = (size_t)c.batch_size * c.seq_len, D = c.d_model, F = c.ffn_dim;
   const size_t Q = qkv_width(c);
   size_t o = plan_layout(c.batch_size, c.seq_len, c.num_heads, &w);
+  if (full_rows) {
+    WsLayout wa{};
+    w.attn_plan = o;
+    o += plan_layout(1, full_rows, c.num_heads, &wa);
+  }
+  const size_t TQ = full_rows ? full_rows : T;
   w.resid = o; o += align_up(T * D * 4);
   w.x16 = o; o += align_up(T * D * 2);
-  w.qkv = o; o += align_up(T * 3 * Q * 2);
-  w.ctx = o; o += align_up(T * Q * 2);
+  w.qkv = o; o += align_up(TQ * 3 * Q * 2);
+  w.ctx = o; o += align_up(TQ * Q * 2);
   w.hid = o; o += align_up(T * F * 2);
   w.stats = o; o += align_up((size_t)2 * T * stats_parts(c) * 8);
   w.pivot = o; o += align_up((size_t)2 * T * 4);
@@ -450,6 +461,11 @@ struct tttj_plan {
   __half *x16, *qkv, *ctx, *hid;  // x16: fp16 copy of resid - pivot (GEMM A operand)
   float2* stats;  // [2][T][parts] LayerNorm statistics partials: LN1 (next QKV), LN2 (ffn_in)
   float* pivot;   // [2][T] per-row pivot of each statistics buffer
+  // Split plan (tttj_plan_create_cp): this rank runs rows [cp_lo, cp_lo + T) of one
+  // sequence of cp_len valid tokens; qkv / ctx hold cp_full rows of the whole sequence.
+  bool cp = false;
+  int cp_lo = 0, cp_len = 0, cp_full = 0;
+  TokenPlan tp_attn;  // the whole sequence's attention items (this rank's queries)
   int parts;      // statistics partials per row of LN1 (ffn_out, the gather -> QKV)
   int parts_ln2;  // ... of LN2 (out_proj -> ffn_in)
   std::vector<LayerGemms> layers;
@@ -490,10 +506,13 @@ struct DeviceGuard {
 }  // namespace
 
 int layerwise_launches(const tttj_config& c) { return 5 * c.num_layers + 3; }
+// Most launches one forward of a plan may record (a split plan's first has two plans).
+int max_launches(const tttj_config& c) { return layerwise_launches(c) + 1; }
 bool use_resident(const tttj_plan* p) {
   return p->path == TTTJ_PATH_RESIDENT || (p->path == TTTJ_PATH_AUTO && p->res_auto);
 }
 int launches_per_forward(const tttj_plan* p) {
+  if (p->cp) return layerwise_launches(p->cfg) - 1 + (p->plan_static ? 0 : 2);
   return use_resident(p) ? 1 : layerwise_launches(p->cfg) - (p->plan_static ? 1 : 0);
 }
 
@@ -706,13 +725,24 @@ int tttj_fold_weights(const tttj_config* cfg, const void* weights, void* folded,
   return TTTJ_OK;
 }
 
-int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, const void* folded,
-                     void* workspace, size_t workspace_bytes, tttj_plan** out_plan) {
+}  // extern "C"
+
+namespace {
+// A rank's share of one sequence split across ranks (tttj_plan_create_cp).
+struct CpArgs {
+  int len;   // valid tokens of the sequence (positions 0 .. len - 1)
+  int lo;    // first of this rank's rows
+  int full;  // rows of the whole-sequence qkv / ctx buffers (>= len)
+};
+
+int plan_create_impl(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                     void* workspace, size_t workspace_bytes, const CpArgs* cp,
+                     tttj_plan** out_plan) {
   int rc = check_config(cfg);
   if (rc) return rc;
   if (!weights || !folded || !workspace || !out_plan)
     return fail(TTTJ_ERR_INVALID, "null pointer argument");
-  const WsLayout lay = ws_layout(*cfg);
+  const WsLayout lay = ws_layout(*cfg, cp ? (size_t)cp->full : 0);
   if (workspace_bytes < lay.total)
     return fail(TTTJ_ERR_INVALID, "workspace too small: %zu < %zu", workspace_bytes, lay.total);
   if ((reinterpret_cast<uintptr_t>(weights) | reinterpret_cast<uintptr_t>(workspace) |
@@ -741,6 +771,15 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, co
   p->ws = static_cast<uint8_t*>(workspace);
   p->lay = lay;
   p->tp = token_plan_at(p->ws, lay);
+  if (cp) {
+    p->cp = true;
+    p->cp_lo = cp->lo;
+    p->cp_len = cp->len;
+    p->cp_full = cp->full;
+    WsLayout wa{};
+    plan_layout(1, cp->full, cfg->num_heads, &wa);
+    p->tp_attn = token_plan_at(p->ws + lay.attn_plan, wa);
+  }
   p->status = reinterpret_cast<int*>(p->ws + lay.status);
   p->resid = reinterpret_cast<float*>(p->ws + lay.resid);
   p->x16 = reinterpret_cast<__half*>(p->ws + lay.x16);
@@ -807,14 +846,17 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, co
       p->parts_ln2 = 2 * ((D + out_bn - 1) / out_bn);
       p->parts = 2 * ((D + ffn_bn - 1) / ffn_bn);
     }
-    rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, p->qkv, 3 * Q, nullptr, 0, T, rows_dev,
+    // A split plan writes its rows' q|k|v at their sequence positions.
+    __half* qkv_out = p->qkv + (cp ? (size_t)cp->lo * 3 * Q : 0);
+    rc = build_gemm(&L.qkv, p->x16, D, wqkv_f, D, bqkv_f, qkv_out, 3 * Q, nullptr, 0, T, rows_dev,
                     3 * Q, D, EPI_LN_FOLD, p->status, p->num_sms);
     L.qkv.p.stats_in = st_ln1;
     L.qkv.p.stats_parts = p->parts;
     L.qkv.p.colsum = cqkv;
     L.qkv.p.ln_eps = kLnEps;
     if (!rc)
-      rc = build_gemm(&L.out, p->ctx, Q, wo_pad ? static_cast<const void*>(wo_pad) : W(l, TTTJ_W_OUT),
+      rc = build_gemm(&L.out, p->ctx + (cp ? (size_t)cp->lo * Q : 0), Q,
+                      wo_pad ? static_cast<const void*>(wo_pad) : W(l, TTTJ_W_OUT),
                       Q, reinterpret_cast<const float*>(W(l, TTTJ_B_OUT)), p->resid, D, p->resid,
                       D, T, rows_dev, D, Q, EPI_RESIDUAL_F32_STATS, p->status, p->num_sms);
     L.out.p.out16 = p->x16;
@@ -856,14 +898,63 @@ int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, co
   p->lnf_w = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_W));
   p->lnf_b = reinterpret_cast<const float*>(W(cfg->num_layers, TTTJ_LNF_B));
 
-  rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S,
-                       cfg->num_heads, hd, hp, p->tp, p->status, p->num_sms);
+  if (cp)
+    rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, cp->full, 1, cp->full,
+                         cfg->num_heads, hd, hp, p->tp_attn, p->status, p->num_sms);
+  else
+    rc = build_attention(&p->attn_tm, &p->attn, &p->attn_grid, p->qkv, p->ctx, T, B, S,
+                         cfg->num_heads, hd, hp, p->tp, p->status, p->num_sms);
   if (rc) return bail(rc);
-  if (resident_fits(*cfg)) {
+  if (resident_fits(*cfg) && !cp) {
     rc = build_resident(p, fl);
     if (rc) return bail(rc);
   }
   *out_plan = p;
+  return TTTJ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int tttj_plan_create(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                     void* workspace, size_t workspace_bytes, tttj_plan** out_plan) {
+  return plan_create_impl(cfg, device, weights, folded, workspace, workspace_bytes, nullptr,
+                          out_plan);
+}
+
+size_t tttj_workspace_bytes_cp(const tttj_config* cfg, int full_rows) {
+  if (check_config(cfg) || full_rows <= 0) return 0;
+  return ws_layout(*cfg, (size_t)full_rows).total;
+}
+
+int tttj_plan_create_cp(const tttj_config* cfg, int device, const void* weights, const void* folded,
+                        int seq_len_valid, int row_lo, int full_rows, void* workspace,
+                        size_t workspace_bytes, tttj_plan** out_plan) {
+  int rc = check_config(cfg);
+  if (rc) return rc;
+  const int item = atc_item_rows(layout_hd(*cfg));
+  const int rows = cfg->seq_len;  // this rank's rows
+  if (cfg->batch_size != 1)
+    return fail(TTTJ_ERR_INVALID, "plan_create_cp: batch_size must be 1 (one sequence per split)");
+  if (row_lo < 0 || row_lo % item || rows <= 0 || row_lo + rows > seq_len_valid ||
+      seq_len_valid > full_rows)
+    return fail(TTTJ_ERR_INVALID,
+                "plan_create_cp: rows [%d, %d) of %d valid tokens (buffers of %d rows): the first "
+                "row must be a multiple of %d and the share inside the sequence",
+                row_lo, row_lo + rows, seq_len_valid, full_rows, item);
+  if (row_lo + rows != seq_len_valid && (row_lo + rows) % item)
+    return fail(TTTJ_ERR_INVALID, "plan_create_cp: a share that ends before the sequence does "
+                "must end on a multiple of %d rows", item);
+  const CpArgs cp{seq_len_valid, row_lo, full_rows};
+  return plan_create_impl(cfg, device, weights, folded, workspace, workspace_bytes, &cp, out_plan);
+}
+
+int tttj_plan_cp_qkv(tttj_plan* p, size_t* offset, size_t* row_bytes, int* full_rows) {
+  if (!p || !offset || !row_bytes || !full_rows) return fail(TTTJ_ERR_INVALID, "cp_qkv: null argument");
+  if (!p->cp) return fail(TTTJ_ERR_INVALID, "cp_qkv: not a split plan");
+  *offset = p->lay.qkv;
+  *row_bytes = 3 * qkv_width(p->cfg) * sizeof(__half);
+  *full_rows = p->cp_full;
   return TTTJ_OK;
 }
 
@@ -898,7 +989,7 @@ int tttj_plan_enable_timing(tttj_plan* p, int enable) {
   if (!p) return fail(TTTJ_ERR_INVALID, "timing: null plan");
   DeviceGuard guard(p->device);
   if (enable && !p->timing) {
-    const int n = layerwise_launches(p->cfg);  // the larger of the two paths
+    const int n = max_launches(p->cfg);  // the largest forward of any path
     p->ev_start.resize(n);
     p->ev_stop.resize(n);
     p->ev_class.assign(n, 0);
@@ -957,11 +1048,20 @@ size_t debug_floats(const tttj_config& c) {
 }  // namespace
 
 static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
-                        void* out, void* stream_ptr, const DebugCapture* dbg);
+                        void* out, void* stream_ptr, const DebugCapture* dbg,
+                        tttj_exchange_fn exchange = nullptr, void* user = nullptr);
 
 extern "C" int tttj_forward(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
                             void* out, void* stream_ptr) {
+  if (p && p->cp) return fail(TTTJ_ERR_INVALID, "forward: a split plan runs with tttj_forward_cp");
   return forward_impl(p, x, x_dtype, valid_mask, out, stream_ptr, nullptr);
+}
+
+extern "C" int tttj_forward_cp(tttj_plan* p, const void* x, int x_dtype, void* out,
+                               tttj_exchange_fn exchange, void* user, void* stream_ptr) {
+  if (!p || !p->cp) return fail(TTTJ_ERR_INVALID, "forward_cp: not a split plan");
+  if (!exchange) return fail(TTTJ_ERR_INVALID, "forward_cp: null exchange callback");
+  return forward_impl(p, x, x_dtype, nullptr, out, stream_ptr, nullptr, exchange, user);
 }
 
 extern "C" size_t tttj_debug_floats(const tttj_config* cfg) {
@@ -973,6 +1073,7 @@ extern "C" int tttj_forward_debug(tttj_plan* p, const void* x, int x_dtype,
                                   const uint8_t* valid_mask, void* out, int layer, int sequence,
                                   float* debug, void* stream) {
   if (!p || !debug) return fail(TTTJ_ERR_INVALID, "forward_debug: null argument");
+  if (p->cp) return fail(TTTJ_ERR_INVALID, "forward_debug: not available for split plans");
   if (layer < 0 || layer >= p->cfg.num_layers || sequence < 0 || sequence >= p->cfg.batch_size)
     return fail(TTTJ_ERR_INVALID, "forward_debug: layer %d / sequence %d out of range", layer,
                 sequence);
@@ -981,7 +1082,8 @@ extern "C" int tttj_forward_debug(tttj_plan* p, const void* x, int x_dtype,
 }
 
 static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t* valid_mask,
-                        void* out, void* stream_ptr, const DebugCapture* dbg) {
+                        void* out, void* stream_ptr, const DebugCapture* dbg,
+                        tttj_exchange_fn exchange, void* user) {
   if (!p || !x || !out) return fail(TTTJ_ERR_INVALID, "forward: null argument");
   if (x_dtype != TTTJ_DTYPE_F16 && x_dtype != TTTJ_DTYPE_F32)
     return fail(TTTJ_ERR_INVALID, "forward: x must be fp16 or fp32");
@@ -1046,7 +1148,7 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
     TTTJ_CUDA(tock());             \
   } while (0)
 
-  if (use_resident(p) && dbg == nullptr) {  // a capture always runs layer by layer
+  if (use_resident(p) && dbg == nullptr && !p->cp) {  // a capture always runs layer by layer
     // The whole stack in one launch: one CTA per sequence reads x and the mask directly.
     ResLaunch r = p->res;
     r.p.x = x;
@@ -1060,13 +1162,21 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   // Without a mask the plan is the all-valid one every time: built by the first such
   // forward, reused by the next ones (the reference caches the all-valid case too,
   // kernels/sequence_resident.py:173-192).
-  if (!(valid_mask == nullptr && p->plan_static))
+  if (!(valid_mask == nullptr && p->plan_static)) {
     TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
                                                     atc_item_rows(hp), ATC_BN, p->tp, s));
+    // A split plan's attention: the whole sequence's keys, this rank's query blocks.
+    if (p->cp)
+      TTTJ_TIMED(TTTJ_KCLASS_PLAN,
+                 plan_tokens_launch(nullptr, 1, p->cp_len, c.num_heads, c.causal,
+                                    atc_item_rows(hp), ATC_BN, p->tp_attn, s, p->cp_lo,
+                                    p->cp_lo + T));
+  }
   p->plan_static = valid_mask == nullptr;
+  const TokenPlan& tpa = p->cp ? p->tp_attn : p->tp;  // attention items and work counters
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,
-                              p->stats, p->pivot, p->parts, p->tp.counters, s));
+                              p->stats, p->pivot, p->parts, tpa.counters, s));
   // Capture buffers (floats) of tttj_forward_debug, filled at its layer.
   const size_t SD = (size_t)S * D, HSS = (size_t)c.num_heads * S * S;
   float* dg = dbg ? dbg->buf : nullptr;
@@ -1092,8 +1202,14 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
       TTTJ_CUDA(debug_scores_launch(d_q, d_k, dmap, bq, S, c.num_heads, hd, c.causal,
                                     1.0f / sqrtf((float)hd), d_sc, d_pr, s));
     }
+    if (p->cp) {
+      // Every rank of the split has written its rows' q|k|v; the exchange (enqueued on
+      // the stream by the caller) completes the whole sequence's before the attention.
+      const int xr = exchange(user, l, stream_ptr);
+      if (xr != 0) return fail(TTTJ_ERR_CUDA, "forward_cp: exchange failed at layer %d (%d)", l, xr);
+    }
     AtcParams ap = p->attn;
-    ap.work_counter = p->tp.counters + l;
+    ap.work_counter = tpa.counters + l;
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
                attention_tc_launch(p->attn_tm, ap, hp, c.causal, p->attn_grid, s));
     if (cap) TTTJ_CUDA(debug_gather_launch(p->ctx, 1, Qw, 0, D, hd, hp, dmap, bq, S, d_pv, s));

@@ -86,8 +86,10 @@ struct ResLaunch {
 };
 cudaError_t resident_launch(const ResLaunch& r, cudaStream_t stream);
 
+// Items for the query blocks starting in [q_lo, q_hi) only (defaults: all).
 cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
-                               int kv_block, const TokenPlan& plan, cudaStream_t stream);
+                               int kv_block, const TokenPlan& plan, cudaStream_t stream,
+                               int q_lo = 0, int q_hi = 0x7fffffff);
 cudaError_t ln_gather_launch(const void* x, int x_dtype, const int* packed_src, const int* rows_dev,
                              int rows_max, int D, float* resid, __half* x16, float2* stats,
                              float* pivot, int n_parts, int* counters, cudaStream_t stream);

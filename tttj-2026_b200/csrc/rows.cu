@@ -11,7 +11,8 @@ inline int ln_vpl(int D) { return (D + 255) / 256; }
 }  // namespace
 
 cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int causal, int q_block,
-                               int kv_block, const TokenPlan& plan, cudaStream_t stream) {
+                               int kv_block, const TokenPlan& plan, cudaStream_t stream, int q_lo,
+                               int q_hi) {
   const int nkeys = (S + kv_block - 1) / kv_block + 1;
   const size_t smem = sizeof(int) * (size_t)(2 * B + 1 + nkeys + 1);
   if (smem > 48 * 1024) {
@@ -20,7 +21,7 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
     if (e != cudaSuccess) return e;
   }
   return launch_pdl(plan_tokens_kernel, dim3(1), dim3(PLAN_THREADS), smem, stream, mask, B, S, H,
-                    causal, q_block, kv_block, plan);
+                    causal, q_block, kv_block, q_lo, q_hi, plan);
 }
 
 #define TTTJ_VPL_DISPATCH(VPL_EXPR, CALL) \

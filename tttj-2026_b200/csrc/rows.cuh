@@ -22,10 +22,13 @@
 
 namespace tttj {
 
-// Single-CTA plan.  Dynamic shared memory: (2*B + 1 + nkeys + 1) ints.
+// Single-CTA plan.  Dynamic shared memory: (2*B + 1 + nkeys + 1) ints.  Attention items
+// are listed for the query blocks starting in [q_lo, q_hi) of each sequence (a rank's
+// share of a sequence split across ranks; 0 and INT_MAX otherwise).
 __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t* __restrict__ mask,
                                                                    int B, int S, int H, int causal,
                                                                    int q_block, int kv_block,
+                                                                   int q_lo, int q_hi,
                                                                    TokenPlan plan) {
   griddep_wait();
   griddep_launch();
@@ -94,7 +97,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
     const int b = i / qt_max;
     const int qt = i - b * qt_max;
     const int len = cnt[b];
-    if (qt * q_block < len) {
+    if (qt * q_block < len && qt * q_block >= q_lo && qt * q_block < q_hi) {
       const int kv_end = causal ? min(len, (qt + 1) * q_block) : len;
       const int key = (kv_end + kv_block - 1) / kv_block;
       atomicAdd(&hist[key], H);
@@ -115,7 +118,7 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
     const int b = i / qt_max;
     const int qt = i - b * qt_max;
     const int len = cnt[b];
-    if (qt * q_block < len) {
+    if (qt * q_block < len && qt * q_block >= q_lo && qt * q_block < q_hi) {
       const int kv_end = causal ? min(len, (qt + 1) * q_block) : len;
       const int key = (kv_end + kv_block - 1) / kv_block;
       const int pos = atomicAdd(&hist[key], H);

@@ -93,6 +93,10 @@ def parse_args(argv=None):
                          "sequences of small layers); layerwise / resident: force one path")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline time budget")
+    ap.add_argument("--cp", type=int, default=1,
+                    help="context parallelism: groups of CP ranks each split one sequence at a "
+                         "time (tttj_2026_b200.context_parallel); for batches smaller than the "
+                         "GPU count, e.g. --config C4 --gpus 8 --cp 2")
     return ap.parse_args(argv)
 
 
@@ -351,6 +355,111 @@ def run_reference(args, rank: int, world: int):
     return 0
 
 
+def run_cp(args, rank: int, world: int, local_rank: int):
+    """--cp K: the ranks form world / K groups of K; each group takes its LPT share of the
+    batch's sequences and runs them one after another, each split across the group's
+    ranks (ContextParallelTransformer: token-sliced GEMMs, one q|k|v all-gather per
+    layer).  value = B * S * steps / max-over-ranks time; e2e adds, per sequence, the
+    H2D of its input and the D2H of the rank's output rows."""
+    import torch
+    import torch.distributed as dist
+
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    import optimized_transformer  # noqa: F401
+    import tttj_2026_b200 as tb
+    from tttj_2026_b200 import sharding
+    from tttj_2026_b200.context_parallel import ContextParallelTransformer
+
+    name, K = args.config, args.cp
+    if world % K:
+        raise SystemExit(f"--cp {K} must divide the number of ranks ({world})")
+    B, S = CONFIGS[name][0], CONFIGS[name][1]
+    cfg, model, x_full, mask_full = make_case(name, args.seed, dev)
+    groups = [dist.new_group(list(range(g * K, (g + 1) * K))) for g in range(world // K)]
+    gi = rank // K
+    lengths = sharding.lengths_of(mask_full, B, S)
+    mine = sharding.local_shard(lengths, cfg, gi, world // K)  # this group's sequences
+    cp = ContextParallelTransformer(model, groups[gi])
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    seqs = [(x_full[b:b + 1].contiguous(),
+             None if mask_full is None else mask_full[b:b + 1].contiguous()) for b in mine]
+
+    def step():
+        for xs, ms in seqs:
+            cp(xs, ms, gather=False)
+
+    def max_over_ranks(v: float) -> float:
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local_rank).start()
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step()
+            flush.zero_()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+        for a, b in ev:
+            a.record(stream)
+            step()
+            b.record(stream)
+            flush.zero_()
+        torch.cuda.synchronize(dev)
+        dist.barrier(device_ids=[local_rank])
+        total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev))
+        # e2e: every sequence's input in from pinned host memory, the rank's rows out.
+        hosts = [(xs.cpu().pin_memory(), None if ms is None else ms.cpu().pin_memory()) for xs, ms in seqs]
+        h2d = sum(h.numel() * h.element_size() + (0 if m is None else m.numel()) for h, m in hosts)
+        outs = []
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+        t0.record(stream)
+        d2h = 0
+        for _ in range(args.steps):
+            for hx, hm in hosts:
+                xs = hx.to(dev, non_blocking=True)
+                ms = None if hm is None else hm.to(dev, non_blocking=True)
+                _, _, rows = cp(xs, ms, gather=False)
+                outs.append(rows.to("cpu", non_blocking=True))
+            flush.zero_()
+        t1.record(stream)
+        torch.cuda.synchronize(dev)
+        d2h = sum(o.numel() * o.element_size() for o in outs[-len(hosts):]) if hosts else 0
+        e2e_ms = max_over_ranks(t0.elapsed_time(t1))
+        nb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
+        dist.all_reduce(nb)
+        launches = (5 * cfg.num_layers + 2) * len(seqs)
+    clk = clocks.stop()
+    if rank != 0:
+        return 0
+    value = B * S * args.steps / (total_ms / 1e3)
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+        "config": {"workload": workload_desc(name), "global_batch": B, "seq_len": S,
+                   "parallelism": f"cp{K} x dp{world // K} (each sequence split across {K} ranks, "
+                                  f"one q|k|v all-gather per layer; groups take LPT shares of "
+                                  f"the batch)",
+                   "l2": "flushed between steps (256 MiB write)",
+                   "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",
+                   "inputs": f"x~N(0,1), input seed {args.seed + 1}"},
+        "e2e": {"value": B * S * args.steps / (e2e_ms / 1e3), "unit": UNIT,
+                "h2d_bytes_per_step": int(nb[0].item()), "d2h_bytes_per_step": int(nb[1].item()),
+                "copies": "each rank copies its group's sequences in and its output rows out"},
+        "roofline": None, "cpu_baseline": None, "clocks": clk,
+        "gpu_launches": launches * args.steps, "launches_per_step": launches,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_b200(args, rank: int, world: int, local_rank: int):
     import torch
     import torch.distributed as dist
@@ -370,8 +479,8 @@ def run_b200(args, rank: int, world: int, local_rank: int):
     sel = torch.as_tensor(mine, device=dev, dtype=torch.long)
     x = x_full.index_select(0, sel).contiguous()
     mask = None if mask_full is None else mask_full.index_select(0, sel).contiguous()
-    b_local = len(mine)
-    cfg = tb.TransformerConfig(b_local, S, cfg_full.d_model, cfg_full.num_heads, cfg_full.ffn_dim,
+    b_local = len(mine)  # 0 when the batch has fewer sequences than ranks (the rank idles)
+    cfg = tb.TransformerConfig(max(b_local, 1), S, cfg_full.d_model, cfg_full.num_heads, cfg_full.ffn_dim,
                                cfg_full.num_layers, cfg_full.causal)
     opt = tb.make_optimized_transformer(model)
     opt.set_path(args.path)
@@ -502,13 +611,15 @@ def run_b200(args, rank: int, world: int, local_rank: int):
                     out_full.index_select(0, sel), opt(x, mask)))
 
         # ---- per-kernel-class timing inside real forwards ----
-        opt.set_kernel_timing(b_local, S, True)
-        for _ in range(args.steps):
-            opt(x, mask)
-            flush.zero_()
-        ktimes = opt.kernel_times(b_local, S)
-        opt.set_kernel_timing(b_local, S, False)
-        launches = opt.launches_per_forward(b_local, S)
+        ktimes, launches = {}, 0
+        if b_local:
+            opt.set_kernel_timing(b_local, S, True)
+            for _ in range(args.steps):
+                opt(x, mask)
+                flush.zero_()
+            ktimes = opt.kernel_times(b_local, S)
+            opt.set_kernel_timing(b_local, S, False)
+            launches = opt.launches_per_forward(b_local, S)
         opt.device_status()
     clk = clocks.stop()
 
@@ -627,6 +738,8 @@ def main(argv=None) -> int:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        if args.cp > 1:
+            return run_cp(args, rank, world, local_rank)
         return run_b200(args, rank, world, local_rank)
     finally:
         if world > 1:

@@ -321,6 +321,7 @@ int build_gemm(GemmLaunch* g, const void* a, int lda, const void* w, int ldw, co
   std::memset(g, 0, sizeof(*g));
   gemm_choose(rows, n, k, epi, num_sms, &g->bn, &g->pair);
   g->rbuf = gemm_choose_rbuf(g->bn, g->pair, k, epi, residual == out && ldr == ldo);
+  g->epiw = gemm_choose_epiw(g->bn, epi, g->rbuf);
   g->epi = epi;
   int rc = make_tmap(&g->tmA, a, (uint64_t)(rows > 0 ? rows : 1), (uint64_t)k, (uint64_t)lda, GEMM_BM);
   if (rc) return rc;

@@ -22,17 +22,18 @@ constexpr int STAGES_RB_PAIR_BN128 = 6;
 constexpr int STAGES_RB_BN128 = 5;
 constexpr int STAGES_RB_BN64 = 6;
 
-template <int BN, int EPI, int STAGES, bool PAIR, int RB = 0>
+template <int BN, int EPI, int STAGES, bool PAIR, int RB = 0, int EPIW = GEMM_EPI_WARPS>
 cudaError_t launch_t(const GemmLaunch& g, cudaStream_t stream) {
-  auto kern = gemm_tc_kernel<BN, EPI, STAGES, PAIR, RB>;
-  constexpr int smem = GemmSmem<BN, STAGES, PAIR, RB>::TOTAL;
+  auto kern = gemm_tc_kernel<BN, EPI, STAGES, PAIR, RB, EPIW>;
+  constexpr int smem = GemmSmem<BN, STAGES, PAIR, RB, EPIW>::TOTAL;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   static_assert(smem <= 232448, "GEMM shared memory exceeds the 227 KB per-CTA limit");
   if (PAIR)
-    return launch_pdl_cluster(kern, dim3(g.grid), dim3(GEMM_THREADS), smem, stream, 2, g.tmA,
-                              g.tmB, g.tmC, g.p);
-  return launch_pdl(kern, dim3(g.grid), dim3(GEMM_THREADS), smem, stream, g.tmA, g.tmB, g.tmC, g.p);
+    return launch_pdl_cluster(kern, dim3(g.grid), dim3(gemm_threads(EPIW)), smem, stream, 2,
+                              g.tmA, g.tmB, g.tmC, g.p);
+  return launch_pdl(kern, dim3(g.grid), dim3(gemm_threads(EPIW)), smem, stream, g.tmA, g.tmB,
+                    g.tmC, g.p);
 }
 
 template <int BN, int STAGES, bool PAIR>
@@ -52,6 +53,20 @@ cudaError_t launch_bn(const GemmLaunch& g, cudaStream_t stream) {
       return launch_t<BN, EPI_LN_FOLD, STAGES, PAIR>(g, stream);
     case EPI_LN_FOLD_GELU:
       return launch_t<BN, EPI_LN_FOLD_GELU, STAGES, PAIR>(g, stream);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+// The erf-GELU epilogues of 256-wide tiles with twelve epilogue warps.
+template <int STAGES, bool PAIR>
+cudaError_t launch_wide(const GemmLaunch& g, cudaStream_t stream) {
+  constexpr int W = GEMM_EPI_WARPS_WIDE;
+  switch (g.epi) {
+    case EPI_BIAS_GELU:
+      return launch_t<256, EPI_BIAS_GELU, STAGES, PAIR, 0, W>(g, stream);
+    case EPI_LN_FOLD_GELU:
+      return launch_t<256, EPI_LN_FOLD_GELU, STAGES, PAIR, 0, W>(g, stream);
     default:
       return cudaErrorInvalidValue;
   }
@@ -159,7 +174,22 @@ void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pai
   }
 }
 
+// Epilogue warps: twelve for the erf-GELU epilogues of 256-wide tiles, whose per-element
+// arithmetic makes the epilogue as long as or longer than the main loop at K <= 1024
+// (per-tile clock stamps: C5 ffn_in ~9.5k epilogue vs ~8.7k MMA clocks per tile, C2
+// ~9k vs ~4k); eight otherwise.  Measured same box: ffn_in C5 403 -> 381 us, C2 35.3 ->
+// 33.9 us; the LayerNorm fold alone (QKV) measured 1-3% slower with twelve.
+int gemm_choose_epiw(int bn, int epi, int rbuf) {
+  const bool gelu = epi == EPI_BIAS_GELU || epi == EPI_LN_FOLD_GELU;
+  return (gelu && bn == 256 && rbuf == 0) ? GEMM_EPI_WARPS_WIDE : GEMM_EPI_WARPS;
+}
+
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream) {
+  if (g.epiw == GEMM_EPI_WARPS_WIDE) {
+    if (g.bn != 256) return cudaErrorInvalidValue;
+    if (g.pair) return launch_wide<STAGES_PAIR_BN256, true>(g, stream);
+    return launch_wide<STAGES_BN256, false>(g, stream);
+  }
   if (g.rbuf) {
     if (g.rbuf != RBUF) return cudaErrorInvalidValue;
     if (g.pair && g.bn == 256) return launch_rbuf<256, STAGES_RB_PAIR_BN256, true>(g, stream);

@@ -37,26 +37,34 @@ namespace tttj {
 // owns RBUF 32 x 32 fp32 staging blocks into which TMA loads the residual chunks
 // RBUF - 1 chunks ahead of the one being drained (0: one staging block, the residual
 // prefetched one chunk ahead through registers).
-template <int BN, int STAGES, bool PAIR = false, int RBUF = 0>
+// EPIW: epilogue warps (GEMM_EPI_WARPS, or GEMM_EPI_WARPS_WIDE for fp16 outputs).
+template <int BN, int STAGES, bool PAIR = false, int RBUF = 0, int EPIW = GEMM_EPI_WARPS>
 struct GemmSmem {
   static constexpr int A_BYTES = GEMM_BM * GEMM_BK * 2;
   static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * GEMM_BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TILE_BYTES = STAGES * STAGE_BYTES;
   static constexpr int OUT_BUFS = RBUF > 0 ? RBUF : 1;
-  static constexpr int OUT_BYTES = GEMM_EPI_WARPS * GEMM_STAGE_OUT_BYTES * OUT_BUFS;
+  // Staging block per epilogue warp: 32 x 32 fp32, or 32 x 32 fp16 for the wide variant.
+  static constexpr int BLK_BYTES = EPIW == GEMM_EPI_WARPS ? GEMM_STAGE_OUT_BYTES : GEMM_STAGE_OUT_BYTES / 2;
+  static constexpr int OUT_BYTES = EPIW * BLK_BYTES * OUT_BUFS;
   // full / empty per stage, 2 + 2 accumulator barriers, drain, TMEM slot + abort flag,
   // one residual-load barrier per staging block.
-  static constexpr int BAR_BYTES = (2 * STAGES + 6 + GEMM_EPI_WARPS * RBUF) * 8 + 16;
+  static constexpr int BAR_BYTES = (2 * STAGES + 6 + EPIW * RBUF) * 8 + 16;
   // +1024 so the tile ring can be aligned to the 1024-byte swizzle atom.
   static constexpr int TOTAL = TILE_BYTES + OUT_BYTES + BAR_BYTES + 1024;
 };
 
-template <int BN, int EPI, int STAGES, bool PAIR, int RBUF = 0>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+template <int BN, int EPI, int STAGES, bool PAIR, int RBUF = 0, int EPIW = GEMM_EPI_WARPS>
+__global__ void __launch_bounds__(gemm_threads(EPIW), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const GemmParams p) {
-  using L = GemmSmem<BN, STAGES, PAIR, RBUF>;
+  using L = GemmSmem<BN, STAGES, PAIR, RBUF, EPIW>;
+  static_assert(EPIW == GEMM_EPI_WARPS ||
+                    (EPIW == GEMM_EPI_WARPS_WIDE && BN == 256 && RBUF == 0 &&
+                     EPI != EPI_BIAS_RESIDUAL && EPI != EPI_BIAS_RESIDUAL_F32 &&
+                     EPI != EPI_RESIDUAL_F32_STATS),
+                "12 epilogue warps serve the fp16-output epilogues of 256-wide tiles");
   static_assert(RBUF == 0 || RBUF >= 2, "residual staging: one block, or at least two");
   static_assert(RBUF == 0 || EPI == EPI_BIAS_RESIDUAL_F32 || EPI == EPI_RESIDUAL_F32_STATS,
                 "TMA residual loads serve the in-place fp32 residual epilogues");
@@ -101,10 +109,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar_accf + 8 * b, 1);
       // One arrival per epilogue warp of each CTA (a pair's leader counts both CTAs).
-      mbar_init(bar_acce + 8 * b, GEMM_EPI_WARPS * CTAS);
+      mbar_init(bar_acce + 8 * b, EPIW * CTAS);
     }
     mbar_init(bar_drain, 1);
-    for (int i = 0; i < GEMM_EPI_WARPS * RBUF; ++i) mbar_init(bar_res + 8 * i, 1);
+    for (int i = 0; i < EPIW * RBUF; ++i) mbar_init(bar_res + 8 * i, 1);
     *abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -272,14 +280,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     constexpr bool OUT_F32 = RES_F32;
     constexpr bool FOLD = EPI == EPI_LN_FOLD || EPI == EPI_LN_FOLD_GELU;
     const int quad = warp & 3;                  // TMEM lane quadrant this warp may access
-    const int col_half = (warp - 2) >> 2;       // which half of the tile's columns
+    const int col_half = (warp - 2) >> 2;       // which share of the tile's columns
     const int row_in_tile = quad * 32 + lane;
-    const uint32_t stage_out = sOut + (uint32_t)((warp - 2) * GEMM_STAGE_OUT_BYTES);
+    const uint32_t stage_out = sOut + (uint32_t)((warp - 2) * L::BLK_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
-    // This warp's columns of a tile are one contiguous run of BN/2: chunks
-    // col_half*(BN/64) .. +BN/64-1 of 32 columns each.
-    constexpr int CHUNKS = BN / 64;
+    // Eight epilogue warps: this warp's columns of a tile are one contiguous run of
+    // BN/2, chunks col_half*(BN/64) .. +BN/64-1 of 32 columns each.  Twelve: every third
+    // chunk, starting at chunk col_half (3, 3 and 2 chunks of a 256-wide tile).
+    constexpr int NPART = EPIW / 4;
+    constexpr int CHUNKS = EPIW == GEMM_EPI_WARPS ? BN / 64 : (BN / 32 + NPART - 1) / NPART;
     // Residual reads are the epilogue's long-latency operand.  Each warp asks L2 for
     // its rows' segment of the NEXT tile while the current one is drained, loads the
     // first chunk of the current tile before the accumulator is ready, and loads chunk
@@ -457,7 +467,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int cc = 0; cc < CHUNKS; ++cc) {
-        const int c = col_half * CHUNKS + cc;
+        const int c = EPIW == GEMM_EPI_WARPS ? col_half * CHUNKS + cc : col_half + NPART * cc;
+        if (EPIW != GEMM_EPI_WARPS && c >= BN / 32) break;  // warp-uniform
         const int col0 = n_blk * BN + c * 32;
         uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + (uint32_t)(c * 32), r);

@@ -57,6 +57,7 @@ struct GemmLaunch {
   int epi;   // GemmEpilogue
   int grid;  // persistent CTAs (even for pairs)
   int rbuf;  // fp32 residual staging blocks per epilogue warp fed by TMA (0: none)
+  int epiw;  // epilogue warps (GEMM_EPI_WARPS or GEMM_EPI_WARPS_WIDE)
 };
 
 // Tile shape for a GEMM of `rows` x `n` x `k` with epilogue `epi` on `num_sms` SMs:
@@ -67,6 +68,8 @@ void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pai
 // Residual staging blocks (gemm_tc.cuh RBUF) for a GEMM with that tile shape: 2 for the
 // in-place fp32 residual epilogues with short K, else 0.
 int gemm_choose_rbuf(int bn, int pair, int k, int epi, bool in_place);
+// Epilogue warps for a GEMM with that tile width, epilogue and residual staging.
+int gemm_choose_epiw(int bn, int epi, int rbuf);
 cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
 // tcgen05 attention for a head-dim layout of 32, 64, 128 or 256 (plan with q_block

@@ -77,6 +77,10 @@ constexpr int GEMM_BK = 64;
 constexpr int GEMM_EPI_WARPS = 8;  // two per TMEM lane quadrant, each owning half the columns
 constexpr int GEMM_THREADS = 64 + 32 * GEMM_EPI_WARPS;
 constexpr int GEMM_STAGE_OUT_BYTES = 32 * 32 * 4;  // per-warp staging: 32 rows x 32 fp32
+// fp16-output epilogues on 256-wide tiles may run 12 epilogue warps (three per TMEM lane
+// quadrant, every third 32-column chunk each), staging 32 rows x 32 fp16 per warp.
+constexpr int GEMM_EPI_WARPS_WIDE = 12;
+constexpr int gemm_threads(int epi_warps) { return 64 + 32 * epi_warps; }
 
 // tcgen05 attention: work items of 2 query tiles x 128 rows (one tile at head_dim 256),
 // 128-key KV tiles.

@@ -385,7 +385,10 @@ int check_config(const tttj_config* c) {
   if (T * widest >= (1ll << 40) ||
       T >= (1ll << 31) - 256)
     return fail(TTTJ_ERR_INVALID, "batch_size*seq_len too large");
-  const long long plan_smem = 4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATC_BN - 1) / ATC_BN + 1);
+  // Token plan shared memory (rows.cuh plan_tokens_kernel): ints plus mask staging.
+  const long long plan_smem =
+      4ll * (2ll * c->batch_size + 3 + (c->seq_len + ATC_BN - 1) / ATC_BN + 1 + 3) +
+      512ll * (PLAN_THREADS / 32);
   if (plan_smem > 200 * 1024) return fail(TTTJ_ERR_INVALID, "batch_size/seq_len too large for the token plan");
   return TTTJ_OK;
 }

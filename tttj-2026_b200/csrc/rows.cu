@@ -14,7 +14,8 @@ cudaError_t plan_tokens_launch(const uint8_t* mask, int B, int S, int H, int cau
                                int kv_block, const TokenPlan& plan, cudaStream_t stream, int q_lo,
                                int q_hi) {
   const int nkeys = (S + kv_block - 1) / kv_block + 1;
-  const size_t smem = sizeof(int) * (size_t)(2 * B + 1 + nkeys + 1);
+  const size_t ints = ((size_t)(2 * B + 1 + nkeys + 1) + 3) & ~(size_t)3;
+  const size_t smem = sizeof(int) * ints + 512 * (PLAN_THREADS / 32);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(plan_tokens_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

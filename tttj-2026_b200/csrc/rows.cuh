@@ -22,7 +22,24 @@
 
 namespace tttj {
 
-// Single-CTA plan.  Dynamic shared memory: (2*B + 1 + nkeys + 1) ints.  Attention items
+// Number of non-zero bytes among 16 mask bytes.
+__device__ __forceinline__ int mask16_count(uint4 m) {
+  int c = 0;
+  const uint32_t w[4] = {m.x, m.y, m.z, m.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    // Each byte -> 1 if non-zero: fold the byte's bits into its lowest bit.
+    uint32_t v = w[i];
+    v |= v >> 4;
+    v |= v >> 2;
+    v |= v >> 1;
+    c += __popc(v & 0x01010101u);
+  }
+  return c;
+}
+
+// Single-CTA plan.  Dynamic shared memory: (2*B + 1 + nkeys + 1) ints rounded up to 16
+// bytes, then 512 bytes of mask staging per warp.  Attention items
 // are listed for the query blocks starting in [q_lo, q_hi) of each sequence (a rank's
 // share of a sequence split across ranks; 0 and INT_MAX otherwise).
 __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t* __restrict__ mask,
@@ -33,20 +50,30 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
   griddep_wait();
   griddep_launch();
   extern __shared__ int sh[];
+  const int nkeys = (S + kv_block - 1) / kv_block + 1;
   int* cnt = sh;             // [B]
   int* off = sh + B;         // [B+1]
   int* hist = sh + 2 * B + 1;  // [nkeys+1]
-  const int nkeys = (S + kv_block - 1) / kv_block + 1;
+  // Per-warp 512-byte mask staging slots after the ints (16-byte aligned).
+  uint4* stage = reinterpret_cast<uint4*>(sh + ((2 * B + 1 + nkeys + 1 + 3) & ~3));
   const int warp = warp_id();
   const int lane = lane_id();
   const int nwarps = blockDim.x >> 5;
 
   for (int i = threadIdx.x; i <= nkeys; i += blockDim.x) hist[i] = 0;
   for (int i = threadIdx.x; i < PLAN_COUNTERS; i += blockDim.x) plan.counters[i] = 0;
+  // Mask bytes are read 16 per lane (512 positions per warp step) when the rows are
+  // 16-byte aligned, else one per lane.
+  const bool vec_mask = mask != nullptr && (S % 16) == 0 &&
+                        (reinterpret_cast<uintptr_t>(mask) & 15) == 0;
   for (int b = warp; b < B; b += nwarps) {
     int c = 0;
     if (mask == nullptr) {
       c = S;
+    } else if (vec_mask) {
+      const uint4* row = reinterpret_cast<const uint4*>(mask + (size_t)b * S);
+      for (int i = lane; i < S / 16; i += 32) c += mask16_count(row[i]);
+      for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffff, c, o);
     } else {
       for (int s = lane; s < S; s += 32) c += mask[(size_t)b * S + s] != 0;
       for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffff, c, o);
@@ -69,8 +96,41 @@ __global__ void __launch_bounds__(PLAN_THREADS) plan_tokens_kernel(const uint8_t
   }
   if (threadIdx.x == 0) plan.seq_off[B] = off[B];
 
-  // Packed row maps: a warp per sequence, ballot-scan over 32 positions at a time.
-  for (int b = warp; b < B; b += nwarps) {
+  // Packed row maps: a warp per sequence, ballot scan over 32 positions at a time (so
+  // every map store is one coalesced 128-byte row).  Vector path: each 512-position step
+  // of the sequence's mask is first staged in this warp's shared-memory slot, 16 bytes
+  // per lane, so the scan reads shared memory instead of waiting on one global load per
+  // 32 positions.
+  for (int b = warp; b < B && vec_mask; b += nwarps) {
+    int running = off[b];
+    const uint4* row = reinterpret_cast<const uint4*>(mask + (size_t)b * S);
+    uint8_t* slot = reinterpret_cast<uint8_t*>(stage) + warp * 512;
+    for (int s0 = 0; s0 < S; s0 += 512) {
+      const int sv = s0 + 16 * lane;
+      reinterpret_cast<uint4*>(slot)[lane] = sv < S ? row[sv / 16] : make_uint4(0u, 0u, 0u, 0u);
+      __syncwarp();
+#pragma unroll 4
+      for (int k = 0; k < 16; ++k) {
+        const int s = s0 + 32 * k + lane;
+        const bool in = s < S;
+        const bool v = in && slot[32 * k + lane] != 0;
+        const unsigned bal = __ballot_sync(0xffffffff, v);
+        const int rank = __popc(bal & ((1u << lane) - 1u));
+        if (in) {
+          const int tok = b * S + s;
+          if (v) {
+            plan.packed_src[running + rank] = tok;
+            plan.dst_map[tok] = running + rank;
+          } else {
+            plan.dst_map[tok] = -1;
+          }
+        }
+        running += __popc(bal);
+      }
+      __syncwarp();
+    }
+  }
+  for (int b = warp; b < B && !vec_mask; b += nwarps) {
     int running = off[b];
     for (int s0 = 0; s0 < S; s0 += 32) {
       const int s = s0 + lane;

@@ -285,6 +285,10 @@ __global__ void __launch_bounds__(gemm_threads(EPIW), 1)
     const uint32_t stage_out = sOut + (uint32_t)((warp - 2) * L::BLK_BYTES);
     int acc = 0;
     uint32_t acc_phase = 0;
+    // fp16-output staging halves per warp block (32 x 32 x 2 B each), and the TMA stores
+    // this warp issued from them.
+    constexpr int NSB16 = OUT_F32 ? 1 : (L::BLK_BYTES / 2048 >= 2 ? 2 : 1);
+    uint32_t out_seq = 0;
     // Eight epilogue warps: this warp's columns of a tile are one contiguous run of
     // BN/2, chunks col_half*(BN/64) .. +BN/64-1 of 32 columns each.  Twelve: every third
     // chunk, starting at chunk col_half (3, 3 and 2 chunks of a 256-wide tile).
@@ -643,8 +647,18 @@ __global__ void __launch_bounds__(gemm_threads(EPIW), 1)
                                 pack_half2(d[8 * q + 6], d[8 * q + 7]));
         }
         if (full_tile) {
-          // The previous TMA store from this warp's staging block must have read it.
-          if (lane == 0) bulk_wait_read_all();
+          // fp16 outputs take 2 KB of the warp's staging block per chunk: with a 4 KB
+          // block the chunks alternate between its halves, and a half is rewritten once
+          // the store before last (which read it) is done reading.  Otherwise the
+          // previous TMA store from the block must have read it.
+          const uint32_t sbuf =
+              OUT_F32 ? stage_out : stage_out + (uint32_t)((out_seq % NSB16) * 2048);
+          if (lane == 0) {
+            if (NSB16 > 1)
+              bulk_wait_read_1();
+            else
+              bulk_wait_read_all();
+          }
           __syncwarp();
           if (OUT_F32) {
             // 32 rows x 128 B, 128-byte swizzle: 16-byte chunk j of row r at j ^ (r % 8).
@@ -659,7 +673,7 @@ __global__ void __launch_bounds__(gemm_threads(EPIW), 1)
             }
           } else {
             // 32 rows x 64 B, 64-byte swizzle: 16-byte chunk j of row r at j ^ ((r / 2) % 4).
-            const uint32_t rbase = stage_out + (uint32_t)(lane * 64);
+            const uint32_t rbase = sbuf + (uint32_t)(lane * 64);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const uint32_t dst = rbase + (uint32_t)(((j ^ ((lane >> 1) & 3)) & 3) << 4);
@@ -674,9 +688,10 @@ __global__ void __launch_bounds__(gemm_threads(EPIW), 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, stage_out, col0, row0);
+            tma_store_2d(&tmC, sbuf, col0, row0);
             bulk_commit();
           }
+          ++out_seq;
         } else if (row_ok) {
           if (OUT_F32) {
             float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) +

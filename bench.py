@@ -380,15 +380,18 @@ def run_cp(args, rank: int, world: int, local_rank: int):
     gi = rank // K
     lengths = sharding.lengths_of(mask_full, B, S)
     mine = sharding.local_shard(lengths, cfg, gi, world // K)  # this group's sequences
-    cp = ContextParallelTransformer(model, groups[gi])
+    # Each sequence's split forward is captured once into a CUDA graph and replayed; its
+    # valid length is known on the host (no read-back of the mask per call).
+    cp = ContextParallelTransformer(model, groups[gi], graphs=True)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     seqs = [(x_full[b:b + 1].contiguous(),
              None if mask_full is None else mask_full[b:b + 1].contiguous()) for b in mine]
+    lens = [int(lengths[b]) for b in mine]
 
     def step():
-        for xs, ms in seqs:
-            cp(xs, ms, gather=False)
+        for (xs, ms), n in zip(seqs, lens):
+            cp(xs, ms, gather=False, length=n)
 
     def max_over_ranks(v: float) -> float:
         t = torch.tensor([v], dtype=torch.float64, device=dev)
@@ -422,10 +425,10 @@ def run_cp(args, rank: int, world: int, local_rank: int):
         t0.record(stream)
         d2h = 0
         for _ in range(args.steps):
-            for hx, hm in hosts:
+            for (hx, hm), n in zip(hosts, lens):
                 xs = hx.to(dev, non_blocking=True)
                 ms = None if hm is None else hm.to(dev, non_blocking=True)
-                _, _, rows = cp(xs, ms, gather=False)
+                _, _, rows = cp(xs, ms, gather=False, length=n)
                 outs.append(rows.to("cpu", non_blocking=True))
             flush.zero_()
         t1.record(stream)
@@ -435,6 +438,7 @@ def run_cp(args, rank: int, world: int, local_rank: int):
         nb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
         dist.all_reduce(nb)
         launches = (5 * cfg.num_layers + 2) * len(seqs)
+    cp.close()  # the graphs hold NCCL calls: released before the process group
     clk = clocks.stop()
     if rank != 0:
         return 0
@@ -445,8 +449,9 @@ def run_cp(args, rank: int, world: int, local_rank: int):
         "scaling": "strong", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
         "config": {"workload": workload_desc(name), "global_batch": B, "seq_len": S,
                    "parallelism": f"cp{K} x dp{world // K} (each sequence split across {K} ranks, "
-                                  f"one q|k|v all-gather per layer; groups take LPT shares of "
-                                  f"the batch)",
+                                  f"one q|k|v all-gather per layer, each sequence's split "
+                                  f"forward replayed from a CUDA graph; groups take LPT shares "
+                                  f"of the batch)",
                    "l2": "flushed between steps (256 MiB write)",
                    "weights": f"default nn.Linear/LayerNorm init, torch.manual_seed({args.seed})",
                    "inputs": f"x~N(0,1), input seed {args.seed + 1}"},

@@ -5,7 +5,8 @@ world size 2 puts every rank's q|k|v rows at their sequence positions -- and the
 decomposition itself, restated on the fp32 oracle: token-sliced projections plus
 attention of a rank's queries over the gathered keys equal the whole forward.
 GPU (two devices, NCCL): ``ContextParallelTransformer`` against the single-GPU module
-and the fp32 oracle.
+and the fp32 oracle, eager and replayed from CUDA graphs (identical outputs; the third
+case leaves one rank without rows).
 """
 import multiprocessing as mp
 import os
@@ -188,17 +189,23 @@ def _gpu_rank_main(rank, world, port, q):
             mask = torch.arange(3072, device=dev)[None, :] < length
             x = x.masked_fill(~mask[..., None], 0)
             cp = ContextParallelTransformer(model, None)
+            cpg = ContextParallelTransformer(model, None, graphs=True)
             single = tbr.make_optimized_transformer(model)
             with torch.inference_mode():
                 out = cp(x, mask)
                 again = cp(x, mask)
+                # graph replays (captured on the first call), the length given by the caller
+                g1 = cpg(x, mask, length=length)
+                g2 = cpg(x, mask, length=length)
                 ref1 = single(x, mask)
                 ref = forward_fp32_per_sequence(state_dict_fp32(model, dev), cfg, x.float(), mask)
             torch.cuda.synchronize(dev)
+            cpg.close()
             r = gate(ref, out, mask)
             d = float((out.float() - ref1.float()).abs().max())
             results.append((causal, length, r.passed, r.max_abs, r.mean_abs, d,
-                            bool(torch.equal(out, again))))
+                            bool(torch.equal(out, again) and torch.equal(out, g1) and
+                                 torch.equal(out, g2))))
         q.put((rank, results))
     finally:
         dist.destroy_process_group()

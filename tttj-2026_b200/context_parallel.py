@@ -21,6 +21,10 @@ no multi-GPU path; its long-sequence answer on one GPU is query-chunked attentio
   for CPU tensors), enqueued on the current stream.
 * ``ContextParallelTransformer`` runs a split forward through the C ABI
   (``tttj_plan_create_cp`` / ``tttj_forward_cp``), calling the exchange once per layer.
+  With ``graphs=True`` each (valid length, dtype) is captured once into a CUDA graph --
+  the forward's kernels and its per-layer all-gathers -- and replayed: the eager forward
+  re-enters Python at every layer's exchange, and at C4's shape (~0.1 ms of device work
+  per layer and rank) that host time can set the pace instead of the GPUs.
 """
 from __future__ import annotations
 
@@ -146,7 +150,7 @@ class ContextParallelTransformer(nn.Module):
     LayerNorm-folded once, as ``make_optimized_transformer`` does).
     """
 
-    def __init__(self, parameter_model: nn.Module, group=None):
+    def __init__(self, parameter_model: nn.Module, group=None, graphs: bool = False):
         super().__init__()
         import torch.distributed as dist
         from .model import B200Transformer
@@ -159,6 +163,18 @@ class ContextParallelTransformer(nn.Module):
         self.world = dist.get_world_size(group)
         self._plans: dict[tuple[int, int, int, int], _CpPlan] = {}
         self._exchange_error: Optional[BaseException] = None
+        self.graphs = graphs
+        # (length, dtype) -> (graph, static input rows, static output rows);
+        # ("idle", length) -> (graph, buffer) for a rank without rows
+        self._graphs: dict = {}
+
+    def close(self) -> None:
+        """Release the captured graphs (they hold NCCL calls: release them before
+        ``destroy_process_group``) and the split plans."""
+        self._graphs.clear()
+        for plan in self._plans.values():
+            plan.close()
+        self._plans.clear()
 
     def shares(self, length: int) -> list[tuple[int, int]]:
         hd = self.config.d_model // self.config.num_heads
@@ -175,14 +191,87 @@ class ContextParallelTransformer(nn.Module):
             self._plans[key] = plan
         return plan
 
+    def _run(self, plan: _CpPlan, xl: torch.Tensor, out_local: torch.Tensor, slot: int) -> None:
+        """One split forward of the rank's rows xl into out_local on the current stream,
+        the exchange called back once per layer."""
+        stream = torch.cuda.current_stream(self.device)
+
+        def exchange(_user, _layer, _stream):
+            try:
+                allgather_shares(plan.workspace, plan.qkv_offset, plan.row_bytes, slot,
+                                 self.group)
+                return 0
+            except BaseException as e:  # reported after the C call returns
+                self._exchange_error = e
+                return 1
+
+        cb = _lib.EXCHANGE_FN(exchange)
+        rc = _lib.lib().tttj_forward_cp(plan.handle, ctypes.c_void_p(xl.data_ptr()),
+                                        _lib.DTYPE_F16 if xl.dtype == torch.float16 else _lib.DTYPE_F32,
+                                        ctypes.c_void_p(out_local.data_ptr()), cb, None,
+                                        ctypes.c_void_p(stream.cuda_stream))
+        if self._exchange_error is not None:
+            err, self._exchange_error = self._exchange_error, None
+            raise RuntimeError("context-parallel exchange failed") from err
+        _lib.check(rc, "forward_cp")
+
+    def _graph(self, plan: _CpPlan, length: int, rows: int, dtype, slot: int):
+        """The captured split forward for (length, dtype): on its first use an eager
+        forward (it builds the split plan's token plans, which replays reuse, and brings
+        up the group's communicator), then the capture."""
+        key = (length, dtype)
+        entry = self._graphs.get(key)
+        if entry is None:
+            static_x = torch.zeros((rows, self.config.d_model), dtype=dtype, device=self.device)
+            static_out = torch.zeros_like(static_x)
+            self._run(plan, static_x, static_out, slot)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self._run(plan, static_x, static_out, slot)
+            entry = (graph, static_x, static_out)
+            self._graphs[key] = entry
+        return entry
+
+    def _idle(self, length: int, slot: int) -> None:
+        """A rank without rows (a sequence shorter than one work item per rank) still
+        takes part in every layer's exchange, with the same collectives in the same
+        order as its peers: eagerly, or -- with graphs -- an eager pass, a captured one
+        and a replay on the first call for a length (what a peer's _graph and replay
+        run), a replay afterwards."""
+        row_bytes = 3 * self._qkv_width() * 2
+        if not self.graphs:
+            buf = torch.zeros(slot * self.world * row_bytes, dtype=torch.uint8, device=self.device)
+            for _ in range(self.config.num_layers):
+                allgather_shares(buf, 0, row_bytes, slot, self.group)
+            return
+        key = ("idle", length)
+        entry = self._graphs.get(key)
+        if entry is None:
+            buf = torch.zeros(slot * self.world * row_bytes, dtype=torch.uint8, device=self.device)
+            for _ in range(self.config.num_layers):
+                allgather_shares(buf, 0, row_bytes, slot, self.group)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(self.config.num_layers):
+                    allgather_shares(buf, 0, row_bytes, slot, self.group)
+            entry = (graph, buf)
+            self._graphs[key] = entry
+        entry[0].replay()
+
     def forward(self, x: torch.Tensor, valid_token_mask: Optional[torch.Tensor] = None,
-                gather: bool = True):
+                gather: bool = True, length: Optional[int] = None):
+        """``length``: the number of valid tokens when the caller knows it (skips reading
+        the mask back to the host, which waits for the device)."""
         import torch.distributed as dist
 
         if x.dim() != 3 or x.shape[0] != 1 or x.shape[2] != self.config.d_model:
             raise ValueError(f"x must be [1, S, {self.config.d_model}], got {tuple(x.shape)}")
         S = x.shape[1]
-        if valid_token_mask is None:
+        if length is not None:
+            length = int(length)
+            if not 0 <= length <= S:
+                raise ValueError(f"length {length} outside [0, {S}]")
+        elif valid_token_mask is None:
             length = S
         else:
             m = valid_token_mask.reshape(-1).to(torch.bool)
@@ -192,36 +281,19 @@ class ContextParallelTransformer(nn.Module):
         shares = self.shares(length)
         slot = max(hi - lo for lo, hi in shares)
         lo, hi = shares[self.rank]
-        out_local = x.new_zeros((hi - lo, x.shape[2]))
         if hi > lo:
             plan = self._plan(length, lo, hi, slot * self.world)
-            xl = x[0, lo:hi].contiguous()
-            stream = torch.cuda.current_stream(self.device)
-
-            def exchange(_user, _layer, _stream):
-                try:
-                    allgather_shares(plan.workspace, plan.qkv_offset, plan.row_bytes, slot,
-                                     self.group)
-                    return 0
-                except BaseException as e:  # reported after the C call returns
-                    self._exchange_error = e
-                    return 1
-
-            cb = _lib.EXCHANGE_FN(exchange)
-            rc = _lib.lib().tttj_forward_cp(plan.handle, ctypes.c_void_p(xl.data_ptr()),
-                                            _lib.DTYPE_F16 if x.dtype == torch.float16 else _lib.DTYPE_F32,
-                                            ctypes.c_void_p(out_local.data_ptr()), cb, None,
-                                            ctypes.c_void_p(stream.cuda_stream))
-            if self._exchange_error is not None:
-                err, self._exchange_error = self._exchange_error, None
-                raise RuntimeError("context-parallel exchange failed") from err
-            _lib.check(rc, "forward_cp")
+            if self.graphs:
+                graph, static_x, static_out = self._graph(plan, length, hi - lo, x.dtype, slot)
+                static_x.copy_(x[0, lo:hi])
+                graph.replay()
+                out_local = static_out.clone()
+            else:
+                out_local = x.new_zeros((hi - lo, x.shape[2]))
+                self._run(plan, x[0, lo:hi].contiguous(), out_local, slot)
         else:
-            # A rank without rows still takes part in every layer's exchange.
-            buf = torch.zeros(slot * self.world * 3 * self._qkv_width() * 2, dtype=torch.uint8,
-                              device=self.device)
-            for _ in range(self.config.num_layers):
-                allgather_shares(buf, 0, 3 * self._qkv_width() * 2, slot, self.group)
+            out_local = x.new_zeros((0, x.shape[2]))
+            self._idle(length, slot)
         if not gather:
             return lo, hi, out_local
         pad = x.new_zeros((slot, x.shape[2]))

@@ -1117,18 +1117,26 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
     }
   }
   // The workspace belongs to the plan: a forward on another stream than the previous
-  // one first waits for the previous one.
-  if (p->has_last && s != p->last_stream) TTTJ_CUDA(cudaStreamWaitEvent(s, p->done, 0));
+  // one first waits for the previous one.  A forward captured into a CUDA graph skips
+  // this ordering (an event recorded outside the capture cannot be waited on inside
+  // it): the capturing caller orders the capture after earlier work (torch.cuda.graph
+  // synchronises the device first) and its replays after each other.
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  TTTJ_CUDA(cudaStreamIsCapturing(s, &capture));
+  const bool capturing = capture != cudaStreamCaptureStatusNone;
+  if (!capturing && p->has_last && s != p->last_stream)
+    TTTJ_CUDA(cudaStreamWaitEvent(s, p->done, 0));
   struct DoneRecord {  // record completion on every return path after launches began
     tttj_plan* p;
     cudaStream_t s;
+    bool active;
     ~DoneRecord() {
-      if (cudaEventRecord(p->done, s) == cudaSuccess) {
+      if (active && cudaEventRecord(p->done, s) == cudaSuccess) {
         p->last_stream = s;
         p->has_last = true;
       }
     }
-  } done_record{p, s};
+  } done_record{p, s, !capturing};
 
   // Per-class timing: an event pair around every launch when enabled.
   if (p->timing) {

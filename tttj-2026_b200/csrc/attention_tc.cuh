@@ -137,6 +137,10 @@ __device__ __forceinline__ uint64_t atc_desc_v(uint32_t addr) {
                   : desc_mnmajor_sw128(addr, AtcSmem<HD>::BOX_BYTES, 1024);
 }
 
+#ifndef ATC_P_EARLY
+#define ATC_P_EARLY 2
+#endif
+
 template <int HD, bool CAUSAL>
 __global__ void __launch_bounds__(ATC_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const AtcParams p) {
@@ -510,27 +514,34 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         const float base = (m_run == -INFINITY) ? 0.f : m_run;
         const float2 sc2 = make_float2(scale, scale), nb2 = make_float2(-base, -base);
         unsigned long long ps2[2] = {0ull, 0ull};  // partial row sums, f32x2 pairs
-        // P as fp16 pairs (128 keys -> 64 packed registers, each replacing two scores)
-        // computed before waiting for the previous P V, so the exponentials overlap it.
-        // One pair in four takes its exponentials from the FMA pipe (exp2_fma2): the
-        // MUFU (16 per clock per SM) is the tighter resource at head_dim 64.
-        uint32_t pk[64];
+        // P as fp16 pairs (128 keys -> 64 packed registers, each replacing two scores),
+        // in four chunks of 16 pairs; the first ATC_P_EARLY chunks are computed before
+        // waiting for the previous P V, so their exponentials overlap it, the rest after
+        // it, each stored as soon as it is ready (fewer live registers).  One pair in
+        // four takes its exponentials from the FMA pipe (exp2_fma2): the MUFU (16 per
+        // clock per SM) is the tighter resource at head_dim 64.
+        uint32_t pk[4][16];
+        auto exp_chunk = [&](int q) {
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float2 x = ffma2(make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])),
-                                 sc2, nb2);
-          float p0, p1;
-          if ((c & 3) == 3) {
-            const float2 e = exp2_fma2(x);
-            p0 = e.x;
-            p1 = e.y;
-          } else {
-            p0 = ex2_approx(x.x);
-            p1 = ex2_approx(x.y);
+          for (int cc = 0; cc < 16; ++cc) {
+            const int c = q * 16 + cc;
+            const float2 x = ffma2(make_float2(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1])),
+                                   sc2, nb2);
+            float p0, p1;
+            if ((c & 3) == 3) {
+              const float2 e = exp2_fma2(x);
+              p0 = e.x;
+              p1 = e.y;
+            } else {
+              p0 = ex2_approx(x.x);
+              p1 = ex2_approx(x.y);
+            }
+            ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
+            pk[q][cc] = pack_half2(p0, p1);
           }
-          ps2[c & 1] = add2p(ps2[c & 1], pk2(p0, p1));
-          pk[c] = pack_half2(p0, p1);
-        }
+        };
+#pragma unroll
+        for (int q = 0; q < ATC_P_EARLY; ++q) exp_chunk(q);
         // P(j) replaces P(j-1) in the P buffer, and O is rescaled below: P V(j-1) must
         // be complete.  (It was issued when this thread published P(j-1); completion
         // number pv_before + j - 1 of pv_done.  P V(j) cannot exist yet, and completion
@@ -547,10 +558,8 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         }
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          uint32_t chunk[16];
-#pragma unroll
-          for (int c = 0; c < 16; ++c) chunk[c] = pk[q * 16 + c];
-          tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), chunk);
+          if (q >= ATC_P_EARLY) exp_chunk(q);
+          tmem_st_32x32b_x16(p_addr + (uint32_t)(q * 16), pk[q]);
         }
         const float2 rs2 = upk2(add2p(ps2[0], ps2[1]));
         l_run = l_run * alpha + (rs2.x + rs2.y);

@@ -445,14 +445,19 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
         ok = false;
         break;
       }
-      const AtcItem w = info[qb];
-      if (w.n_kv < 0) break;  // no more items
-      mbar_arrive(bar_q_empty + 8 * qb);  // this thread no longer needs the info slot
+      // The item's fields as scalars (a copy of the whole struct, indexed by the
+      // run-time tile, would live in local memory).
+      const AtcItem& wi = info[qb];
+      if (wi.n_kv < 0) break;  // no more items
       const int tq = atc_query_tile<NT>(t, k);  // query tile of this item on this side
-      const int n = w.n[tq];
+      const int n = tq == 0 ? wi.n[0] : wi.n[1];
+      const int kv_end = tq == 0 ? wi.kv_end[0] : wi.kv_end[1];
+      struct {
+        int seq0, len, q0, h;
+      } w = {wi.seq0, wi.len, wi.q0, wi.h};
+      mbar_arrive(bar_q_empty + 8 * qb);  // this thread no longer needs the info slot
       if (n == 0) continue;
       const int qrow = w.q0 + tq * ATC_BM + row;  // query index inside the sequence
-      const int kv_end = w.kv_end[tq];
       float m_run = -INFINITY;  // running max (log2 domain) used as the exp base
       float l_run = 0.f;
       for (int j = 0; j < n; ++j) {

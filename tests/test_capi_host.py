@@ -162,12 +162,12 @@ STATS, FOLD, FOLD_GELU, RES_F32 = 4, 5, 6, 3
         ("C2/2 out_proj", 4096, 512, 512, STATS, (64, 0)),
         ("C2/4 ffn_out", 2048, 512, 2048, STATS, (64, 0)),
         ("C2/8 ffn_out", 1024, 512, 2048, STATS, (64, 0)),
-        # C4 / C5: CTA pairs where the main loop dominates, not under the GELU epilogue
+        # C4 / C5: CTA pairs where the main loop dominates (K >= 1024 and many waves)
         ("C4 qkv", 32768, 2304, 768, FOLD, (256, 0)),
         ("C4 ffn_out", 32768, 768, 3072, STATS, (256, 1)),
         ("C5 qkv", 65536, 3072, 1024, FOLD, (256, 1)),
         ("C5 out_proj", 65536, 1024, 1024, STATS, (256, 1)),
-        ("C5 ffn_in", 65536, 4096, 1024, FOLD_GELU, (256, 0)),
+        ("C5 ffn_in", 65536, 4096, 1024, FOLD_GELU, (256, 1)),
         ("C5 ffn_out", 65536, 1024, 4096, STATS, (256, 1)),
         # small shapes fall back to narrow single-CTA tiles
         ("C1 ffn_out", 256, 256, 1024, RES_F32, (64, 0)),

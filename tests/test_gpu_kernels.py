@@ -18,7 +18,8 @@ def _close(out, ref, atol, rtol):
 
 
 @pytest.mark.parametrize("M,N,K", [(128, 128, 64), (300, 768, 256), (1000, 512, 512),
-                                   (4096, 2048, 512), (2048, 1024, 4096), (77, 1536, 1024)])
+                                   (4096, 2048, 512), (2048, 1024, 4096), (77, 1536, 1024),
+                                   (8192, 4096, 1024)])  # CTA pairs, 12 epilogue warps (gelu)
 @pytest.mark.parametrize("epilogue", ["bias", "gelu", "residual", "residual_f32"])
 def test_linear_matches_torch(M, N, K, epilogue):
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N * 3 + K)

@@ -162,15 +162,15 @@ void gemm_choose(int rows, int n, int k, int epi, int num_sms, int* bn, int* pai
   *bn = gemm_choose_bn(rows, n, num_sms);
   // CTA pairs (256-row tiles) cut each SM's operand traffic by a third and deepen the
   // ring, which pays where the main loop dominates: long K, and enough tiles that the
-  // doubled tile size does not cost a partial wave.  They lose (measured) where the
-  // erf-GELU epilogue is the longer stage, and on short-K / few-wave GEMMs where the
-  // pair's coupling and ramp-up outweigh the feed.
-  const bool gelu = epi == EPI_BIAS_GELU || epi == EPI_LN_FOLD_GELU;
+  // doubled tile size does not cost a partial wave.  They lose (measured) on short-K /
+  // few-wave GEMMs where the pair's coupling and ramp-up outweigh the feed.  (The
+  // erf-GELU GEMMs at K = 1024 lost with eight epilogue warps and win with twelve:
+  // C5 ffn_in 397-407 -> 382-383 us, same box.)
   *pair = 0;
   if (*bn == 128 || *bn == 256) {
     const double units = (double)(num_sms / 2);
     const double waves = (double)((rows + 2 * GEMM_BM - 1) / (2 * GEMM_BM)) * (n / *bn) / units;
-    if ((k >= 2048 && waves >= 3.0) || (k >= 1024 && !gelu && waves >= 6.0)) *pair = 1;
+    if ((k >= 2048 && waves >= 3.0) || (k >= 1024 && waves >= 6.0)) *pair = 1;
   }
 }
 

@@ -415,25 +415,31 @@ def run_cp(args, rank: int, world: int, local_rank: int):
         torch.cuda.synchronize(dev)
         dist.barrier(device_ids=[local_rank])
         total_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev))
-        # e2e: every sequence's input in from pinned host memory, the rank's rows out.
-        hosts = [(xs.cpu().pin_memory(), None if ms is None else ms.cpu().pin_memory()) for xs, ms in seqs]
-        h2d = sum(h.numel() * h.element_size() + (0 if m is None else m.numel()) for h, m in hosts)
-        outs = []
+        # e2e: each rank copies its own rows of every sequence in from pinned host memory
+        # and its output rows out to pinned host memory (the valid lengths are known on
+        # the host, so the mask itself is not needed).
+        dev_x, host_x, host_out, spans = [], [], [], []
+        for (xs, _), n in zip(seqs, lens):
+            lo, hi = cp.shares(n)[cp.rank]
+            spans.append((lo, hi))
+            dev_x.append(torch.zeros_like(xs))
+            host_x.append(xs[0, lo:hi].cpu().pin_memory())
+            host_out.append(torch.empty((hi - lo, xs.shape[2]), dtype=xs.dtype).pin_memory())
+        h2d = sum(h.numel() * h.element_size() for h in host_x)
+        d2h = sum(h.numel() * h.element_size() for h in host_out)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         dist.barrier(device_ids=[local_rank])
         torch.cuda.synchronize(dev)
         t0.record(stream)
-        d2h = 0
         for _ in range(args.steps):
-            for (hx, hm), n in zip(hosts, lens):
-                xs = hx.to(dev, non_blocking=True)
-                ms = None if hm is None else hm.to(dev, non_blocking=True)
-                _, _, rows = cp(xs, ms, gather=False, length=n)
-                outs.append(rows.to("cpu", non_blocking=True))
+            for i, n in enumerate(lens):
+                lo, hi = spans[i]
+                dev_x[i][0, lo:hi].copy_(host_x[i], non_blocking=True)
+                _, _, rows = cp(dev_x[i], None, gather=False, length=n)
+                host_out[i].copy_(rows, non_blocking=True)
             flush.zero_()
         t1.record(stream)
         torch.cuda.synchronize(dev)
-        d2h = sum(o.numel() * o.element_size() for o in outs[-len(hosts):]) if hosts else 0
         e2e_ms = max_over_ranks(t0.elapsed_time(t1))
         nb = torch.tensor([h2d, d2h], dtype=torch.float64, device=dev)
         dist.all_reduce(nb)
@@ -457,7 +463,8 @@ def run_cp(args, rank: int, world: int, local_rank: int):
                    "inputs": f"x~N(0,1), input seed {args.seed + 1}"},
         "e2e": {"value": B * S * args.steps / (e2e_ms / 1e3), "unit": UNIT,
                 "h2d_bytes_per_step": int(nb[0].item()), "d2h_bytes_per_step": int(nb[1].item()),
-                "copies": "each rank copies its group's sequences in and its output rows out"},
+                "copies": "each rank copies its own rows of its group's sequences in and its "
+                          "output rows out (pinned buffers, bytes summed over ranks)"},
         "roofline": None, "cpu_baseline": None, "clocks": clk,
         "gpu_launches": launches * args.steps, "launches_per_step": launches,
     }

@@ -59,7 +59,7 @@ struct AtcSmem {
   static constexpr int NT = HD == 256 ? 1 : 2;   // query tiles per work item
   static constexpr bool P_ALIAS = HD >= 128;     // P written over its S buffer
   static constexpr int QBUF = HD >= 128 ? 1 : 2;  // Q buffers (items in flight)
-  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? 3 : HD == 128 ? 2 : 1;
+  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? 4 : HD == 128 ? 2 : 1;
   static constexpr int BOX_COLS = HD < 64 ? HD : 64;  // TMA box width (one swizzle atom)
   static constexpr int NBOX = HD / BOX_COLS;
   static constexpr int BOX_BYTES = ATC_BM * BOX_COLS * 2;

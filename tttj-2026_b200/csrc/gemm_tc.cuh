@@ -398,9 +398,22 @@ __global__ void __launch_bounds__(gemm_threads(EPIW), 1)
         const int r = (t / n_tiles) * TM + (int)rank * GEMM_BM + row_in_tile;
         if (r >= rows) return;
         const float2* st = st_src + (size_t)r * st_parts;
+        if ((st_parts & 1) == 0) {
+          // Two partials per 16-byte load (even counts: a row starts 16-byte aligned).
+          const float4* st4 = reinterpret_cast<const float4*>(st);
 #pragma unroll
-        for (int j = 0; j < MAXP; ++j)
-          if (j < st_parts) pst[j] = __ldg(st + j);
+          for (int j = 0; j < MAXP / 2; ++j) {
+            if (2 * j < st_parts) {
+              const float4 v = __ldg(st4 + j);
+              pst[2 * j] = make_float2(v.x, v.y);
+              pst[2 * j + 1] = make_float2(v.z, v.w);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < MAXP; ++j)
+            if (j < st_parts) pst[j] = __ldg(st + j);
+        }
         if (EPI == EPI_RESIDUAL_F32_STATS) ppiv = __ldg(p.pivot_prev + r);
       }
     };

@@ -132,6 +132,12 @@ int tttj_plan_destroy(tttj_plan* plan);
  * copies a non-zero device status word (a bounded device wait gave up) into the plan's
  * pinned host mirror, and the next tttj_forward of the plan that finds it set returns
  * TTTJ_ERR_DEVICE_TIMEOUT (launching nothing) and clears it.
+ * A forward enqueued while `stream` is capturing becomes part of the CUDA graph: it
+ * builds its token plan from valid_mask at every replay, does not wait for the plan's
+ * previous forward (the capturing caller orders the capture and its replays), and
+ * from then on no forward of the plan reuses a token plan left in the workspace.
+ * Per-kernel timing must be off while capturing; a replay's device errors are read
+ * with tttj_plan_status.
  * Replaces the pybind forward(input, valid_mask, packed_weights, capture_debug)
  * (kernels/csrc/sequence_resident.cpp:23-32), its per-launch error check
  * (C10_CUDA_KERNEL_LAUNCH_CHECK, kernels/csrc/sequence_resident.cu:531) and the Python

@@ -482,6 +482,7 @@ struct tttj_plan {
   // a forward without a mask skips the plan kernel.  The gather kernel, first of every
   // layer-by-layer forward, zeroes the attention work counters.
   bool plan_static = false;
+  bool captured = false;     // a forward of this plan was captured into a CUDA graph
   bool res_ok = false;       // the resident kernel fits this shape (launch built)
   bool res_auto = false;     // ... and TTTJ_PATH_AUTO prefers it
   int path = TTTJ_PATH_AUTO;
@@ -1124,6 +1125,8 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
   TTTJ_CUDA(cudaStreamIsCapturing(s, &capture));
   const bool capturing = capture != cudaStreamCaptureStatusNone;
+  if (capturing && p->timing)
+    return fail(TTTJ_ERR_INVALID, "forward: per-kernel timing cannot be on while the stream is capturing");
   if (!capturing && p->has_last && s != p->last_stream)
     TTTJ_CUDA(cudaStreamWaitEvent(s, p->done, 0));
   struct DoneRecord {  // record completion on every return path after launches began
@@ -1174,7 +1177,12 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
   // Without a mask the plan is the all-valid one every time: built by the first such
   // forward, reused by the next ones (the reference caches the all-valid case too,
   // kernels/sequence_resident.py:173-192).
-  if (!(valid_mask == nullptr && p->plan_static)) {
+  // A captured forward always builds its plan, so that the graph does not depend on
+  // what the forward before the capture left in the workspace; and once a plan has been
+  // captured, its replays may rewrite the workspace's token plan behind the library's
+  // back, so no later forward of it reuses one.
+  if (capturing) p->captured = true;
+  if (!(valid_mask == nullptr && p->plan_static) || p->captured) {
     TTTJ_TIMED(TTTJ_KCLASS_PLAN, plan_tokens_launch(valid_mask, B, S, c.num_heads, c.causal,
                                                     atc_item_rows(hp), ATC_BN, p->tp, s));
     // A split plan's attention: the whole sequence's keys, this rank's query blocks.
@@ -1184,7 +1192,7 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
                                     atc_item_rows(hp), ATC_BN, p->tp_attn, s, p->cp_lo,
                                     p->cp_lo + T));
   }
-  p->plan_static = valid_mask == nullptr;
+  p->plan_static = valid_mask == nullptr && !p->captured;
   const TokenPlan& tpa = p->cp ? p->tp_attn : p->tp;  // attention items and work counters
   TTTJ_TIMED(TTTJ_KCLASS_LAYERNORM,
              ln_gather_launch(x, x_dtype, p->tp.packed_src, rows_dev, T, D, p->resid, p->x16,

@@ -53,13 +53,20 @@
 
 namespace tttj {
 
+// Q buffers (work items in flight) at head_dim <= 64.  Three (with three K/V stages at
+// head_dim 64, for shared memory) measured C2 attention 26.4 -> 25.9 us but C5 156 ->
+// 166 us; two with four stages is the default.
+#ifndef ATC_QBUF_SMALL
+#define ATC_QBUF_SMALL 2
+#endif
 template <int HD>
 struct AtcSmem {
   static_assert(HD == 32 || HD == 64 || HD == 128 || HD == 256, "head_dim layout");
   static constexpr int NT = HD == 256 ? 1 : 2;   // query tiles per work item
   static constexpr bool P_ALIAS = HD >= 128;     // P written over its S buffer
-  static constexpr int QBUF = HD >= 128 ? 1 : 2;  // Q buffers (items in flight)
-  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? 4 : HD == 128 ? 2 : 1;
+  static constexpr int QBUF = HD >= 128 ? 1 : ATC_QBUF_SMALL;  // Q buffers (items in flight)
+  static constexpr int QS = QBUF < 2 ? 2 : QBUF;  // Q barrier / info slots
+  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? (ATC_QBUF_SMALL > 2 ? 3 : 4) : HD == 128 ? 2 : 1;
   static constexpr int BOX_COLS = HD < 64 ? HD : 64;  // TMA box width (one swizzle atom)
   static constexpr int NBOX = HD / BOX_COLS;
   static constexpr int BOX_BYTES = ATC_BM * BOX_COLS * 2;
@@ -67,8 +74,8 @@ struct AtcSmem {
   static constexpr int KV_TILE = ATC_BN * HD * 2;
   static constexpr int Q_BYTES = QBUF * NT * Q_TILE;
   static constexpr int KV_BYTES = STAGES * 2 * KV_TILE;
-  static constexpr int NBAR = 2 + 2 + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 2;
-  static constexpr int INFO_BYTES = 2 * 64;  // decoded item (AtcItem, 40 B) per Q buffer
+  static constexpr int NBAR = QS + QS + 2 * STAGES + 2 + 2 + 2 + 2 + 2 + 2 + 2;
+  static constexpr int INFO_BYTES = QS * 64;  // decoded item (AtcItem, 40 B) per Q buffer
   // Epilogue staging per softmax warp: its 32 output rows x HD fp16 (head_dim <= 64;
   // wider heads store straight from registers).
   static constexpr bool STAGED_EPI = HD <= 64;
@@ -155,9 +162,9 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
   const uint32_t sQ = smem_u32(smem);
   const uint32_t sKV = sQ + SM::Q_BYTES;
   const uint32_t bar0 = sKV + SM::KV_BYTES;
-  const uint32_t bar_q_full = bar0;                     // [2]
-  const uint32_t bar_q_empty = bar0 + 16;               // [2]
-  const uint32_t bar_kv_full = bar0 + 32;               // [STAGES]
+  const uint32_t bar_q_full = bar0;                     // [QS]
+  const uint32_t bar_q_empty = bar0 + 8 * SM::QS;       // [QS]
+  const uint32_t bar_kv_full = bar0 + 16 * SM::QS;      // [STAGES]
   const uint32_t bar_kv_empty = bar_kv_full + 8 * STAGES;  // [STAGES]
   const uint32_t bar_s_full = bar_kv_empty + 8 * STAGES;   // [2]
   const uint32_t bar_p_full = bar_s_full + 16;             // [2]
@@ -180,11 +187,13 @@ __global__ void __launch_bounds__(ATC_THREADS, 1)
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQKV);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < SM::QS; ++i) {
       mbar_init(bar_q_full + 8 * i, 1);
       // Released by the MMA warp's commit after the item's last Q K^T and by every
       // softmax thread once it copied the item's decoded info out of the slot.
       mbar_init(bar_q_empty + 8 * i, NT + NT * ATC_BM);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(bar_s_full + 8 * i, 1);
       mbar_init(bar_p_full + 8 * i, ATC_BM);
       mbar_init(bar_o_full + 8 * i, 1);

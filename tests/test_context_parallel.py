@@ -240,3 +240,69 @@ def test_context_parallel_two_gpus_matches_single_gpu_and_oracle():
             # The ranks' GEMM tiles differ from the single GPU's (fewer rows), which
             # regroups the LayerNorm statistics: agreement to about two fp16 ulps.
             assert diff_single < 2e-2, (rank, causal, length, diff_single)
+
+
+def test_graph_mode_ranks_with_and_without_rows_run_the_same_collectives(monkeypatch):
+    """With graphs, a rank that holds rows runs an eager forward, captures one and
+    replays it on the first call for a length (a replay afterwards); a rank without rows
+    must run the same exchanges in the same order, or NCCL's collectives pair up wrongly
+    and the group hangs until its timeout.  Checked on the host with a fake graph that
+    records the exchanges called while capturing and runs them at replay."""
+    import types
+    from contextlib import contextmanager
+    from tttj_2026_b200 import context_parallel as cpm
+
+    L = 3
+    state = {"capture": None}
+
+    class FakeGraph:
+        def __init__(self):
+            self.recorded = []
+
+        def replay(self):
+            for f in self.recorded:
+                f()
+
+    @contextmanager
+    def fake_graph(g):
+        state["capture"] = g
+        try:
+            yield
+        finally:
+            state["capture"] = None
+
+    monkeypatch.setattr(torch.cuda, "CUDAGraph", FakeGraph)
+    monkeypatch.setattr(torch.cuda, "graph", fake_graph)
+
+    def make(rank, log):
+        def exchange(*_a, **_k):
+            if state["capture"] is not None:
+                state["capture"].recorded.append(lambda: log.append("allgather"))
+            else:
+                log.append("allgather")
+
+        monkeypatch.setattr(cpm, "allgather_shares", exchange)
+        m = cpm.ContextParallelTransformer.__new__(cpm.ContextParallelTransformer)
+        torch.nn.Module.__init__(m)
+        m.config = types.SimpleNamespace(num_layers=L, d_model=64, num_heads=2, ffn_dim=128,
+                                         causal=True)
+        m.device, m.group, m.rank, m.world = torch.device("cpu"), None, rank, 2
+        m.graphs, m._graphs, m._plans, m._exchange_error = True, {}, {}, None
+        m._plan = lambda *a: types.SimpleNamespace()
+        m._run = lambda plan, xl, out, slot: [exchange() for _ in range(L)]
+        return m
+
+    def calls(rank, length):
+        log = []
+        m = make(rank, log)
+        x = torch.zeros(1, 600, 64)
+        for _ in range(2):
+            m(x, None, gather=False, length=length)
+            log.append("|")
+        return log
+
+    # 300 tokens: one 256-row item each (rank 1 rows 256..299); 200 tokens: rank 1 has none.
+    assert calls(0, 300) == calls(1, 300)
+    assert calls(0, 200) == calls(1, 200)
+    log = calls(0, 200)
+    assert log.count("allgather") == 3 * L  # eager + replay on the first call, replay after

@@ -82,7 +82,8 @@ def test_c2_per_rank_shapes_vs_oracle(batch):
 
 def test_organizer_slot_pattern():
     """The organizer harness's slot (UserOptimizedTransformer.forward building the B200
-    module from itself, as INTEGRATION.md shows; the reference's class itself is
+    module from itself on its first call and keeping it outside the module's
+    submodules; the reference's class itself is
     exercised on the CPU by tests/test_reference_classes.py): the output matches the
     oracle, a second call reuses the module, and the model's state_dict still works."""
     cfg = tb.TransformerConfig(4, 200, 256, 4, 512, 2, True)

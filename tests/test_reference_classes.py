@@ -9,8 +9,9 @@ machine, so these tests run on the CPU and are skipped elsewhere).  They check t
 * make_optimized_transformer reads a reference BaselineTransformer exactly as it reads
   this package's TransformerParameters (same module tree, byte-identical packed weights),
 * the reference's copy_model_weights moves weights between the two (strict state dict),
-* the organizer's UserOptimizedTransformer slot, with the body INTEGRATION.md gives,
-  reaches the constructor (on a CPU model it raises the constructor's ValueError; on a
+* the organizer's UserOptimizedTransformer slot, whose forward builds the B200 module
+  from itself on first use (kept in the instance dict, outside the submodules), reaches
+  the constructor (on a CPU model it raises the constructor's ValueError; on a
   CUDA device the same slot runs the B200 forward), and
 * the reference's own regression gate, compare_outputs (rtol 0.01 / atol 0.001,
   benchmarks/torch_transformer_benchmark.py:289-330), accepts the fp32 oracle against the

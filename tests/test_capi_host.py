@@ -152,7 +152,7 @@ STATS, FOLD, FOLD_GELU, RES_F32 = 4, 5, 6, 3
 @pytest.mark.parametrize(
     "what,rows,n,k,epi,expect",
     [
-        # C2 on one B200 (the launch list in profiles/launches_c2_forward.md)
+        # C2 on one B200
         ("C2 qkv", 8192, 1536, 512, FOLD, (256, 0)),
         ("C2 out_proj", 8192, 512, 512, STATS, (128, 0)),
         ("C2 ffn_in", 8192, 2048, 512, FOLD_GELU, (256, 0)),

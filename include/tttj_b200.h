@@ -166,7 +166,9 @@ int tttj_forward(tttj_plan* plan, const void* x, int x_dtype, const uint8_t* val
  * workspace.  tttj_forward_cp calls exchange(user, layer, stream) once per layer,
  * after the rank's q|k|v rows are enqueued on `stream`; the callback enqueues the
  * all-gather on the same stream (returning non-zero aborts the forward).  x and out are
- * the rank's own rows [seq_len, d_model]. */
+ * the rank's own rows [seq_len, d_model].  Under stream capture (as tttj_forward) the
+ * callback runs once, while capturing, and its enqueued all-gathers become part of the
+ * graph; every rank of the group must capture and replay the same forwards. */
 typedef int (*tttj_exchange_fn)(void* user, int layer, void* stream);
 size_t tttj_workspace_bytes_cp(const tttj_config* cfg, int full_rows);
 int tttj_plan_create_cp(const tttj_config* cfg, int device, const void* weights, const void* folded,

@@ -53,20 +53,20 @@
 
 namespace tttj {
 
-// Q buffers (work items in flight) at head_dim <= 64.  Three (with three K/V stages at
-// head_dim 64, for shared memory) measured C2 attention 26.4 -> 25.9 us but C5 156 ->
-// 166 us; two with four stages is the default.
-#ifndef ATC_QBUF_SMALL
-#define ATC_QBUF_SMALL 2
-#endif
-template <int HD>
+// QB: Q buffers (work items in flight) at head_dim <= 64.  Two, with four K/V stages
+// at head_dim 64, suit sequences of at most 256 tokens (items of one or two key tiles:
+// the deeper ring keeps the next items' tiles coming); three, with three K/V stages (the
+// shared memory holds no more), suit sequences of up to 2048 (measured: C5 attention 156
+// vs 166 us, C2 26.7 vs 26.2 us; C4's 8192-token sequences no better).  The launcher
+// picks by the longest sequence the plan allows.
+template <int HD, int QB = 2>
 struct AtcSmem {
   static_assert(HD == 32 || HD == 64 || HD == 128 || HD == 256, "head_dim layout");
   static constexpr int NT = HD == 256 ? 1 : 2;   // query tiles per work item
   static constexpr bool P_ALIAS = HD >= 128;     // P written over its S buffer
-  static constexpr int QBUF = HD >= 128 ? 1 : ATC_QBUF_SMALL;  // Q buffers (items in flight)
+  static constexpr int QBUF = HD >= 128 ? 1 : QB;  // Q buffers (items in flight)
   static constexpr int QS = QBUF < 2 ? 2 : QBUF;  // Q barrier / info slots
-  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? (ATC_QBUF_SMALL > 2 ? 3 : 4) : HD == 128 ? 2 : 1;
+  static constexpr int STAGES = HD == 32 ? 4 : HD == 64 ? (QB > 2 ? 3 : 4) : HD == 128 ? 2 : 1;
   static constexpr int BOX_COLS = HD < 64 ? HD : 64;  // TMA box width (one swizzle atom)
   static constexpr int NBOX = HD / BOX_COLS;
   static constexpr int BOX_BYTES = ATC_BM * BOX_COLS * 2;
@@ -148,10 +148,10 @@ __device__ __forceinline__ uint64_t atc_desc_v(uint32_t addr) {
 #define ATC_P_EARLY 2
 #endif
 
-template <int HD, bool CAUSAL>
+template <int HD, bool CAUSAL, int QB>
 __global__ void __launch_bounds__(ATC_THREADS, 1)
     attention_tc_kernel(const __grid_constant__ CUtensorMap tmQKV, const AtcParams p) {
-  using SM = AtcSmem<HD>;
+  using SM = AtcSmem<HD, QB>;
   constexpr int STAGES = SM::STAGES;
   constexpr int NT = SM::NT;
   constexpr int QBUF = SM::QBUF;

@@ -1231,7 +1231,8 @@ static int forward_impl(tttj_plan* p, const void* x, int x_dtype, const uint8_t*
     AtcParams ap = p->attn;
     ap.work_counter = tpa.counters + l;
     TTTJ_TIMED(TTTJ_KCLASS_ATTENTION,
-               attention_tc_launch(p->attn_tm, ap, hp, c.causal, p->attn_grid, s));
+               attention_tc_launch(p->attn_tm, ap, hp, c.causal, p->attn_grid,
+                                   p->cp ? p->cp_len : S, s));
     if (cap) TTTJ_CUDA(debug_gather_launch(p->ctx, 1, Qw, 0, D, hd, hp, dmap, bq, S, d_pv, s));
     TTTJ_TIMED(TTTJ_KCLASS_GEMM_OUT, gemm_launch(L.out, s));
     if (cap) {  // attention branch = x after the residual add - x before
@@ -1333,7 +1334,7 @@ int tttj_attention(const void* qkv, void* ctx, int qkv_rows, const uint8_t* vali
   if (rc) return rc;
   TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, atc_item_rows(hd),
                                ATC_BN, tp, s));
-  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
+  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, seq_len, s));
   return TTTJ_OK;
 }
 
@@ -1481,6 +1482,6 @@ extern "C" int tttj_attention_noalloc(const void* qkv, void* ctx, int qkv_rows,
   if (rc) return rc;
   TTTJ_CUDA(plan_tokens_launch(valid_mask, batch, seq_len, num_heads, causal, atc_item_rows(hd),
                                ATC_BN, tp, s));
-  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, s));
+  TTTJ_CUDA(attention_tc_launch(tm, ap, hd, causal, grid, seq_len, s));
   return TTTJ_OK;
 }

@@ -74,9 +74,10 @@ cudaError_t gemm_launch(const GemmLaunch& g, cudaStream_t stream);
 
 // tcgen05 attention for a head-dim layout of 32, 64, 128 or 256 (plan with q_block
 // atc_item_rows(head_dim), kv_block ATC_BN).  tmQKV: fp16 [rows, 3 * qkv_width] map, box
-// {min(head_dim, 64), 128}, swizzle 64 B (head_dim 32) / 128 B.
+// {min(head_dim, 64), 128}, swizzle 64 B (head_dim 32) / 128 B.  max_seq_len: the
+// longest sequence the launch may see (it picks the kernel's item buffering).
 cudaError_t attention_tc_launch(const CUtensorMap& tmQKV, const AtcParams& p, int head_dim,
-                                int causal, int grid, cudaStream_t stream);
+                                int causal, int grid, int max_seq_len, cudaStream_t stream);
 
 // K3 resident stack (resident.cuh): weights as 3-D TMA maps over the layers
 // ({columns, rows, layer}, one box per MMA unit).
